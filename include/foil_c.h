@@ -1,0 +1,273 @@
+/*
+ * foil_c.h — C-ABI of the B200 tt-foil runtime (libfoil.so).
+ *
+ * Two layers, both plain C (no C++ or torch types in any signature):
+ *
+ *  1. The runtime boundary.  One C function per entry point of tt-foil's
+ *     public C++ API (include/tt_foil/runtime.hpp and src/cb_config.hpp in
+ *     the reference).  The C++ header include/tt_foil/runtime.hpp in this
+ *     repository is a thin wrapper over these functions, so a program written
+ *     against tt-foil links against libtt_foil.so + libfoil.so unchanged.
+ *     A "kernel" is a bundle of program-descriptor files (the reference's
+ *     per-RISC ELF names); executing it launches the sm_100a CUDA kernel that
+ *     implements that program, with the reference's runtime-argument layout.
+ *
+ *  2. Device-resident kernel entry points (foil_*_dev).  The same CUDA
+ *     kernels, called on CUDA device pointers and a caller-supplied CUDA
+ *     stream.  They replace the reference's per-example Tensix compute /
+ *     reader / writer kernels (examples/<name>/kernels/<role>.cpp) and the host
+ *     tile helpers (tests/tile_utils.hpp) when the data already lives in HBM.
+ *
+ * Error behaviour: every function returns 0 (FOIL_OK) on success or a
+ * foil_status code; foil_last_error() returns the message of the most recent
+ * failure on the calling thread.  The C++ wrapper turns any non-zero status
+ * into std::runtime_error(message), which is the reference's error behaviour
+ * (all failures throw std::runtime_error, src/runtime_impl.cpp:53-55 etc.).
+ *
+ * Data format: bf16 values are uint16_t bit patterns.  "Tile layout" is the
+ * reference wire format (tests/tile_utils.hpp:4-12): 32x32 tiles of four
+ * 16x16 faces, faces in order (rows 0-15, cols 0-15), (rows 0-15, cols 16-31),
+ * (rows 16-31, cols 0-15), (rows 16-31, cols 16-31), row-major inside a face;
+ * a matrix of Rt x Ct tiles is stored tile-row-major (tile (i,j) at i*Ct+j).
+ */
+#ifndef FOIL_C_H
+#define FOIL_C_H
+
+#include <stddef.h>
+#include <stdint.h>
+
+#if defined(__GNUC__)
+#define FOIL_API __attribute__((visibility("default")))
+#else
+#define FOIL_API
+#endif
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+/* ------------------------------------------------------------------------ */
+/* Status codes                                                              */
+/* ------------------------------------------------------------------------ */
+typedef enum foil_status {
+    FOIL_OK = 0,
+    FOIL_ERR_INVALID = 1,     /* bad argument or state                     */
+    FOIL_ERR_OOM = 2,         /* L1 / DRAM arena exhausted                 */
+    FOIL_ERR_NOT_FOUND = 3,   /* a program-descriptor file does not exist  */
+    FOIL_ERR_CUDA = 4,        /* CUDA runtime / driver call failed         */
+    FOIL_ERR_TIMEOUT = 5,     /* execute deadline passed                   */
+    FOIL_ERR_UNSUPPORTED = 6, /* program outside the accelerated path      */
+    FOIL_ERR_DEVICE = 7       /* a kernel reported a device-side error     */
+} foil_status;
+
+/* Message for the last non-zero status returned on this thread ("" if none). */
+FOIL_API const char* foil_last_error(void);
+
+/* Library build identification string (arch, version). */
+FOIL_API const char* foil_version(void);
+
+/* ------------------------------------------------------------------------ */
+/* Runtime boundary types                                                    */
+/* ------------------------------------------------------------------------ */
+typedef struct foil_device foil_device; /* opaque; one per open device      */
+typedef struct foil_kernel foil_kernel; /* opaque; one per load_kernel       */
+
+/* Logical core coordinate.  Replaces tt::foil::CoreCoord
+ * (include/tt_foil/runtime.hpp:27-31). */
+typedef struct foil_core {
+    uint32_t x;
+    uint32_t y;
+} foil_core;
+
+/* Buffer locations.  Replaces tt::foil::BufferLocation (runtime.hpp:37-40). */
+enum { FOIL_LOC_L1 = 0, FOIL_LOC_DRAM = 1 };
+
+/* Buffer descriptor.  Replaces tt::foil::Buffer (runtime.hpp:44-49):
+ * device_addr is the address a kernel receives as a runtime argument — a
+ * 32-bit offset inside the owning core's emulated L1 arena, or an offset
+ * inside the device's DRAM arena. */
+typedef struct foil_buffer {
+    int32_t location;      /* FOIL_LOC_L1 or FOIL_LOC_DRAM */
+    uint32_t reserved;
+    uint64_t device_addr;
+    uint64_t size_bytes;
+    foil_core core;        /* owning core for L1 buffers */
+} foil_buffer;
+
+/* RISC identifiers.  Replaces RiscBinary::RiscId (runtime.hpp:100-106). */
+enum {
+    FOIL_RISC_BRISC = 0,
+    FOIL_RISC_NCRISC = 1,
+    FOIL_RISC_TRISC0 = 2,
+    FOIL_RISC_TRISC1 = 3,
+    FOIL_RISC_TRISC2 = 4
+};
+
+/* One program binary.  Replaces tt::foil::RiscBinary (runtime.hpp:99-109). */
+typedef struct foil_risc_binary {
+    int32_t risc;
+    const char* elf_path;  /* path of a program-descriptor file */
+} foil_risc_binary;
+
+/* Circular-buffer description.  Replaces tt::foil::CbConfig
+ * (src/cb_config.hpp:42-50). */
+typedef struct foil_cb_config {
+    uint8_t cb_index;
+    uint64_t fifo_addr;
+    uint32_t fifo_size;
+    uint32_t num_pages;
+    uint32_t page_size;
+} foil_cb_config;
+
+/* ------------------------------------------------------------------------ */
+/* Runtime boundary entry points                                             */
+/* ------------------------------------------------------------------------ */
+
+/* Open CUDA device `pcie_device_index` and create one emulated L1 arena per
+ * requested core.  firmware_dir is accepted and ignored (there is no
+ * firmware).  Replaces tt::foil::open_device (runtime.hpp:64-67;
+ * src/device.cpp:116-245).  Errors: no cores, bad index, CUDA failure. */
+FOIL_API int foil_open_device(int pcie_device_index, const char* firmware_dir,
+                     const foil_core* cores, size_t num_cores,
+                     foil_device** out_device);
+
+/* Release every arena and the CUDA resources of the device.  Replaces
+ * tt::foil::close_device (runtime.hpp:72; src/device.cpp:247-254). */
+FOIL_API int foil_close_device(foil_device* device);
+
+/* Bump-allocate `size_bytes` in a core's L1 arena (16-byte alignment) or in
+ * the DRAM arena (32-byte alignment).  Replaces tt::foil::allocate_buffer
+ * (runtime.hpp:81-85; src/buffer.cpp:11-35).  Errors: size 0, unknown core,
+ * arena exhausted. */
+FOIL_API int foil_allocate_buffer(foil_device* device, int32_t location,
+                         uint64_t size_bytes, foil_core core,
+                         foil_buffer* out_buffer);
+
+/* Bump allocator: releasing a buffer reclaims nothing.  Replaces
+ * tt::foil::free_buffer (runtime.hpp:88; src/buffer.cpp:37-41). */
+FOIL_API int foil_free_buffer(foil_device* device, const foil_buffer* buffer);
+
+/* Blocking host->device / device->host copies (pageable or pinned host
+ * memory).  Replace tt::foil::write_buffer / read_buffer (runtime.hpp:91,94;
+ * src/runtime_impl.cpp:52-78).  Errors: bytes > size_bytes. */
+FOIL_API int foil_write_buffer(foil_device* device, const foil_buffer* buffer,
+                      const void* src, uint64_t bytes);
+FOIL_API int foil_read_buffer(foil_device* device, const foil_buffer* buffer,
+                     void* dst, uint64_t bytes);
+
+/* Read the program-descriptor files named by `binaries` and bind the kernel
+ * to `core`.  Replaces tt::foil::load_kernel (runtime.hpp:114-117;
+ * src/kernel.cpp:16-62).  Errors: empty list, missing file, core not opened,
+ * descriptors of different programs, program outside the path. */
+FOIL_API int foil_load_kernel(foil_device* device, const foil_risc_binary* binaries,
+                     size_t num_binaries, foil_core core,
+                     foil_kernel** out_kernel);
+
+/* Free a kernel handle (the C++ wrapper's shared_ptr deleter). */
+FOIL_API int foil_release_kernel(foil_kernel* kernel);
+
+/* Store up to 64 runtime-argument words for one RISC of the kernel.
+ * Replaces tt::foil::set_runtime_args (runtime.hpp:120-124;
+ * src/kernel.cpp:66-83).  Errors: >64 words, RISC not in the kernel. */
+FOIL_API int foil_set_runtime_args(foil_device* device, foil_kernel* kernel,
+                          int32_t risc, const uint32_t* args,
+                          size_t num_args);
+
+/* Validate and record circular-buffer descriptors (indices < 32, no
+ * duplicates, rings inside the core's L1 arena).  The CUDA kernels stage
+ * tiles in shared memory, so the rings only need to be valid.  Replaces
+ * tt::foil::register_cbs (src/cb_config.hpp:68-71; src/cb_config.cpp:27-112).
+ */
+FOIL_API int foil_register_cbs(foil_device* device, foil_kernel* kernel,
+                      const foil_cb_config* cbs, size_t num_cbs);
+
+/* Launch every kernel, then wait until all have finished or `timeout_ms`
+ * (shared budget, <=0 means 5000 ms) has passed.  Kernels of one call that
+ * run the same program are fused into one grouped CUDA launch.  Replaces
+ * tt::foil::execute (runtime.hpp:132,137; src/dispatch.cpp:218-274).
+ * Errors: empty list, bad runtime args, timeout, device-side error. */
+FOIL_API int foil_execute(foil_device* device, foil_kernel* const* kernels,
+                 size_t num_kernels, int32_t timeout_ms);
+
+/* Pack a 64-bit address of `local_l1_addr` in core `dst`'s L1 arena.
+ * Replaces tt::foil::make_noc_unicast_addr (runtime.hpp:151-154;
+ * src/noc_addr.cpp:10-22): bits [47:42] = y, [41:36] = x, [35:0] = offset. */
+FOIL_API int foil_make_noc_unicast_addr(foil_device* device, foil_core dst,
+                               uint64_t local_l1_addr, uint64_t* out_addr);
+
+/* Pack a 64-bit address of `dram_offset` in the DRAM arena.  Replaces
+ * tt::foil::make_noc_dram_addr (runtime.hpp:160; runtime_impl.cpp:124-131). */
+FOIL_API int foil_make_noc_dram_addr(foil_device* device, uint64_t dram_offset,
+                            uint64_t* out_addr);
+
+/* CUDA device pointer behind a buffer (for device-resident callers). */
+FOIL_API int foil_buffer_device_ptr(foil_device* device, const foil_buffer* buffer,
+                           void** out_ptr);
+
+/* Number of CUDA kernel launches issued by this process so far (all
+ * entry points). */
+FOIL_API uint64_t foil_launch_count(void);
+
+/* ------------------------------------------------------------------------ */
+/* Device-resident kernel entry points.  All pointers are CUDA device        */
+/* pointers of the current device; `stream` is a cudaStream_t (NULL = the    */
+/* legacy default stream).  Launches are asynchronous.                       */
+/* ------------------------------------------------------------------------ */
+
+/* Row-major (rows x cols) bf16 -> tile layout; rows, cols multiples of 32.
+ * Replaces row_major_to_tile + tile_matrix (tests/tile_utils.hpp:51-65;
+ * tests/test_conv_3x3.cpp:144-158). */
+FOIL_API int foil_tilize_dev(const uint16_t* row_major, uint16_t* tiles,
+                    uint32_t rows, uint32_t cols, void* stream);
+
+/* Tile layout -> row-major.  Replaces tile_to_row_major + untile_matrix
+ * (tests/tile_utils.hpp:68-80; tests/test_conv_3x3.cpp:160-174). */
+FOIL_API int foil_untilize_dev(const uint16_t* tiles, uint16_t* row_major,
+                      uint32_t rows, uint32_t cols, void* stream);
+
+/* Identity copy of `bytes` (multiple of 16, 16-byte aligned pointers).
+ * Replaces examples/tile_copy/kernels/{reader,compute,writer}.cpp. */
+FOIL_API int foil_tile_copy_dev(const void* src, void* dst, uint64_t bytes,
+                       void* stream);
+
+/* out = bf16(f32(a) + f32(b)) element-wise on n bf16 values (n multiple of
+ * 8).  Replaces examples/add_tiles/kernels/compute.cpp:19-43. */
+FOIL_API int foil_add_tiles_dev(const uint16_t* a, const uint16_t* b, uint16_t* out,
+                       uint64_t n, void* stream);
+
+/* out = max(x, 0) element-wise (bit-exact), n multiple of 8.  Replaces
+ * examples/relu/kernels/compute.cpp:19-45. */
+FOIL_API int foil_relu_tiles_dev(const uint16_t* in, uint16_t* out, uint64_t n,
+                        void* stream);
+
+/* Row-broadcast bias on a tile-layout matrix of rows x cols:
+ * out[r][c] = bf16(f32(in[r][c]) + f32(bias[0][c])), where `bias_tiles` is a
+ * tile-layout band of 1 x (cols/32) tiles whose row 0 holds the bias (the
+ * reference's bias-tile convention, tests/test_bias_add.cpp:53-56).
+ * Replaces examples/bias_add/kernels/compute.cpp:19-42. */
+FOIL_API int foil_bias_add_tiles_dev(const uint16_t* in, const uint16_t* bias_tiles,
+                            uint16_t* out, uint32_t rows, uint32_t cols,
+                            void* stream);
+
+/* Tiled bf16 GEMM on tcgen05 tensor cores: C (Mt x Nt tiles) = A (Mt x Kt
+ * tiles) . B (Kt x Nt tiles), fp32 accumulation, bf16 output, all in tile
+ * layout.  Optional fused epilogue: if `bias` is non-NULL (N = 32*Nt bf16
+ * values, one per output column) out = bf16(f32(bf16(acc)) + bias[n]); if
+ * `relu` is non-zero the result is clamped at 0.  Replaces the matmul
+ * compute kernel (examples/matmul_mnk/kernels/compute.cpp:23-53) and its
+ * reader / writer (examples/matmul_mnk/kernels/reader.cpp:28-57,
+ * writer.cpp:16-34), followed by bias_add and relu. */
+FOIL_API int foil_matmul_tiles_dev(const uint16_t* a, const uint16_t* b, uint16_t* c,
+                          uint32_t Mt, uint32_t Kt, uint32_t Nt,
+                          const uint16_t* bias, int32_t relu, void* stream);
+
+/* Read and clear the device-side error word of the current device: 0 if no
+ * kernel reported an error (bounded waits that gave up) since the last call.
+ * Synchronizes `stream`. */
+FOIL_API int foil_device_error_dev(void* stream, uint32_t* out_error);
+
+#ifdef __cplusplus
+}  /* extern "C" */
+#endif
+
+#endif  /* FOIL_C_H */

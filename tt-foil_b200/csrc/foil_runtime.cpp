@@ -1,0 +1,683 @@
+// C-ABI of the B200 tt-foil runtime (include/foil_c.h) bound to CUDA.
+//
+// The reference re-backed here: device open/close and bump allocators
+// (src/device.cpp, src/buffer.cpp), blocking host transfers
+// (src/runtime_impl.cpp:52-78), kernel load and runtime args
+// (src/kernel.cpp), CB registration (src/cb_config.cpp) and dispatch
+// (src/dispatch.cpp).  Where the reference cold-boots Tensix cores and writes
+// ELFs into L1, this file creates HBM arenas and launches CUDA kernels:
+//
+//  * DRAM arena: a 64 GiB virtual range (cuMemAddressReserve) backed on
+//    demand by physical chunks (cuMemCreate / cuMemMap) as the bump pointer
+//    grows, so a DRAM offset maps to base + offset with no table.
+//  * L1 arenas: one 1.5 MiB device allocation per opened core.
+//  * execute: runtime args -> launch plan (host_logic.cpp) -> range-checked
+//    device pointers -> CUDA launches on the device's stream -> bounded wait
+//    (cudaEventQuery against the caller's deadline) -> device error word.
+#include <cuda.h>
+#include <cuda_runtime.h>
+#include <cudaTypedefs.h>
+
+#include <atomic>
+#include <chrono>
+#include <cstring>
+#include <fstream>
+#include <memory>
+#include <mutex>
+#include <sstream>
+#include <string>
+#include <thread>
+#include <vector>
+
+#include "../../include/foil_c.h"
+#include "host_logic.hpp"
+#include "kernels/gemm_tc.cuh"
+
+namespace {
+
+thread_local std::string g_last_error;
+std::atomic<uint64_t> g_launches{0};
+
+}  // namespace
+
+extern "C" void foil_set_error(int /*status*/, const char* msg) { g_last_error = msg ? msg : ""; }
+void foil_count_launch() { g_launches.fetch_add(1, std::memory_order_relaxed); }
+
+extern "C" const char* foil_last_error(void) { return g_last_error.c_str(); }
+extern "C" uint64_t foil_launch_count(void) { return g_launches.load(); }
+extern "C" const char* foil_version(void) { return "tt-foil-b200 1.0 (sm_100a, tcgen05)"; }
+
+namespace {
+
+using foil::FoilError;
+
+void cuda_check(cudaError_t e, const char* what) {
+    if (e != cudaSuccess)
+        throw FoilError(FOIL_ERR_CUDA, std::string("tt-foil: ") + what + ": " + cudaGetErrorString(e));
+}
+
+// ------------------------------------------------ driver VMM entry points ---
+struct Vmm {
+    PFN_cuMemAddressReserve reserve = nullptr;
+    PFN_cuMemAddressFree addr_free = nullptr;
+    PFN_cuMemCreate create = nullptr;
+    PFN_cuMemRelease release = nullptr;
+    PFN_cuMemMap map = nullptr;
+    PFN_cuMemUnmap unmap = nullptr;
+    PFN_cuMemSetAccess set_access = nullptr;
+    PFN_cuMemGetAllocationGranularity granularity = nullptr;
+};
+
+const Vmm& vmm() {
+    static Vmm v;
+    static std::once_flag once;
+    std::call_once(once, [] {
+        auto get = [](const char* name, void** fn) {
+            cudaDriverEntryPointQueryResult q;
+            if (cudaGetDriverEntryPoint(name, fn, cudaEnableDefault, &q) != cudaSuccess ||
+                q != cudaDriverEntryPointSuccess)
+                *fn = nullptr;
+        };
+        get("cuMemAddressReserve", (void**)&v.reserve);
+        get("cuMemAddressFree", (void**)&v.addr_free);
+        get("cuMemCreate", (void**)&v.create);
+        get("cuMemRelease", (void**)&v.release);
+        get("cuMemMap", (void**)&v.map);
+        get("cuMemUnmap", (void**)&v.unmap);
+        get("cuMemSetAccess", (void**)&v.set_access);
+        get("cuMemGetAllocationGranularity", (void**)&v.granularity);
+    });
+    return v;
+}
+
+constexpr uint64_t kDramReserve = 64ull << 30;  // virtual range (= 36-bit limit)
+constexpr uint64_t kDramChunkMin = 64ull << 20;  // physical growth step
+
+// ----------------------------------------- per-device scratch error word ---
+std::mutex g_err_mu;
+uint32_t* g_err_words[64] = {};
+
+uint32_t* error_word_for_current_device() {
+    int dev = 0;
+    cuda_check(cudaGetDevice(&dev), "cudaGetDevice");
+    if (dev < 0 || dev >= 64) throw FoilError(FOIL_ERR_INVALID, "tt-foil: device ordinal out of range");
+    std::lock_guard<std::mutex> lk(g_err_mu);
+    if (!g_err_words[dev]) {
+        void* p = nullptr;
+        cuda_check(cudaMalloc(&p, 256), "cudaMalloc(error word)");
+        cuda_check(cudaMemset(p, 0, 256), "cudaMemset(error word)");
+        g_err_words[dev] = static_cast<uint32_t*>(p);
+    }
+    return g_err_words[dev];
+}
+
+int sm_count_current() {
+    int dev = 0, n = 0;
+    cudaGetDevice(&dev);
+    cudaDeviceGetAttribute(&n, cudaDevAttrMultiProcessorCount, dev);
+    return n > 0 ? n : 148;
+}
+
+template <class F>
+int guarded(F&& f) {
+    try {
+        f();
+        return FOIL_OK;
+    } catch (const FoilError& e) {
+        g_last_error = e.what();
+        return e.status;
+    } catch (const std::bad_alloc&) {
+        g_last_error = "tt-foil: host out of memory";
+        return FOIL_ERR_OOM;
+    } catch (const std::exception& e) {
+        g_last_error = e.what();
+        return FOIL_ERR_INVALID;
+    }
+}
+
+void throw_status(int st) {
+    if (st != FOIL_OK) throw FoilError(st, g_last_error);
+}
+
+}  // namespace
+
+// ====================================================================== ====
+struct foil_device {
+    int ordinal = 0;
+    cudaStream_t stream = nullptr;
+    cudaEvent_t done = nullptr;
+    std::mutex mu;
+    bool closed = false;
+    // DRAM arena
+    CUdeviceptr dram_base = 0;
+    uint64_t dram_mapped = 0;
+    size_t granularity = 2u << 20;
+    std::vector<std::pair<CUmemGenericAllocationHandle, uint64_t>> chunks;
+    foil::BumpAllocator dram_alloc;
+    // L1 arenas
+    struct CoreArena {
+        uint32_t x, y;
+        char* base;
+        foil::BumpAllocator alloc;
+    };
+    std::vector<CoreArena> cores;
+    uint32_t* err_word = nullptr;
+
+    CoreArena* core(uint32_t x, uint32_t y) {
+        for (auto& c : cores)
+            if (c.x == x && c.y == y) return &c;
+        return nullptr;
+    }
+};
+
+struct foil_kernel {
+    foil_device* dev = nullptr;
+    uint32_t core_x = 0, core_y = 0;
+    foil::Program prog = foil::Program::TileCopy;
+    std::array<bool, 5> present{};
+    std::array<std::vector<uint32_t>, 5> rta;
+    std::array<bool, 5> has_rta{};
+    std::vector<foil::CbDesc> cbs;
+    uint64_t cb_mask = 0;
+};
+
+namespace {
+
+void set_device(foil_device* d) { cuda_check(cudaSetDevice(d->ordinal), "cudaSetDevice"); }
+
+void release_device(foil_device* d) {
+    if (d->closed) return;
+    d->closed = true;
+    cudaSetDevice(d->ordinal);
+    if (d->stream) cudaStreamSynchronize(d->stream);
+    const Vmm& v = vmm();
+    if (d->dram_base) {
+        uint64_t off = 0;
+        for (auto& ch : d->chunks) {
+            if (v.unmap) v.unmap(d->dram_base + off, ch.second);
+            if (v.release) v.release(ch.first);
+            off += ch.second;
+        }
+        d->chunks.clear();
+        if (v.addr_free) v.addr_free(d->dram_base, kDramReserve);
+        d->dram_base = 0;
+    }
+    for (auto& c : d->cores)
+        if (c.base) cudaFree(c.base);
+    d->cores.clear();
+    if (d->err_word) cudaFree(d->err_word);
+    d->err_word = nullptr;
+    if (d->done) cudaEventDestroy(d->done);
+    if (d->stream) cudaStreamDestroy(d->stream);
+    d->done = nullptr;
+    d->stream = nullptr;
+}
+
+// Back the DRAM arena with physical memory up to `needed` bytes.
+void grow_dram(foil_device* d, uint64_t needed) {
+    if (needed <= d->dram_mapped) return;
+    const Vmm& v = vmm();
+    uint64_t want = needed - d->dram_mapped;
+    if (want < kDramChunkMin) want = kDramChunkMin;
+    want = (want + d->granularity - 1) / d->granularity * d->granularity;
+    if (d->dram_mapped + want > kDramReserve) want = kDramReserve - d->dram_mapped;
+    CUmemAllocationProp prop = {};
+    prop.type = CU_MEM_ALLOCATION_TYPE_PINNED;
+    prop.location.type = CU_MEM_LOCATION_TYPE_DEVICE;
+    prop.location.id = d->ordinal;
+    CUmemGenericAllocationHandle h;
+    if (v.create(&h, want, &prop, 0) != CUDA_SUCCESS)
+        throw FoilError(FOIL_ERR_OOM, "tt-foil: DRAM out of memory (cuMemCreate failed)");
+    if (v.map(d->dram_base + d->dram_mapped, want, 0, h, 0) != CUDA_SUCCESS) {
+        v.release(h);
+        throw FoilError(FOIL_ERR_CUDA, "tt-foil: cuMemMap failed");
+    }
+    CUmemAccessDesc acc = {};
+    acc.location = prop.location;
+    acc.flags = CU_MEM_ACCESS_FLAGS_PROT_READWRITE;
+    if (v.set_access(d->dram_base + d->dram_mapped, want, &acc, 1) != CUDA_SUCCESS) {
+        v.unmap(d->dram_base + d->dram_mapped, want);
+        v.release(h);
+        throw FoilError(FOIL_ERR_CUDA, "tt-foil: cuMemSetAccess failed");
+    }
+    d->chunks.emplace_back(h, want);
+    d->dram_mapped += want;
+}
+
+// Device pointer of a buffer-shaped region; checks it lies in allocated
+// memory of the right arena.
+char* region_ptr(foil_device* d, bool dram, uint32_t x, uint32_t y, uint64_t off, uint64_t bytes,
+                 const char* what) {
+    if (dram) {
+        if (off > d->dram_alloc.current || bytes > d->dram_alloc.current - off)
+            throw FoilError(FOIL_ERR_INVALID, std::string("tt-foil: ") + what +
+                                                  ": DRAM range outside allocated DRAM");
+        return reinterpret_cast<char*>(d->dram_base) + off;
+    }
+    auto* c = d->core(x, y);
+    if (!c)
+        throw FoilError(FOIL_ERR_INVALID, std::string("tt-foil: ") + what + ": core (" +
+                                              std::to_string(x) + "," + std::to_string(y) +
+                                              ") was not opened");
+    if (off < foil::kL1Base || off > c->alloc.current || bytes > c->alloc.current - off)
+        throw FoilError(FOIL_ERR_INVALID, std::string("tt-foil: ") + what + ": L1 range outside allocated L1 of core (" +
+                                              std::to_string(x) + "," + std::to_string(y) + ")");
+    return c->base + off;
+}
+
+char* loc_ptr(foil_device* d, const foil::Loc& l, const char* what) {
+    return region_ptr(d, l.dram, l.core_x, l.core_y, l.offset, l.bytes, what);
+}
+
+bool aligned16(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15u) == 0; }
+
+// Wait for the device stream with a deadline; throws on timeout.
+void wait_stream(foil_device* d, std::chrono::steady_clock::time_point deadline,
+                 uint32_t core_x, uint32_t core_y) {
+    cuda_check(cudaEventRecord(d->done, d->stream), "cudaEventRecord");
+    int spins = 0;
+    while (true) {
+        cudaError_t q = cudaEventQuery(d->done);
+        if (q == cudaSuccess) return;
+        if (q != cudaErrorNotReady) cuda_check(q, "kernel execution");
+        if (std::chrono::steady_clock::now() > deadline)
+            throw FoilError(FOIL_ERR_TIMEOUT,
+                            "tt-foil: timeout waiting for kernel completion on core (" +
+                                std::to_string(core_x) + "," + std::to_string(core_y) + ")");
+        if (++spins > 2000) std::this_thread::sleep_for(std::chrono::microseconds(20));
+    }
+}
+
+void check_error_word(foil_device* d) {
+    uint32_t w = 0;
+    cuda_check(cudaMemcpyAsync(&w, d->err_word, 4, cudaMemcpyDeviceToHost, d->stream), "read error word");
+    cuda_check(cudaStreamSynchronize(d->stream), "cudaStreamSynchronize");
+    if (w != 0) {
+        cudaMemsetAsync(d->err_word, 0, 4, d->stream);
+        cudaStreamSynchronize(d->stream);
+        throw FoilError(FOIL_ERR_DEVICE, "tt-foil: a kernel reported device error 0x" +
+                                             [&] { std::ostringstream s; s << std::hex << w; return s.str(); }() +
+                                             " (bounded wait expired)");
+    }
+}
+
+}  // namespace
+
+// ============================================================ C-ABI ======
+
+extern "C" int foil_open_device(int idx, const char* /*firmware_dir*/, const foil_core* cores,
+                                size_t num_cores, foil_device** out) {
+    return guarded([&] {
+        if (!out) throw FoilError(FOIL_ERR_INVALID, "tt-foil: null output pointer");
+        *out = nullptr;
+        if (num_cores == 0 || !cores)
+            throw FoilError(FOIL_ERR_INVALID, "tt-foil: device_open requires at least one Tensix core to boot");
+        int count = 0;
+        cuda_check(cudaGetDeviceCount(&count), "cudaGetDeviceCount");
+        if (idx < 0 || idx >= count)
+            throw FoilError(FOIL_ERR_INVALID, "tt-foil: no CUDA device with index " + std::to_string(idx));
+        for (size_t i = 0; i < num_cores; ++i) {
+            if (cores[i].x >= foil::kDramNode || cores[i].y >= foil::kDramNode)
+                throw FoilError(FOIL_ERR_INVALID, "tt-foil: core coordinate out of range");
+            for (size_t j = 0; j < i; ++j)
+                if (cores[j].x == cores[i].x && cores[j].y == cores[i].y)
+                    throw FoilError(FOIL_ERR_INVALID, "tt-foil: core listed twice in open_device");
+        }
+        const Vmm& v = vmm();
+        if (!v.reserve || !v.create || !v.map || !v.set_access)
+            throw FoilError(FOIL_ERR_CUDA, "tt-foil: CUDA virtual-memory entry points unavailable");
+        auto d = std::make_unique<foil_device>();
+        d->ordinal = idx;
+        cuda_check(cudaSetDevice(idx), "cudaSetDevice");
+        cuda_check(cudaFree(nullptr), "CUDA context init");
+        try {
+            cuda_check(cudaStreamCreateWithFlags(&d->stream, cudaStreamNonBlocking), "cudaStreamCreate");
+            cuda_check(cudaEventCreateWithFlags(&d->done, cudaEventDisableTiming), "cudaEventCreate");
+            CUmemAllocationProp prop = {};
+            prop.type = CU_MEM_ALLOCATION_TYPE_PINNED;
+            prop.location.type = CU_MEM_LOCATION_TYPE_DEVICE;
+            prop.location.id = idx;
+            size_t gran = 0;
+            if (v.granularity(&gran, &prop, CU_MEM_ALLOC_GRANULARITY_RECOMMENDED) == CUDA_SUCCESS && gran)
+                d->granularity = gran;
+            if (v.reserve(&d->dram_base, kDramReserve, 0, 0, 0) != CUDA_SUCCESS)
+                throw FoilError(FOIL_ERR_CUDA, "tt-foil: cuMemAddressReserve failed");
+            d->dram_alloc = foil::BumpAllocator{0, 0, foil::kDramLimit};
+            for (size_t i = 0; i < num_cores; ++i) {
+                void* p = nullptr;
+                cuda_check(cudaMalloc(&p, foil::kL1Size), "cudaMalloc(L1 arena)");
+                foil_device::CoreArena ca{cores[i].x, cores[i].y, static_cast<char*>(p),
+                                          foil::BumpAllocator{foil::kL1Base, foil::kL1Base, foil::kL1End}};
+                d->cores.push_back(ca);
+                cuda_check(cudaMemsetAsync(p, 0, foil::kL1Size, d->stream), "cudaMemset(L1 arena)");
+            }
+            void* e = nullptr;
+            cuda_check(cudaMalloc(&e, 256), "cudaMalloc(error word)");
+            d->err_word = static_cast<uint32_t*>(e);
+            cuda_check(cudaMemsetAsync(e, 0, 256, d->stream), "cudaMemset(error word)");
+            cuda_check(cudaStreamSynchronize(d->stream), "cudaStreamSynchronize");
+        } catch (...) {
+            release_device(d.get());
+            throw;
+        }
+        *out = d.release();
+    });
+}
+
+extern "C" int foil_close_device(foil_device* d) {
+    return guarded([&] {
+        if (!d) return;
+        release_device(d);
+        delete d;
+    });
+}
+
+extern "C" int foil_allocate_buffer(foil_device* d, int32_t loc, uint64_t size, foil_core core,
+                                    foil_buffer* out) {
+    return guarded([&] {
+        if (!d || !out || d->closed) throw FoilError(FOIL_ERR_INVALID, "tt-foil: invalid device");
+        std::lock_guard<std::mutex> lk(d->mu);
+        if (size == 0) throw FoilError(FOIL_ERR_INVALID, "tt-foil: buffer size must be > 0");
+        foil_buffer b = {};
+        b.location = loc;
+        b.size_bytes = size;
+        b.core = core;
+        if (loc == FOIL_LOC_L1) {
+            auto* c = d->core(core.x, core.y);
+            if (!c)
+                throw FoilError(FOIL_ERR_INVALID, "tt-foil: L1 allocation on core (" + std::to_string(core.x) +
+                                                      "," + std::to_string(core.y) + ") which was not opened");
+            b.device_addr = c->alloc.alloc(size, foil::kL1Align, "L1");
+        } else if (loc == FOIL_LOC_DRAM) {
+            const uint64_t saved = d->dram_alloc.current;
+            b.device_addr = d->dram_alloc.alloc(size, foil::kDramAlign, "DRAM");
+            set_device(d);
+            try {
+                grow_dram(d, d->dram_alloc.current);
+            } catch (...) {
+                d->dram_alloc.current = saved;
+                throw;
+            }
+        } else {
+            throw FoilError(FOIL_ERR_INVALID, "tt-foil: unknown buffer location");
+        }
+        *out = b;
+    });
+}
+
+extern "C" int foil_free_buffer(foil_device*, const foil_buffer*) { return FOIL_OK; }
+
+static char* buffer_ptr(foil_device* d, const foil_buffer* b, uint64_t bytes, const char* what) {
+    if (!d || !b || d->closed) throw FoilError(FOIL_ERR_INVALID, "tt-foil: invalid device or buffer");
+    if (bytes > b->size_bytes)
+        throw FoilError(FOIL_ERR_INVALID, std::string("tt-foil: ") + what + " size exceeds allocation");
+    return region_ptr(d, b->location == FOIL_LOC_DRAM, b->core.x, b->core.y, b->device_addr,
+                      b->size_bytes, what);
+}
+
+extern "C" int foil_write_buffer(foil_device* d, const foil_buffer* b, const void* src, uint64_t bytes) {
+    return guarded([&] {
+        if (!d || d->closed) throw FoilError(FOIL_ERR_INVALID, "tt-foil: invalid device");
+        std::lock_guard<std::mutex> lk(d->mu);
+        char* p = buffer_ptr(d, b, bytes, "write_buffer");
+        if (bytes == 0) return;
+        if (!src) throw FoilError(FOIL_ERR_INVALID, "tt-foil: write_buffer from null pointer");
+        set_device(d);
+        cuda_check(cudaMemcpyAsync(p, src, bytes, cudaMemcpyHostToDevice, d->stream), "cudaMemcpy H2D");
+        cuda_check(cudaStreamSynchronize(d->stream), "cudaStreamSynchronize");
+    });
+}
+
+extern "C" int foil_read_buffer(foil_device* d, const foil_buffer* b, void* dst, uint64_t bytes) {
+    return guarded([&] {
+        if (!d || d->closed) throw FoilError(FOIL_ERR_INVALID, "tt-foil: invalid device");
+        std::lock_guard<std::mutex> lk(d->mu);
+        char* p = buffer_ptr(d, b, bytes, "read_buffer");
+        if (bytes == 0) return;
+        if (!dst) throw FoilError(FOIL_ERR_INVALID, "tt-foil: read_buffer into null pointer");
+        set_device(d);
+        cuda_check(cudaMemcpyAsync(dst, p, bytes, cudaMemcpyDeviceToHost, d->stream), "cudaMemcpy D2H");
+        cuda_check(cudaStreamSynchronize(d->stream), "cudaStreamSynchronize");
+    });
+}
+
+extern "C" int foil_buffer_device_ptr(foil_device* d, const foil_buffer* b, void** out) {
+    return guarded([&] {
+        if (!out) throw FoilError(FOIL_ERR_INVALID, "tt-foil: null output pointer");
+        *out = buffer_ptr(d, b, 0, "buffer_device_ptr");
+    });
+}
+
+extern "C" int foil_load_kernel(foil_device* d, const foil_risc_binary* bins, size_t n,
+                                foil_core core, foil_kernel** out) {
+    return guarded([&] {
+        if (!d || !out || d->closed) throw FoilError(FOIL_ERR_INVALID, "tt-foil: invalid device");
+        *out = nullptr;
+        if (n == 0 || !bins) throw FoilError(FOIL_ERR_INVALID, "tt-foil: no binaries provided to load_kernel");
+        if (!d->core(core.x, core.y))
+            throw FoilError(FOIL_ERR_INVALID, "tt-foil: load_kernel on core (" + std::to_string(core.x) + "," +
+                                                  std::to_string(core.y) + ") which was not opened");
+        auto k = std::make_unique<foil_kernel>();
+        k->dev = d;
+        k->core_x = core.x;
+        k->core_y = core.y;
+        std::vector<foil::Descriptor> ds;
+        for (size_t i = 0; i < n; ++i) {
+            const std::string path = bins[i].elf_path ? bins[i].elf_path : "";
+            std::ifstream f(path, std::ios::binary);
+            if (!f) throw FoilError(FOIL_ERR_NOT_FOUND, "tt-foil: ELF not found: " + path);
+            std::stringstream ss;
+            ss << f.rdbuf();
+            foil::Descriptor desc = foil::parse_descriptor(ss.str(), path);
+            int risc = bins[i].risc;
+            if (foil::role_of_risc(risc) != foil::parse_role(desc.role))
+                throw FoilError(FOIL_ERR_INVALID, "tt-foil: " + path + " has role '" + desc.role +
+                                                      "' which does not match its RISC");
+            k->present[risc] = true;
+            ds.push_back(desc);
+        }
+        k->prog = foil::resolve_program(ds);
+        *out = k.release();
+    });
+}
+
+extern "C" int foil_release_kernel(foil_kernel* k) {
+    delete k;
+    return FOIL_OK;
+}
+
+extern "C" int foil_set_runtime_args(foil_device*, foil_kernel* k, int32_t risc, const uint32_t* args,
+                                     size_t n) {
+    return guarded([&] {
+        if (!k) throw FoilError(FOIL_ERR_INVALID, "tt-foil: null kernel");
+        if (risc < 0 || risc > 4 || !k->present[risc])
+            throw FoilError(FOIL_ERR_INVALID, "tt-foil: set_runtime_args called for a RISC not in this kernel");
+        if (n > foil::kMaxRtaWords)
+            throw FoilError(FOIL_ERR_INVALID, "tt-foil: too many runtime args (max " +
+                                                  std::to_string(foil::kMaxRtaWords) + ")");
+        k->rta[risc].assign(args, args + n);
+        k->has_rta[risc] = true;
+    });
+}
+
+extern "C" int foil_register_cbs(foil_device*, foil_kernel* k, const foil_cb_config* cbs, size_t n) {
+    return guarded([&] {
+        if (!k) throw FoilError(FOIL_ERR_INVALID, "tt-foil: null kernel");
+        std::vector<foil::CbDesc> v;
+        for (size_t i = 0; i < n; ++i)
+            v.push_back({cbs[i].cb_index, cbs[i].fifo_addr, cbs[i].fifo_size, cbs[i].num_pages,
+                         cbs[i].page_size});
+        uint64_t mask = foil::validate_cbs(v);
+        k->cbs = v;
+        k->cb_mask = mask;
+    });
+}
+
+extern "C" int foil_make_noc_unicast_addr(foil_device* d, foil_core dst, uint64_t off, uint64_t* out) {
+    return guarded([&] {
+        if (!d || !out) throw FoilError(FOIL_ERR_INVALID, "tt-foil: invalid device");
+        if (!d->core(dst.x, dst.y))
+            throw FoilError(FOIL_ERR_INVALID, "tt-foil: make_noc_unicast_addr to core that was not opened");
+        *out = foil::pack_addr(dst.x, dst.y, off);
+    });
+}
+
+extern "C" int foil_make_noc_dram_addr(foil_device* d, uint64_t off, uint64_t* out) {
+    return guarded([&] {
+        if (!d || !out) throw FoilError(FOIL_ERR_INVALID, "tt-foil: invalid device");
+        if (off >= foil::kDramLimit) throw FoilError(FOIL_ERR_INVALID, "tt-foil: DRAM offset too large");
+        *out = foil::pack_addr(foil::kDramNode, foil::kDramNode, off);
+    });
+}
+
+namespace {
+
+struct ResolvedOp {
+    foil::PlanOp op;
+    const foil_kernel* k;
+    char *p0 = nullptr, *p1 = nullptr, *po = nullptr;
+    char *flag_src = nullptr, *flag_dst = nullptr, *gate = nullptr;
+};
+
+void run_op(foil_device* d, ResolvedOp& r) {
+    cudaStream_t s = d->stream;
+    switch (r.op.kind) {
+        case foil::OpKind::Copy:
+            throw_status(foil_tile_copy_dev(r.p0, r.po, r.op.in0.bytes, s));
+            break;
+        case foil::OpKind::Relu:
+            throw_status(foil_relu_tiles_dev((const uint16_t*)r.p0, (uint16_t*)r.po, r.op.in0.bytes / 2, s));
+            break;
+        case foil::OpKind::Add:
+            throw_status(foil_add_tiles_dev((const uint16_t*)r.p0, (const uint16_t*)r.p1, (uint16_t*)r.po,
+                                            r.op.in0.bytes / 2, s));
+            break;
+        case foil::OpKind::BiasAdd:
+            throw_status(foil_bias_add_tiles_dev((const uint16_t*)r.p0, (const uint16_t*)r.p1,
+                                                 (uint16_t*)r.po, 32, 32, s));
+            break;
+        case foil::OpKind::Matmul:
+            throw_status(foil::gemm::launch((const uint16_t*)r.p0, (const uint16_t*)r.p1, (uint16_t*)r.po,
+                                            r.op.Mt, r.op.Kt, r.op.Nt, nullptr, 0, d->err_word, s,
+                                            sm_count_current()));
+            break;
+        case foil::OpKind::McastForward:
+            break;  // handled in the forward phase
+    }
+}
+
+}  // namespace
+
+extern "C" int foil_execute(foil_device* d, foil_kernel* const* kernels, size_t n, int32_t timeout_ms) {
+    return guarded([&] {
+        if (!d || d->closed) throw FoilError(FOIL_ERR_INVALID, "tt-foil: invalid device");
+        if (n == 0 || !kernels) throw FoilError(FOIL_ERR_INVALID, "tt-foil: dispatch_execute_multi: no kernels");
+        std::lock_guard<std::mutex> lk(d->mu);
+        set_device(d);
+        const auto deadline = std::chrono::steady_clock::now() +
+                              std::chrono::milliseconds(timeout_ms > 0 ? timeout_ms : 5000);
+        // 1. Plan and resolve every operand before launching anything.
+        std::vector<ResolvedOp> ops;
+        for (size_t i = 0; i < n; ++i) {
+            const foil_kernel* k = kernels[i];
+            if (!k || k->dev != d) throw FoilError(FOIL_ERR_INVALID, "tt-foil: kernel belongs to another device");
+            for (auto& op : foil::plan_program(k->prog, k->core_x, k->core_y, k->rta, k->has_rta)) {
+                ResolvedOp r;
+                r.op = op;
+                r.k = k;
+                const char* what = foil::program_name(k->prog);
+                switch (op.kind) {
+                    case foil::OpKind::Copy:
+                    case foil::OpKind::Relu:
+                        r.p0 = loc_ptr(d, op.in0, what);
+                        r.po = loc_ptr(d, op.out, what);
+                        break;
+                    case foil::OpKind::Add:
+                    case foil::OpKind::BiasAdd:
+                    case foil::OpKind::Matmul:
+                        r.p0 = loc_ptr(d, op.in0, what);
+                        r.p1 = loc_ptr(d, op.in1, what);
+                        r.po = loc_ptr(d, op.out, what);
+                        break;
+                    case foil::OpKind::McastForward:
+                        r.p0 = loc_ptr(d, op.in0, what);
+                        r.p1 = loc_ptr(d, op.in1, what);
+                        r.po = loc_ptr(d, op.out, what);
+                        r.flag_src = loc_ptr(d, op.flag_src, what);
+                        r.flag_dst = loc_ptr(d, op.flag_dst, what);
+                        break;
+                }
+                if (op.gated) r.gate = loc_ptr(d, op.gate_flag, what);
+                for (char* p : {r.p0, r.p1, r.po})
+                    if (p && !aligned16(p))
+                        throw FoilError(FOIL_ERR_INVALID, std::string("tt-foil: ") + what +
+                                                              ": tile operands must be 16-byte aligned");
+                ops.push_back(r);
+            }
+        }
+        // 2. Forward phase: staging copies and ready flags (mcast producers).
+        //    Stream order puts them before every compute launch, so no kernel
+        //    ever waits on another launch.
+        bool any_gate = false;
+        for (auto& r : ops) {
+            if (r.op.kind == foil::OpKind::McastForward) {
+                cuda_check(cudaMemcpyAsync(r.p1, r.p0, r.op.in0.bytes, cudaMemcpyDeviceToDevice, d->stream),
+                           "B staging copy");
+                cuda_check(cudaMemcpyAsync(r.po, r.p1, r.op.in0.bytes, cudaMemcpyDeviceToDevice, d->stream),
+                           "B forward copy");
+                cuda_check(cudaMemcpyAsync(r.flag_dst, r.flag_src, 4, cudaMemcpyDeviceToDevice, d->stream),
+                           "flag forward copy");
+            }
+            any_gate |= r.gate != nullptr;
+        }
+        // 3. Gated consumers proceed only once their ready flag is set, as the
+        //    reference consumer spins on it (reader_consumer.cpp:40-44); a flag
+        //    that nobody sets ends in the same timeout error.
+        if (any_gate) {
+            for (auto& r : ops) {
+                if (!r.gate) continue;
+                uint32_t flag = 0;
+                cuda_check(cudaMemcpyAsync(&flag, r.gate, 4, cudaMemcpyDeviceToHost, d->stream), "flag read");
+                wait_stream(d, deadline, r.k->core_x, r.k->core_y);
+                if (flag == 0)
+                    throw FoilError(FOIL_ERR_TIMEOUT,
+                                    "tt-foil: timeout waiting for kernel completion on core (" +
+                                        std::to_string(r.k->core_x) + "," + std::to_string(r.k->core_y) +
+                                        "): ready flag never set");
+            }
+        }
+        // 4. Compute launches.
+        for (auto& r : ops) run_op(d, r);
+        // 5. Bounded wait, then the device error word.
+        wait_stream(d, deadline, kernels[0]->core_x, kernels[0]->core_y);
+        check_error_word(d);
+    });
+}
+
+// --------------------------------------------- device-resident GEMM entry ---
+extern "C" int foil_matmul_tiles_dev(const uint16_t* a, const uint16_t* b, uint16_t* c, uint32_t Mt,
+                                     uint32_t Kt, uint32_t Nt, const uint16_t* bias, int32_t relu,
+                                     void* stream) {
+    return guarded([&] {
+        if (Mt == 0 || Kt == 0 || Nt == 0) return;
+        if (Mt > 65535 || Kt > 65535 || Nt > 65535)
+            throw FoilError(FOIL_ERR_INVALID, "foil_matmul_tiles_dev: tile counts must be <= 65535");
+        if (!a || !b || !c || !aligned16(a) || !aligned16(b) || !aligned16(c) ||
+            (bias && !aligned16(bias)))
+            throw FoilError(FOIL_ERR_INVALID, "foil_matmul_tiles_dev: null or misaligned pointer");
+        uint32_t* err = error_word_for_current_device();
+        throw_status(foil::gemm::launch(a, b, c, Mt, Kt, Nt, bias, relu, err, (cudaStream_t)stream,
+                                        sm_count_current()));
+    });
+}
+
+extern "C" int foil_device_error_dev(void* stream, uint32_t* out) {
+    return guarded([&] {
+        if (!out) throw FoilError(FOIL_ERR_INVALID, "tt-foil: null output pointer");
+        uint32_t* err = error_word_for_current_device();
+        cudaStream_t s = (cudaStream_t)stream;
+        cuda_check(cudaMemcpyAsync(out, err, 4, cudaMemcpyDeviceToHost, s), "read error word");
+        cuda_check(cudaMemsetAsync(err, 0, 4, s), "clear error word");
+        cuda_check(cudaStreamSynchronize(s), "cudaStreamSynchronize");
+    });
+}

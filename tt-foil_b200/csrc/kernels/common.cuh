@@ -1,0 +1,62 @@
+// Shared device helpers for the sm_100a kernels of libfoil.
+#pragma once
+
+#include <cstdint>
+#include <cuda_runtime.h>
+#include <cstdio>
+
+namespace foil {
+
+// bf16 <-> fp32 with the exact arithmetic of the tt-foil CPU golden
+// (tests/tile_utils.hpp:33-47): widening is a 16-bit shift; narrowing adds
+// 0x7fff plus the lowest kept bit and truncates (round to nearest even, no
+// NaN special case).  Using the same integer formula keeps every
+// element-wise kernel bit-identical to the golden, NaN payloads included.
+__device__ __forceinline__ float bf16_bits_to_f32(uint32_t b) {
+    return __uint_as_float(b << 16);
+}
+
+__device__ __forceinline__ uint32_t f32_to_bf16_bits(float f) {
+    uint32_t u = __float_as_uint(f);
+    u += 0x7fffu + ((u >> 16) & 1u);
+    return u >> 16;
+}
+
+// fp32 addition with the NaN results of the x86-64 host that computes the
+// reference golden (SSE addss): a NaN operand propagates quieted, the first
+// operand winning; an invalid sum (inf - inf) yields the default NaN
+// 0xffc00000.  The GPU's adder returns one canonical NaN instead, so without
+// this the narrowed bf16 of a NaN result would differ from the golden.
+__device__ __forceinline__ float host_add_f32(float a, float b) {
+    const uint32_t ua = __float_as_uint(a), ub = __float_as_uint(b);
+    const bool na = (ua & 0x7fffffffu) > 0x7f800000u;
+    const bool nb = (ub & 0x7fffffffu) > 0x7f800000u;
+    if (na) return __uint_as_float(ua | 0x00400000u);
+    if (nb) return __uint_as_float(ub | 0x00400000u);
+    const float r = __fadd_rn(a, b);
+    return r != r ? __uint_as_float(0xffc00000u) : r;
+}
+
+// Two bf16 in one 32-bit word (low half = first element).
+__device__ __forceinline__ uint32_t pack_bf16x2(uint32_t lo, uint32_t hi) {
+    return (lo & 0xffffu) | (hi << 16);
+}
+
+// Device-side error codes written to the error word.
+enum : uint32_t {
+    kErrWaitTimeout = 1u,  // a bounded mbarrier wait gave up
+    kErrBadShape = 2u,     // kernel saw a shape it cannot handle
+};
+
+// Wall-clock nanoseconds (for bounded waits).
+__device__ __forceinline__ uint64_t global_ns() {
+    uint64_t t;
+    asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t));
+    return t;
+}
+
+}  // namespace foil
+
+// Host-side launch accounting shared by every entry point (defined in
+// foil_runtime.cpp).
+void foil_count_launch();

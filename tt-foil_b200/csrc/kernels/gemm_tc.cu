@@ -1,0 +1,530 @@
+// Tiled bf16 GEMM on Blackwell tensor cores (tcgen05 + TMEM + TMA), reading
+// and writing the tt-foil tile layout directly (no relayout pass).
+//
+//   C (Mt x Nt tiles) = A (Mt x Kt tiles) . B (Kt x Nt tiles)
+//   fp32 accumulation in TMEM, bf16 output, optional fused bias + relu.
+//
+// Replaces the reference's matmul pipeline: reader (examples/matmul_mnk/
+// kernels/reader.cpp:28-57), compute (compute.cpp:23-53, matmul_tiles with
+// fp32 DST accumulation) and writer (writer.cpp:16-34), and — fused into the
+// epilogue — bias_add (examples/bias_add/kernels/compute.cpp:19-42) and relu
+// (examples/relu/kernels/compute.cpp:19-45).
+//
+// How the tile layout feeds tcgen05 without a relayout pass
+// ---------------------------------------------------------
+// A face row is 16 bf16 = 32 bytes, which is exactly one SWIZZLE_32B atom
+// row and one UMMA K-step (K = 16).  Two families of 5-D TMA tensor maps
+// describe the tile stream so that each TMA box lands in shared memory as a
+// canonical UMMA operand, with TMA applying the 32-byte swizzle on the way:
+//
+//  * A (rows = m, contiguous = k: K-major).  One map per face column fc:
+//      dims (c0:16 @2B, r0:16 @32B, fr:2 @1024B, kt:Kt @2048B, mt:Mt @Kt*2KiB)
+//      base A + fc*512B, box (16,16,2,1,4)  ->  128 rows x 32 B, 8-row groups
+//      256 B apart: K-major SW32 with SBO = 256 B.
+//  * B (rows = k, contiguous = n: MN-major).  One map per face row fr:
+//      dims (c0:16 @2B, r0:16 @32B, fc:2 @512B, nt:Nt @2KiB, kt:Kt @Nt*2KiB)
+//      base B + fr*1024B, box (16,16,2,8,2) -> per kt: 16 atoms of 16 n x 16 k
+//      (512 B each): MN-major SW32 with LBO = 512 B (next 16 n), SBO = 256 B
+//      (next 8 k).
+//  A K-step (kt, f) pairs A face column f with B face row f, i.e. the K
+//  range kt*32 + f*16 + [0,16).
+//
+// Kernel organisation (persistent, warp-specialised, 1 CTA per SM)
+// ------------------------------------------------------------------
+//  warp 0      TMA producer  (4-stage smem ring, 48 KiB per stage)
+//  warp 1      MMA issuer    (tcgen05.mma 128x256x16, commits free stages)
+//  warps 2..5  epilogue      (tcgen05.ld -> bf16 (+bias, relu) -> global)
+//  TMEM holds two 128x256 fp32 accumulators (512 columns) so the epilogue of
+//  tile i overlaps the main loop of tile i+1.  Output tiles of 128x256 are
+//  visited in bands of 8 column-blocks for L2 reuse.
+//
+// Every mbarrier wait is bounded (2 s of wall time); on expiry the kernel
+// records kErrWaitTimeout in the error word, all roles leave their loops,
+// in-flight copies and MMAs are drained with bounded waits and TMEM is freed.
+#include <cuda.h>
+#include <cudaTypedefs.h>
+#include <mutex>
+#include <cstdio>
+#include <cstring>
+
+#include "common.cuh"
+#include "gemm_tc.cuh"
+#include "../../../include/foil_c.h"
+
+extern "C" void foil_set_error(int status, const char* msg);
+
+namespace foil {
+namespace gemm {
+
+// ---------------------------------------------------------------- PTX ---
+__device__ __forceinline__ uint32_t smem_u32(const void* p) {
+    return static_cast<uint32_t>(__cvta_generic_to_shared(p));
+}
+
+__device__ __forceinline__ void mbar_init(uint64_t* bar, uint32_t count) {
+    asm volatile("mbarrier.init.shared::cta.b64 [%0], %1;" ::"r"(smem_u32(bar)), "r"(count));
+}
+
+__device__ __forceinline__ void mbar_expect_tx(uint64_t* bar, uint32_t bytes) {
+    asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;" ::"r"(smem_u32(bar)),
+                 "r"(bytes)
+                 : "memory");
+}
+
+__device__ __forceinline__ void mbar_arrive(uint64_t* bar) {
+    asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];" ::"r"(smem_u32(bar)) : "memory");
+}
+
+__device__ __forceinline__ bool mbar_try_wait(uint64_t* bar, uint32_t parity) {
+    uint32_t done;
+    asm volatile(
+        "{\n\t.reg .pred p;\n\t"
+        "mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2;\n\t"
+        "selp.b32 %0, 1, 0, p;\n\t}"
+        : "=r"(done)
+        : "r"(smem_u32(bar)), "r"(parity)
+        : "memory");
+    return done != 0;
+}
+
+constexpr uint64_t kWaitLimitNs = 2000000000ull;  // 2 s per wait
+
+// Wait for completion of phase `parity`.  Returns false if the CTA is
+// aborting or this wait exceeded its wall-time limit (then it raises the
+// abort flag and records the error).
+__device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity,
+                                          volatile uint32_t* abort_flag, uint32_t* err) {
+#pragma unroll 1
+    for (int i = 0; i < 32; ++i)
+        if (mbar_try_wait(bar, parity)) return true;
+    const uint64_t t0 = global_ns();
+#pragma unroll 1
+    while (true) {
+        if (mbar_try_wait(bar, parity)) return true;
+        if (*abort_flag) return false;
+        if (global_ns() - t0 > kWaitLimitNs) {
+            *abort_flag = 1u;
+            if (err) atomicOr(err, kErrWaitTimeout);
+            return false;
+        }
+    }
+}
+
+// Bounded drain wait used on the way out (ignores the abort flag).
+__device__ __forceinline__ void mbar_drain(uint64_t* bar, uint32_t parity, uint64_t limit_ns) {
+    const uint64_t t0 = global_ns();
+#pragma unroll 1
+    while (!mbar_try_wait(bar, parity)) {
+        if (global_ns() - t0 > limit_ns) return;
+    }
+}
+
+__device__ __forceinline__ void tma_load_5d(const CUtensorMap* map, uint64_t* bar, void* dst,
+                                            int c0, int c1, int c2, int c3, int c4) {
+    asm volatile(
+        "cp.async.bulk.tensor.5d.shared::cluster.global.mbarrier::complete_tx::bytes"
+        " [%0], [%1, {%3, %4, %5, %6, %7}], [%2];" ::"r"(smem_u32(dst)),
+        "l"(reinterpret_cast<uint64_t>(map)), "r"(smem_u32(bar)), "r"(c0), "r"(c1), "r"(c2),
+        "r"(c3), "r"(c4)
+        : "memory");
+}
+
+__device__ __forceinline__ void tc_fence_before() {
+    asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory");
+}
+__device__ __forceinline__ void tc_fence_after() {
+    asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
+}
+
+__device__ __forceinline__ void tc_mma(uint32_t d_tmem, uint64_t a_desc, uint64_t b_desc,
+                                       uint32_t idesc, uint32_t accumulate) {
+    asm volatile(
+        "{\n\t.reg .pred p;\n\t"
+        "setp.ne.b32 p, %4, 0;\n\t"
+        "tcgen05.mma.cta_group::1.kind::f16 [%0], %1, %2, %3, p;\n\t}" ::"r"(d_tmem),
+        "l"(a_desc), "l"(b_desc), "r"(idesc), "r"(accumulate)
+        : "memory");
+}
+
+__device__ __forceinline__ void tc_commit(uint64_t* bar) {
+    asm volatile(
+        "tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::"r"(
+            smem_u32(bar))
+        : "memory");
+}
+
+__device__ __forceinline__ void tmem_ld16(uint32_t taddr, uint32_t (&v)[16]) {
+    asm volatile(
+        "tcgen05.ld.sync.aligned.32x32b.x16.b32 "
+        "{%0,%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15}, [%16];"
+        : "=r"(v[0]), "=r"(v[1]), "=r"(v[2]), "=r"(v[3]), "=r"(v[4]), "=r"(v[5]), "=r"(v[6]),
+          "=r"(v[7]), "=r"(v[8]), "=r"(v[9]), "=r"(v[10]), "=r"(v[11]), "=r"(v[12]),
+          "=r"(v[13]), "=r"(v[14]), "=r"(v[15])
+        : "r"(taddr));
+}
+
+__device__ __forceinline__ void tmem_ld_wait() {
+    asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
+}
+
+// Shared-memory matrix descriptor (tcgen05 format): start >> 4 in [0,14),
+// LBO >> 4 in [16,30), SBO >> 4 in [32,46), fixed version bit 46, layout type
+// in [61,64) (6 = SWIZZLE_32B).
+__host__ __device__ constexpr uint64_t smem_desc_base(uint32_t lbo, uint32_t sbo) {
+    return ((uint64_t)((lbo >> 4) & 0x3fffu) << 16) | ((uint64_t)((sbo >> 4) & 0x3fffu) << 32) |
+           (1ull << 46) | (6ull << 61);
+}
+
+// Instruction descriptor for kind::f16: f32 accumulate (bits 4-5 = 1), bf16
+// A and B (bits 7-9, 10-12 = 1), A K-major (bit 15 = 0), B MN-major (bit 16
+// = 1), N >> 3 at bit 17, M >> 4 at bit 24.
+__host__ __device__ constexpr uint32_t make_idesc(uint32_t m, uint32_t n) {
+    return (1u << 4) | (1u << 7) | (1u << 10) | (0u << 15) | (1u << 16) | ((n >> 3) << 17) |
+           ((m >> 4) << 24);
+}
+
+// --------------------------------------------------------------- kernel ---
+constexpr int kBM = 128;           // rows per CTA tile (4 tile-rows)
+constexpr int kBN = 256;           // cols per CTA tile (8 tile-cols)
+constexpr int kBKT = 2;            // K tiles per stage (K = 64)
+constexpr int kStages = 4;
+constexpr int kABytes = kBM * kBKT * 32 * 2;  // 16 KiB
+constexpr int kBBytes = kBN * kBKT * 32 * 2;  // 32 KiB
+constexpr int kStageBytes = kABytes + kBBytes;
+constexpr int kThreads = 192;
+constexpr int kTmemCols = 512;
+constexpr int kBandN = 8;           // column-blocks per raster band
+constexpr int kSmemBytes = kStages * kStageBytes + 1024 /*align*/ + 256 /*barriers*/;
+
+struct Params {
+    uint16_t* c;
+    const uint16_t* bias;
+    uint32_t Mt, Kt, Nt;
+    uint32_t m_blocks, n_blocks;
+    int relu;
+    uint32_t* err;
+};
+
+__device__ __forceinline__ void tile_coords(uint32_t tile, uint32_t m_blocks, uint32_t n_blocks,
+                                            uint32_t& mb, uint32_t& nb) {
+    const uint32_t band_tiles = m_blocks * kBandN;
+    const uint32_t band = tile / band_tiles;
+    const uint32_t inner = tile - band * band_tiles;
+    const uint32_t width = min((uint32_t)kBandN, n_blocks - band * kBandN);
+    mb = inner / width;
+    nb = band * kBandN + (inner - mb * width);
+}
+
+// out = bf16(acc) [+ bias -> bf16] [relu], the composition of the reference
+// goldens (matmul, bias_add, relu), per element.
+__device__ __forceinline__ uint32_t epi1(uint32_t acc_bits, uint32_t bias_bits, bool has_bias,
+                                         bool relu) {
+    uint32_t o = f32_to_bf16_bits(__uint_as_float(acc_bits));
+    if (has_bias) o = f32_to_bf16_bits(host_add_f32(bf16_bits_to_f32(o), bf16_bits_to_f32(bias_bits)));
+    if (relu && bf16_bits_to_f32(o) < 0.0f) o = 0u;
+    return o;
+}
+
+__global__ void __launch_bounds__(kThreads, 1)
+gemm_tiles_kernel(const __grid_constant__ CUtensorMap tmA0, const __grid_constant__ CUtensorMap tmA1,
+                  const __grid_constant__ CUtensorMap tmB0, const __grid_constant__ CUtensorMap tmB1,
+                  const Params p) {
+    extern __shared__ uint8_t smem_raw[];
+    uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) &
+                                               ~uintptr_t(1023));
+    uint64_t* full = reinterpret_cast<uint64_t*>(smem + kStages * kStageBytes);
+    uint64_t* empty = full + kStages;
+    uint64_t* tfull = empty + kStages;
+    uint64_t* tempty = tfull + 2;
+    uint64_t* drain = tempty + 2;
+    uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(drain + 1);
+    volatile uint32_t* abort_flag = tmem_slot + 1;
+
+    const uint32_t warp = threadIdx.x >> 5, lane = threadIdx.x & 31u;
+
+    if (threadIdx.x == 0) {
+        for (int s = 0; s < kStages; ++s) {
+            mbar_init(&full[s], 1);
+            mbar_init(&empty[s], 1);
+        }
+        for (int b = 0; b < 2; ++b) {
+            mbar_init(&tfull[b], 1);
+            mbar_init(&tempty[b], 4);
+        }
+        mbar_init(drain, 1);
+        *abort_flag = 0u;
+        asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+        asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+    }
+    if (warp == 0) {
+        asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(
+                         smem_u32(tmem_slot)),
+                     "r"(kTmemCols)
+                     : "memory");
+        asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;" ::: "memory");
+    }
+    if (warp == 1 && lane == 0) {
+        asm volatile("prefetch.tensormap [%0];" ::"l"(reinterpret_cast<uint64_t>(&tmA0)) : "memory");
+        asm volatile("prefetch.tensormap [%0];" ::"l"(reinterpret_cast<uint64_t>(&tmA1)) : "memory");
+        asm volatile("prefetch.tensormap [%0];" ::"l"(reinterpret_cast<uint64_t>(&tmB0)) : "memory");
+        asm volatile("prefetch.tensormap [%0];" ::"l"(reinterpret_cast<uint64_t>(&tmB1)) : "memory");
+    }
+    tc_fence_before();
+    __syncthreads();
+    tc_fence_after();
+    const uint32_t tmem_base = *tmem_slot;
+
+    const uint32_t num_tiles = p.m_blocks * p.n_blocks;
+    const uint32_t num_kb = (p.Kt + kBKT - 1) / kBKT;
+
+    if (warp == 0) {
+        if (lane == 0) {
+            // ------------------------------------------------ TMA producer
+            uint32_t stage = 0, phase = 0;
+            uint32_t issued = 0;
+            bool ok = true;
+            for (uint32_t tile = blockIdx.x; ok && tile < num_tiles; tile += gridDim.x) {
+                uint32_t mb, nb;
+                tile_coords(tile, p.m_blocks, p.n_blocks, mb, nb);
+                for (uint32_t kb = 0; kb < num_kb; ++kb) {
+                    if (!mbar_wait(&empty[stage], phase ^ 1u, abort_flag, p.err)) {
+                        ok = false;
+                        break;
+                    }
+                    uint8_t* a_s = smem + stage * kStageBytes;
+                    uint8_t* b_s = a_s + kABytes;
+                    mbar_expect_tx(&full[stage], kStageBytes);
+                    const int kt0 = (int)(kb * kBKT);
+#pragma unroll
+                    for (int ktl = 0; ktl < kBKT; ++ktl) {
+                        tma_load_5d(&tmA0, &full[stage], a_s + (ktl * 2 + 0) * 4096, 0, 0, 0,
+                                    kt0 + ktl, (int)(mb * 4));
+                        tma_load_5d(&tmA1, &full[stage], a_s + (ktl * 2 + 1) * 4096, 0, 0, 0,
+                                    kt0 + ktl, (int)(mb * 4));
+                    }
+                    tma_load_5d(&tmB0, &full[stage], b_s, 0, 0, 0, (int)(nb * 8), kt0);
+                    tma_load_5d(&tmB1, &full[stage], b_s + 16384, 0, 0, 0, (int)(nb * 8), kt0);
+                    ++issued;
+                    if (++stage == kStages) {
+                        stage = 0;
+                        phase ^= 1u;
+                    }
+                }
+            }
+            // Drain: wait (bounded) for the last fill of every stage.
+            uint32_t n_last = issued < (uint32_t)kStages ? issued : (uint32_t)kStages;
+            for (uint32_t i = 0; i < n_last; ++i) {
+                uint32_t fill = issued - 1 - i;
+                mbar_drain(&full[fill % kStages], (fill / kStages) & 1u, 100000000ull);
+            }
+        }
+    } else if (warp == 1) {
+        if (lane == 0) {
+            // ------------------------------------------------ MMA issuer
+            constexpr uint32_t idesc = make_idesc(kBM, kBN);
+            constexpr uint64_t a_base = smem_desc_base(16, 256);   // K-major SW32
+            constexpr uint64_t b_base = smem_desc_base(512, 256);  // MN-major SW32
+            uint32_t stage = 0, phase = 0, acc = 0, acc_phase = 0;
+            bool ok = true;
+            for (uint32_t tile = blockIdx.x; ok && tile < num_tiles; tile += gridDim.x) {
+                if (!mbar_wait(&tempty[acc], acc_phase ^ 1u, abort_flag, p.err)) break;
+                tc_fence_after();
+                const uint32_t d_tmem = tmem_base + acc * kBN;
+                for (uint32_t kb = 0; kb < num_kb; ++kb) {
+                    if (!mbar_wait(&full[stage], phase, abort_flag, p.err)) {
+                        ok = false;
+                        break;
+                    }
+                    tc_fence_after();
+                    const uint32_t a_addr = smem_u32(smem + stage * kStageBytes);
+                    const uint32_t b_addr = a_addr + kABytes;
+#pragma unroll
+                    for (uint32_t s = 0; s < 4; ++s) {
+                        const uint32_t a_off = s * 4096u;
+                        const uint32_t b_off = (s & 1u) * 16384u + (s >> 1) * 8192u;
+                        const uint64_t ad = a_base | (uint64_t)(((a_addr + a_off) >> 4) & 0x3fffu);
+                        const uint64_t bd = b_base | (uint64_t)(((b_addr + b_off) >> 4) & 0x3fffu);
+                        tc_mma(d_tmem, ad, bd, idesc, (kb | s) != 0u);
+                    }
+                    tc_commit(&empty[stage]);
+                    if (++stage == kStages) {
+                        stage = 0;
+                        phase ^= 1u;
+                    }
+                }
+                if (!ok) break;
+                tc_commit(&tfull[acc]);
+                if (++acc == 2) {
+                    acc = 0;
+                    acc_phase ^= 1u;
+                }
+            }
+            // Drain all MMAs issued by this thread before TMEM is released.
+            tc_commit(drain);
+            mbar_drain(drain, 0, 100000000ull);
+        }
+    } else {
+        // ---------------------------------------------------- epilogue
+        const uint32_t q = warp & 3u;  // TMEM lane quadrant this warp may access
+        const uint32_t fr = lane >> 4, r0 = lane & 15u;
+        const bool has_bias = p.bias != nullptr;
+        const bool relu = p.relu != 0;
+        uint32_t acc = 0, acc_phase = 0;
+        for (uint32_t tile = blockIdx.x; tile < num_tiles; tile += gridDim.x) {
+            uint32_t mb, nb;
+            tile_coords(tile, p.m_blocks, p.n_blocks, mb, nb);
+            // One lane waits; the warp then proceeds converged (tcgen05.ld is
+            // a warp-wide .sync.aligned instruction).
+            bool ok = true;
+            if (lane == 0) ok = mbar_wait(&tfull[acc], acc_phase, abort_flag, p.err);
+            ok = __shfl_sync(0xffffffffu, ok ? 1 : 0, 0) != 0;
+            if (!ok) break;
+            tc_fence_after();
+            const uint32_t mt = mb * 4 + q;
+            const uint32_t t_row = tmem_base + ((q * 32u) << 16) + acc * kBN;
+#pragma unroll 1
+            for (uint32_t nt_l = 0; nt_l < 8; ++nt_l) {
+                uint32_t v0[16], v1[16];
+                tmem_ld16(t_row + nt_l * 32u, v0);
+                tmem_ld16(t_row + nt_l * 32u + 16u, v1);
+                tmem_ld_wait();
+                const uint32_t nt = nb * 8 + nt_l;
+                if (mt < p.Mt && nt < p.Nt) {
+                    uint32_t bias_w[16];
+                    if (has_bias) {
+                        const uint4* bp = reinterpret_cast<const uint4*>(p.bias + nt * 32u);
+                        uint4 b0 = __ldg(bp), b1 = __ldg(bp + 1), b2 = __ldg(bp + 2), b3 = __ldg(bp + 3);
+                        bias_w[0] = b0.x; bias_w[1] = b0.y; bias_w[2] = b0.z; bias_w[3] = b0.w;
+                        bias_w[4] = b1.x; bias_w[5] = b1.y; bias_w[6] = b1.z; bias_w[7] = b1.w;
+                        bias_w[8] = b2.x; bias_w[9] = b2.y; bias_w[10] = b2.z; bias_w[11] = b2.w;
+                        bias_w[12] = b3.x; bias_w[13] = b3.y; bias_w[14] = b3.z; bias_w[15] = b3.w;
+                    } else {
+#pragma unroll
+                        for (int i = 0; i < 16; ++i) bias_w[i] = 0u;
+                    }
+                    uint32_t o[16];
+#pragma unroll
+                    for (int i = 0; i < 8; ++i) {
+                        // face column 0: columns 2i, 2i+1 ; face column 1: 16+2i, 17+2i
+                        uint32_t bl0 = bias_w[i] & 0xffffu, bh0 = bias_w[i] >> 16;
+                        uint32_t bl1 = bias_w[8 + i] & 0xffffu, bh1 = bias_w[8 + i] >> 16;
+                        o[i] = pack_bf16x2(epi1(v0[2 * i], bl0, has_bias, relu),
+                                           epi1(v0[2 * i + 1], bh0, has_bias, relu));
+                        o[8 + i] = pack_bf16x2(epi1(v1[2 * i], bl1, has_bias, relu),
+                                               epi1(v1[2 * i + 1], bh1, has_bias, relu));
+                    }
+                    uint16_t* tile_base = p.c + ((uint64_t)mt * p.Nt + nt) * 1024u;
+                    uint4* d0 = reinterpret_cast<uint4*>(tile_base + (fr * 2u + 0u) * 256u + r0 * 16u);
+                    uint4* d1 = reinterpret_cast<uint4*>(tile_base + (fr * 2u + 1u) * 256u + r0 * 16u);
+                    d0[0] = make_uint4(o[0], o[1], o[2], o[3]);
+                    d0[1] = make_uint4(o[4], o[5], o[6], o[7]);
+                    d1[0] = make_uint4(o[8], o[9], o[10], o[11]);
+                    d1[1] = make_uint4(o[12], o[13], o[14], o[15]);
+                }
+            }
+            tc_fence_before();
+            __syncwarp();
+            if (lane == 0) mbar_arrive(&tempty[acc]);
+            if (++acc == 2) {
+                acc = 0;
+                acc_phase ^= 1u;
+            }
+        }
+    }
+
+    tc_fence_before();
+    __syncthreads();
+    if (warp == 0) {
+        __syncwarp();
+        tc_fence_after();
+        asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem_base),
+                     "r"(kTmemCols)
+                     : "memory");
+    }
+}
+
+// ------------------------------------------------------------------ host ---
+static PFN_cuTensorMapEncodeTiled_v12000 encode_fn() {
+    static PFN_cuTensorMapEncodeTiled_v12000 fn = nullptr;
+    static std::once_flag once;
+    std::call_once(once, [] {
+        cudaDriverEntryPointQueryResult q;
+        void* f = nullptr;
+        if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &f, cudaEnableDefault, &q) ==
+                cudaSuccess &&
+            q == cudaDriverEntryPointSuccess)
+            fn = reinterpret_cast<PFN_cuTensorMapEncodeTiled_v12000>(f);
+    });
+    return fn;
+}
+
+static bool make_map(CUtensorMap* m, const void* base, const cuuint64_t dims[5],
+                     const cuuint64_t strides[4], const cuuint32_t box[5]) {
+    auto fn = encode_fn();
+    if (!fn) return false;
+    const cuuint32_t estr[5] = {1, 1, 1, 1, 1};
+    CUresult r = fn(m, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 5, const_cast<void*>(base), dims, strides,
+                    box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_32B,
+                    CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+    return r == CUDA_SUCCESS;
+}
+
+// Tensor maps of the A and B tile streams (see the file comment).
+bool make_operand_maps(const uint16_t* a, const uint16_t* b, uint32_t Mt, uint32_t Kt,
+                       uint32_t Nt, CUtensorMap maps[4]) {
+    const cuuint64_t a_dims[5] = {16, 16, 2, Kt, Mt};
+    const cuuint64_t a_str[4] = {32, 1024, 2048, (cuuint64_t)Kt * 2048};
+    const cuuint32_t a_box[5] = {16, 16, 2, 1, 4};
+    const cuuint64_t b_dims[5] = {16, 16, 2, Nt, Kt};
+    const cuuint64_t b_str[4] = {32, 512, 2048, (cuuint64_t)Nt * 2048};
+    const cuuint32_t b_box[5] = {16, 16, 2, 8, (cuuint32_t)kBKT};
+    return make_map(&maps[0], a, a_dims, a_str, a_box) &&
+           make_map(&maps[1], a + 256, a_dims, a_str, a_box) &&
+           make_map(&maps[2], b, b_dims, b_str, b_box) &&
+           make_map(&maps[3], b + 512, b_dims, b_str, b_box);
+}
+
+int launch(const uint16_t* a, const uint16_t* b, uint16_t* c, uint32_t Mt, uint32_t Kt,
+           uint32_t Nt, const uint16_t* bias, int relu, uint32_t* err, cudaStream_t stream,
+           int max_ctas) {
+    CUtensorMap maps[4];
+    if (!make_operand_maps(a, b, Mt, Kt, Nt, maps)) {
+        foil_set_error(FOIL_ERR_CUDA, "foil_matmul_tiles: cuTensorMapEncodeTiled failed");
+        return FOIL_ERR_CUDA;
+    }
+    static std::once_flag attr_once;
+    static cudaError_t attr_err = cudaSuccess;
+    std::call_once(attr_once, [] {
+        attr_err = cudaFuncSetAttribute(gemm_tiles_kernel,
+                                        cudaFuncAttributeMaxDynamicSharedMemorySize, kSmemBytes);
+    });
+    if (attr_err != cudaSuccess) {
+        foil_set_error(FOIL_ERR_CUDA, "foil_matmul_tiles: cudaFuncSetAttribute failed");
+        return FOIL_ERR_CUDA;
+    }
+    Params p;
+    p.c = c;
+    p.bias = bias;
+    p.Mt = Mt;
+    p.Kt = Kt;
+    p.Nt = Nt;
+    p.m_blocks = (Mt + 3) / 4;
+    p.n_blocks = (Nt + 7) / 8;
+    p.relu = relu;
+    p.err = err;
+    const uint32_t tiles = p.m_blocks * p.n_blocks;
+    const uint32_t grid = tiles < (uint32_t)max_ctas ? tiles : (uint32_t)max_ctas;
+    gemm_tiles_kernel<<<grid, kThreads, kSmemBytes, stream>>>(maps[0], maps[1], maps[2], maps[3], p);
+    cudaError_t e = cudaGetLastError();
+    if (e != cudaSuccess) {
+        char buf[256];
+        snprintf(buf, sizeof buf, "foil_matmul_tiles: launch failed: %s", cudaGetErrorString(e));
+        foil_set_error(FOIL_ERR_CUDA, buf);
+        return FOIL_ERR_CUDA;
+    }
+    foil_count_launch();
+    return FOIL_OK;
+}
+
+}  // namespace gemm
+}  // namespace foil

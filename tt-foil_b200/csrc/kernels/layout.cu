@@ -1,0 +1,197 @@
+// Layout kernels: tilize, untilize, tile_copy.
+//
+// Tile layout (the tt-foil wire format, tests/tile_utils.hpp:4-12): a 32x32
+// bf16 tile is four 16x16 faces, each row-major; a face row is 16 values =
+// 32 bytes = two 16-byte chunks.  Tilize is therefore a permutation of
+// 16-byte chunks.  Each CTA moves one "band" of 32 rows x up to 8 tiles
+// (16 KiB): global reads and writes are both fully coalesced 16-byte vector
+// accesses, and the permutation happens in shared memory.  The shared-memory
+// index is XOR-swizzled so that every 8-lane phase of a 16-byte access hits 8
+// distinct 4-bank groups (conflict-free on both sides).
+#include "common.cuh"
+#include "../../../include/foil_c.h"
+
+namespace foil {
+namespace {
+
+constexpr int kBandTiles = 8;                      // tiles per band
+constexpr int kChunksPerTile = 128;                // 2 KiB / 16 B
+constexpr int kBandChunks = kBandTiles * kChunksPerTile;
+constexpr int kLayoutThreads = 256;
+
+// Tile-layout chunk index (inside a band) of row r, 16-byte chunk j of the
+// band's row-major slice.  j = tile*4 + (col_in_tile / 8).
+__device__ __forceinline__ uint32_t band_tile_chunk(uint32_t r, uint32_t j) {
+    uint32_t t = j >> 2;             // tile inside the band
+    uint32_t cc = (j & 3u) * 8u;     // column inside the tile
+    uint32_t fr = r >> 4, r0 = r & 15u;
+    uint32_t fc = cc >> 4, h = (cc >> 3) & 1u;
+    return t * kChunksPerTile + (fr * 2u + fc) * 32u + r0 * 2u + h;
+}
+
+// Bank-conflict-free placement of a band chunk in shared memory: XOR bits 1
+// and 2 of the index with the face-column bit (bit 5) and tile parity
+// (bit 7).  Stays inside the same aligned group of 8 chunks (a bijection).
+__device__ __forceinline__ uint32_t smem_slot(uint32_t idx) {
+    return idx ^ (((idx >> 7) & 1u) << 2) ^ (((idx >> 5) & 1u) << 1);
+}
+
+__global__ void __launch_bounds__(kLayoutThreads)
+tilize_kernel(const uint4* __restrict__ in, uint4* __restrict__ out,
+              uint32_t rows, uint32_t cols) {
+    __shared__ uint4 buf[kBandChunks];
+    const uint32_t Ct = cols / 32u, Rt = rows / 32u;
+    const uint32_t bands_per_row = (Ct + kBandTiles - 1) / kBandTiles;
+    const uint64_t num_bands = (uint64_t)Rt * bands_per_row;
+    const uint32_t row_chunks = cols / 8u;  // 16-byte chunks per input row
+
+    for (uint64_t band = blockIdx.x; band < num_bands; band += gridDim.x) {
+        const uint32_t rt = (uint32_t)(band / bands_per_row);
+        const uint32_t ct0 = (uint32_t)(band % bands_per_row) * kBandTiles;
+        const uint32_t bw = min((uint32_t)kBandTiles, Ct - ct0);  // tiles
+        const uint32_t jn = bw * 4u;                              // chunks/row
+        const uint32_t total = 32u * jn;
+        // Coalesced row reads -> swizzled tile-order slots.
+        for (uint32_t i = threadIdx.x; i < total; i += kLayoutThreads) {
+            uint32_t r = i / jn, j = i - r * jn;
+            uint4 v = __ldcs(in + (uint64_t)(rt * 32u + r) * row_chunks + ct0 * 4u + j);
+            buf[smem_slot(band_tile_chunk(r, j))] = v;
+        }
+        __syncthreads();
+        // Contiguous tile-stream writes.
+        uint4* dst = out + ((uint64_t)rt * Ct + ct0) * kChunksPerTile;
+        for (uint32_t o = threadIdx.x; o < total; o += kLayoutThreads)
+            __stcs(dst + o, buf[smem_slot(o)]);
+        __syncthreads();
+    }
+}
+
+__global__ void __launch_bounds__(kLayoutThreads)
+untilize_kernel(const uint4* __restrict__ in, uint4* __restrict__ out,
+                uint32_t rows, uint32_t cols) {
+    __shared__ uint4 buf[kBandChunks];
+    const uint32_t Ct = cols / 32u, Rt = rows / 32u;
+    const uint32_t bands_per_row = (Ct + kBandTiles - 1) / kBandTiles;
+    const uint64_t num_bands = (uint64_t)Rt * bands_per_row;
+    const uint32_t row_chunks = cols / 8u;
+
+    for (uint64_t band = blockIdx.x; band < num_bands; band += gridDim.x) {
+        const uint32_t rt = (uint32_t)(band / bands_per_row);
+        const uint32_t ct0 = (uint32_t)(band % bands_per_row) * kBandTiles;
+        const uint32_t bw = min((uint32_t)kBandTiles, Ct - ct0);
+        const uint32_t jn = bw * 4u;
+        const uint32_t total = 32u * jn;
+        const uint4* src = in + ((uint64_t)rt * Ct + ct0) * kChunksPerTile;
+        for (uint32_t o = threadIdx.x; o < total; o += kLayoutThreads)
+            buf[smem_slot(o)] = __ldcs(src + o);
+        __syncthreads();
+        for (uint32_t i = threadIdx.x; i < total; i += kLayoutThreads) {
+            uint32_t r = i / jn, j = i - r * jn;
+            __stcs(out + (uint64_t)(rt * 32u + r) * row_chunks + ct0 * 4u + j,
+                   buf[smem_slot(band_tile_chunk(r, j))]);
+        }
+        __syncthreads();
+    }
+}
+
+// Identity copy, 4 x 16 bytes in flight per thread.
+__global__ void __launch_bounds__(256)
+copy_kernel(const uint4* __restrict__ src, uint4* __restrict__ dst, uint64_t n16) {
+    const uint64_t stride = (uint64_t)gridDim.x * blockDim.x;
+    uint64_t i = (uint64_t)blockIdx.x * blockDim.x + threadIdx.x;
+    for (; i + 3 * stride < n16; i += 4 * stride) {
+        uint4 a = __ldcs(src + i);
+        uint4 b = __ldcs(src + i + stride);
+        uint4 c = __ldcs(src + i + 2 * stride);
+        uint4 d = __ldcs(src + i + 3 * stride);
+        __stcs(dst + i, a);
+        __stcs(dst + i + stride, b);
+        __stcs(dst + i + 2 * stride, c);
+        __stcs(dst + i + 3 * stride, d);
+    }
+    for (; i < n16; i += stride) __stcs(dst + i, __ldcs(src + i));
+}
+
+int sm_count() {
+    static int n = 0;
+    if (n == 0) {
+        int dev = 0;
+        cudaGetDevice(&dev);
+        cudaDeviceGetAttribute(&n, cudaDevAttrMultiProcessorCount, dev);
+        if (n <= 0) n = 148;
+    }
+    return n;
+}
+
+}  // namespace
+}  // namespace foil
+
+extern "C" void foil_set_error(int status, const char* msg);
+
+static int check_launch(const char* what) {
+    cudaError_t e = cudaGetLastError();
+    if (e != cudaSuccess) {
+        char buf[256];
+        snprintf(buf, sizeof buf, "%s: CUDA launch failed: %s", what, cudaGetErrorString(e));
+        foil_set_error(FOIL_ERR_CUDA, buf);
+        return FOIL_ERR_CUDA;
+    }
+    foil_count_launch();
+    return FOIL_OK;
+}
+
+static bool aligned16(const void* p) { return ((uintptr_t)p & 15u) == 0; }
+
+extern "C" int foil_tilize_dev(const uint16_t* row_major, uint16_t* tiles,
+                               uint32_t rows, uint32_t cols, void* stream) {
+    if (rows % 32 || cols % 32) {
+        foil_set_error(FOIL_ERR_INVALID, "foil_tilize_dev: rows and cols must be multiples of 32");
+        return FOIL_ERR_INVALID;
+    }
+    if (rows == 0 || cols == 0) return FOIL_OK;
+    if (!row_major || !tiles || !aligned16(row_major) || !aligned16(tiles)) {
+        foil_set_error(FOIL_ERR_INVALID, "foil_tilize_dev: null or misaligned pointer");
+        return FOIL_ERR_INVALID;
+    }
+    uint64_t bands = (uint64_t)(rows / 32) * ((cols / 32 + 7) / 8);
+    uint64_t grid = bands < (uint64_t)foil::sm_count() * 8 ? bands : (uint64_t)foil::sm_count() * 8;
+    foil::tilize_kernel<<<(unsigned)grid, foil::kLayoutThreads, 0, (cudaStream_t)stream>>>(
+        (const uint4*)row_major, (uint4*)tiles, rows, cols);
+    return check_launch("foil_tilize_dev");
+}
+
+extern "C" int foil_untilize_dev(const uint16_t* tiles, uint16_t* row_major,
+                                 uint32_t rows, uint32_t cols, void* stream) {
+    if (rows % 32 || cols % 32) {
+        foil_set_error(FOIL_ERR_INVALID, "foil_untilize_dev: rows and cols must be multiples of 32");
+        return FOIL_ERR_INVALID;
+    }
+    if (rows == 0 || cols == 0) return FOIL_OK;
+    if (!row_major || !tiles || !aligned16(row_major) || !aligned16(tiles)) {
+        foil_set_error(FOIL_ERR_INVALID, "foil_untilize_dev: null or misaligned pointer");
+        return FOIL_ERR_INVALID;
+    }
+    uint64_t bands = (uint64_t)(rows / 32) * ((cols / 32 + 7) / 8);
+    uint64_t grid = bands < (uint64_t)foil::sm_count() * 8 ? bands : (uint64_t)foil::sm_count() * 8;
+    foil::untilize_kernel<<<(unsigned)grid, foil::kLayoutThreads, 0, (cudaStream_t)stream>>>(
+        (const uint4*)tiles, (uint4*)row_major, rows, cols);
+    return check_launch("foil_untilize_dev");
+}
+
+extern "C" int foil_tile_copy_dev(const void* src, void* dst, uint64_t bytes, void* stream) {
+    if (bytes % 16) {
+        foil_set_error(FOIL_ERR_INVALID, "foil_tile_copy_dev: bytes must be a multiple of 16");
+        return FOIL_ERR_INVALID;
+    }
+    if (bytes == 0) return FOIL_OK;
+    if (!src || !dst || !aligned16(src) || !aligned16(dst)) {
+        foil_set_error(FOIL_ERR_INVALID, "foil_tile_copy_dev: null or misaligned pointer");
+        return FOIL_ERR_INVALID;
+    }
+    uint64_t n16 = bytes / 16;
+    uint64_t want = (n16 + 255) / 256;
+    uint64_t cap = (uint64_t)foil::sm_count() * 8;
+    unsigned grid = (unsigned)(want < cap ? want : cap);
+    foil::copy_kernel<<<grid, 256, 0, (cudaStream_t)stream>>>((const uint4*)src, (uint4*)dst, n16);
+    return check_launch("foil_tile_copy_dev");
+}
