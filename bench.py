@@ -1,0 +1,432 @@
+"""Benchmark of the B200 tt-foil hot path: the tiled bf16 GEMM at 8192^3.
+
+One step = one C (8192 x 8192) = A (8192 x 8192) . B (8192 x 8192) product per
+GPU on 32x32-tile-layout bf16 operands with fp32 accumulation (the tt-foil
+matmul_dram program at Mt = Kt = Nt = 256), run by the sm_100a tcgen05 kernel
+of libfoil.  With N GPUs (torchrun, one process per GPU) every rank computes
+its own 8192-row shard of an (8192 N) x 8192 x 8192 product (weak scaling, no
+collective inside the step); the NCCL all-gather that reassembles the global
+tile-layout C is timed separately and reported under "allgather".
+
+value      TFLOP/s over all ranks, operands resident in HBM, CUDA events on the
+           launching stream, max over ranks.
+e2e        TFLOP/s through the tt-foil runtime API (write_buffer A and B from
+           pinned host memory, execute the matmul_dram program, read_buffer C)
+           every step, host timer around blocking calls, max over ranks.
+roofline   GEMM FLOPs per launch / mean launch time against the measured bf16
+           peak (MEASURED_PEAKS.json).
+cpu_baseline  the oracle (the reference golden's loop nest, oracle/golden.cpp)
+           on a bounded sample of output rows, all host threads, rank 0, N=1.
+
+--impl reference times the reference's CPU golden implementation of the same
+workload (the oracle port; see the cpu_baseline note) and prints its line.
+"""
+import argparse
+import json
+import os
+import statistics
+import subprocess
+import sys
+import tempfile
+import time
+
+REPO = os.path.dirname(os.path.abspath(__file__))
+PKG = os.path.join(REPO, "tt-foil_b200")
+for p in (REPO, PKG):
+    if p not in sys.path:
+        sys.path.insert(0, p)
+
+METRIC = "bf16 tile-GEMM TFLOP/s & % peak @8192³; conv TFLOP/s; eltwise HBM GB/s"
+M_PER_GPU = N_DIM = K_DIM = 8192
+FALLBACK_PEAKS = {"hbm_gbs": 6650.0, "bf16_tflops": 1590.0, "bf16_tflops_sustained": 1400.0}
+
+
+def parse():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=400)
+    ap.add_argument("--warmup", type=int, default=10)
+    ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
+    ap.add_argument("--e2e-steps", type=int, default=20)
+    ap.add_argument("--cpu-seconds", type=float, default=12.0)
+    ap.add_argument("--no-cpu-baseline", action="store_true")
+    return ap.parse_args()
+
+
+def host_threads():
+    try:
+        return len(os.sched_getaffinity(0))
+    except AttributeError:
+        return os.cpu_count() or 1
+
+
+def peaks():
+    path = os.path.join(REPO, "MEASURED_PEAKS.json")
+    if os.path.exists(path):
+        with open(path) as f:
+            d = json.load(f)
+        return d, "measured"
+    return FALLBACK_PEAKS, "fallback"
+
+
+# ------------------------------------------------------------ distributed ---
+class Dist:
+    def __init__(self, gpus):
+        self.world = int(os.environ.get("WORLD_SIZE", "1"))
+        self.rank = int(os.environ.get("RANK", "0"))
+        self.local = int(os.environ.get("LOCAL_RANK", "0"))
+        self.pg = None
+        if self.world > 1:
+            import datetime
+            import torch
+            import torch.distributed as dist
+            torch.cuda.set_device(self.local)
+            dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=120),
+                                    device_id=torch.device("cuda", self.local))
+            self.pg = dist
+
+    def barrier(self):
+        if self.pg:
+            self.pg.barrier()
+
+    def max(self, x):
+        if not self.pg:
+            return x
+        import torch
+        t = torch.tensor([x], dtype=torch.float64, device="cuda")
+        self.pg.all_reduce(t, op=self.pg.ReduceOp.MAX)
+        return float(t.item())
+
+    def close(self):
+        if self.pg:
+            self.pg.destroy_process_group()
+
+
+# ---------------------------------------------------------------- clocks ---
+class ClockSampler:
+    """nvidia-smi samples of SM clock and throttle reasons during a region."""
+    FIELDS = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
+              "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
+              "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+
+    def __init__(self, gpu_index):
+        self.idx = gpu_index
+        self.proc = None
+        self.path = None
+
+    def start(self):
+        fd, self.path = tempfile.mkstemp(prefix="clocks_", suffix=".csv")
+        os.close(fd)
+        try:
+            self.proc = subprocess.Popen(
+                ["nvidia-smi", f"--query-gpu={self.FIELDS}", "--format=csv,noheader,nounits",
+                 "-lms", "50", "-i", str(self.idx)],
+                stdout=open(self.path, "w"), stderr=subprocess.DEVNULL)
+        except OSError:
+            self.proc = None
+        time.sleep(0.15)
+
+    def stop(self):
+        if self.proc is None:
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["nvidia-smi unavailable"]}
+        time.sleep(0.1)
+        self.proc.terminate()
+        try:
+            self.proc.wait(timeout=5)
+        except subprocess.TimeoutExpired:
+            self.proc.kill()
+        rows = []
+        with open(self.path) as f:
+            for line in f:
+                p = [x.strip() for x in line.split(",")]
+                if len(p) >= 9:
+                    rows.append(p)
+        os.unlink(self.path)
+        sm = [float(r[1]) for r in rows if r[1].replace(".", "").isdigit()]
+        mx = [float(r[2]) for r in rows if r[2].replace(".", "").isdigit()]
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        reasons = sorted({names[i] for r in rows for i in range(4) if r[5 + i] == "Active"})
+        under_load = [s for s in sm if s > 600] or sm
+        return {"sm_mhz": statistics.median(under_load) if under_load else None,
+                "sm_max_mhz": max(mx) if mx else None, "reasons": reasons,
+                "samples": len(rows),
+                "power_w_max": max((float(r[3]) for r in rows if r[3].replace(".", "").isdigit()),
+                                   default=None)}
+
+
+# ----------------------------------------------------------- CPU baseline ---
+def cpu_gemm_baseline(seconds, threads):
+    """Oracle port of the reference golden (sequential fp32 K loop per output,
+    tests/test_matmul_mnk.cpp:62-76) on whole output rows of the 8192^3
+    workload, all host threads, until `seconds` have elapsed."""
+    import numpy as np
+    from oracle import oracle
+    K = N = 8192
+    rows = max(threads, 1)
+    a = oracle.rand_bf16((rows, K), 91)
+    b = oracle.rand_bf16((K, N), 92)
+    done_rows = 0
+    t0 = time.perf_counter()
+    while True:
+        oracle.matmul(a, b, rows=(0, rows), threads=threads)
+        done_rows += rows
+        el = time.perf_counter() - t0
+        if el >= seconds:
+            break
+    flops = 2.0 * done_rows * N * K
+    return {"value": flops / el / 1e12, "unit": "TFLOP/s", "cores": threads, "kind": "port",
+            "sample": f"{done_rows} output rows x 8192 cols (K=8192) of the 8192^3 product, "
+                      f"{el:.1f} s"}
+
+
+# ------------------------------------------------------------- reference ---
+def run_reference(args, dist):
+    if dist.rank != 0:
+        return
+    threads = host_threads()
+    from oracle import oracle
+    K = N = 8192
+    a = oracle.rand_bf16((threads, K), 91)
+    b = oracle.rand_bf16((K, N), 92)
+    # Size each step so warmup + steps finish in ~150 s.
+    t0 = time.perf_counter()
+    oracle.matmul(a[:1], b, rows=(0, 1), threads=1)
+    t_row = time.perf_counter() - t0
+    budget = 150.0 / max(1, args.steps + args.warmup)
+    rows = max(1, min(threads, int(budget / max(t_row, 1e-6) * threads)))
+    for _ in range(args.warmup):
+        oracle.matmul(a[:rows], b, rows=(0, rows), threads=min(threads, rows))
+    t0 = time.perf_counter()
+    for _ in range(args.steps):
+        oracle.matmul(a[:rows], b, rows=(0, rows), threads=min(threads, rows))
+    el = time.perf_counter() - t0
+    flops = 2.0 * rows * N * K * args.steps
+    v = flops / el / 1e12
+    line = {"impl": "reference", "metric": METRIC, "value": v, "unit": "TFLOP/s",
+            "n_gpus": args.gpus, "steps": args.steps, "warmup": args.warmup,
+            "ms_per_step": el / args.steps * 1e3, "higher_is_better": True, "scaling": "weak",
+            "vs_baseline": None, "dtype": "f32-acc bf16", "data": "synthetic seeded U(-1,1) bf16",
+            "config": {"workload": "tiled bf16 GEMM 8192x8192x8192 (CPU golden, row sample)",
+                       "M": 8192, "N": N, "K": K},
+            "cpu_baseline": {"value": v, "unit": "TFLOP/s", "cores": min(threads, rows),
+                             "kind": "port",
+                             "sample": f"{rows} output rows x 8192 cols per step (K=8192)"},
+            "e2e": {"value": v, "unit": "TFLOP/s", "h2d_bytes_per_step": 0,
+                    "d2h_bytes_per_step": 0}}
+    print(json.dumps(line), flush=True)
+
+
+# ------------------------------------------------------------------- ours ---
+def run_ours(args, dist):
+    import numpy as np
+    import torch
+    import ttfoil
+
+    torch.cuda.set_device(dist.local)
+    dev = torch.device("cuda", dist.local)
+    Mt, Kt, Nt = M_PER_GPU // 32, K_DIM // 32, N_DIM // 32
+    flops = 2.0 * M_PER_GPU * N_DIM * K_DIM
+
+    # Synthetic operands (seeded U(-1,1) bf16), tile layout; B identical on
+    # every rank, A is this rank's row shard.
+    g = torch.Generator(device=dev).manual_seed(1234 + dist.rank)
+    gb = torch.Generator(device=dev).manual_seed(99)
+    a_rm = (torch.rand(M_PER_GPU, K_DIM, device=dev, generator=g) * 2 - 1).to(torch.bfloat16)
+    b_rm = (torch.rand(K_DIM, N_DIM, device=dev, generator=gb) * 2 - 1).to(torch.bfloat16)
+    a = torch.empty(M_PER_GPU * K_DIM, dtype=torch.bfloat16, device=dev)
+    b = torch.empty(K_DIM * N_DIM, dtype=torch.bfloat16, device=dev)
+    c = torch.empty(M_PER_GPU * N_DIM, dtype=torch.bfloat16, device=dev)
+    ttfoil.tilize(a_rm, a, M_PER_GPU, K_DIM)
+    ttfoil.tilize(b_rm, b, K_DIM, N_DIM)
+    torch.cuda.synchronize()
+    del a_rm, b_rm
+
+    stream = torch.cuda.current_stream()
+
+    def step():
+        ttfoil.matmul_tiles(a, b, c, Mt, Kt, Nt, stream=stream)
+
+    for _ in range(max(3, args.warmup)):
+        step()
+    torch.cuda.synchronize()
+    assert ttfoil.device_error(stream) == 0
+
+    clocks = ClockSampler(dist.local)
+    clocks.start()
+    launches0 = ttfoil.launch_count()
+    dist.barrier()
+    torch.cuda.synchronize()
+    ev0 = torch.cuda.Event(enable_timing=True)
+    ev1 = torch.cuda.Event(enable_timing=True)
+    ev0.record(stream)
+    for _ in range(args.steps):
+        step()
+    ev1.record(stream)
+    torch.cuda.synchronize()
+    dist.barrier()
+    launches = ttfoil.launch_count() - launches0
+    clk = clocks.stop()
+    ms_local = ev0.elapsed_time(ev1)
+    ms = dist.max(ms_local)
+    assert ttfoil.device_error(stream) == 0
+    value = dist.world * flops * args.steps / (ms / 1e3) / 1e12
+
+    # Spot-check a few output rows of this rank against the oracle.
+    check = spot_check(ttfoil, a, b, c, Mt, Kt, Nt) if dist.rank == 0 else None
+
+    # Roofline of the dominant (only) kernel: FLOPs per launch / launch time.
+    pk, pk_kind = peaks()
+    per_launch_ms = ms_local / args.steps
+    achieved = flops / (per_launch_ms / 1e3) / 1e12
+    traffic = read_traffic()
+    roofline = {"bound": "tensor", "achieved": achieved, "peak": pk["bf16_tflops"],
+                "unit": "TFLOP/s", "frac": achieved / pk["bf16_tflops"],
+                "frac_of_sustained": achieved / pk.get("bf16_tflops_sustained", pk["bf16_tflops"]),
+                "peak_kind": f"{pk_kind} burst cuBLAS bf16",
+                "traffic": traffic,
+                "algorithmic_bytes": 2.0 * (M_PER_GPU * K_DIM + K_DIM * N_DIM + M_PER_GPU * N_DIM)}
+
+    # All-gather of the C shards (reassembly of the global tile-layout C).
+    allgather = None
+    if dist.world > 1:
+        allgather = time_allgather(dist, c, ms / args.steps, flops)
+
+    e2e = run_e2e(args, dist, flops)
+
+    cpu = None
+    if dist.rank == 0 and dist.world == 1 and not args.no_cpu_baseline:
+        cpu = cpu_gemm_baseline(args.cpu_seconds, host_threads())
+
+    if dist.rank == 0:
+        line = {"metric": METRIC, "value": value, "unit": "TFLOP/s", "n_gpus": dist.world,
+                "steps": args.steps, "warmup": args.warmup, "ms_per_step": ms / args.steps,
+                "higher_is_better": True, "scaling": "weak", "vs_baseline": None,
+                "dtype": "bf16", "data": "synthetic seeded U(-1,1) bf16, 32x32 tile layout",
+                "config": {"workload": "tiled bf16 GEMM 8192x8192x8192 per GPU "
+                                       "(tt-foil 32x32 tile / 16x16 face layout, fp32 accumulate)",
+                           "M_per_gpu": M_PER_GPU, "N": N_DIM, "K": K_DIM,
+                           "global_M": M_PER_GPU * dist.world,
+                           "parallelism": f"M-shard x{dist.world}",
+                           "l2": "operands 384 MiB per GPU > 126 MB L2, no flush"},
+                "roofline": roofline, "cpu_baseline": cpu, "e2e": e2e, "clocks": clk,
+                "gpu_launches": launches, "parity_spot_check": check}
+        if allgather:
+            line["allgather"] = allgather
+        print(json.dumps(line), flush=True)
+
+
+def bits(t):
+    """bf16 CUDA tensor -> numpy uint16 bit patterns."""
+    import numpy as np
+    import torch
+    return t.view(torch.int16).cpu().numpy().view(np.uint16)
+
+
+def spot_check(ttfoil, a, b, c, Mt, Kt, Nt):
+    """Three output rows of the timed product against the oracle."""
+    from oracle import oracle
+    rows = [0, 4097, 8191]
+    K, N = Kt * 32, Nt * 32
+    b_h = oracle.untilize(bits(b), K, N)
+    a_h, c_h = bits(a), bits(c)
+    worst = 0.0
+    for r in rows:
+        mt, r0 = divmod(r, 32)
+        a_row = oracle.untilize(a_h[mt * Kt * 1024:(mt + 1) * Kt * 1024], 32, K)[r0:r0 + 1]
+        c_row = oracle.untilize(c_h[mt * Nt * 1024:(mt + 1) * Nt * 1024], 32, N)[r0:r0 + 1]
+        exp = oracle.matmul(a_row, b_h, threads=8)
+        worst = max(worst, oracle.normalized_error(c_row, exp, K, 1.0, 1.0))
+    return {"rows": rows, "normalized_error": worst, "tolerance": 1e-2, "ok": worst <= 1e-2}
+
+
+def read_traffic():
+    """DRAM bytes per GEMM launch from the committed ncu summary, if any."""
+    path = os.path.join(REPO, "profiles", "gemm_tc_8192_traffic.json")
+    if os.path.exists(path):
+        with open(path) as f:
+            return json.load(f).get("dram_bytes_per_launch")
+    return None
+
+
+def time_allgather(dist, c, compute_ms, flops):
+    import torch
+    out = torch.empty(c.numel() * dist.world, dtype=c.dtype, device=c.device)
+    for _ in range(3):
+        dist.pg.all_gather_into_tensor(out, c)
+    torch.cuda.synchronize()
+    dist.barrier()
+    e0 = torch.cuda.Event(enable_timing=True)
+    e1 = torch.cuda.Event(enable_timing=True)
+    it = 10
+    e0.record()
+    for _ in range(it):
+        dist.pg.all_gather_into_tensor(out, c)
+    e1.record()
+    torch.cuda.synchronize()
+    ms = dist.max(e0.elapsed_time(e1)) / it
+    nbytes = c.numel() * c.element_size()
+    busbw = nbytes * (dist.world - 1) / (ms / 1e3) / 1e9
+    return {"ms": ms, "bytes_per_rank": nbytes, "busbw_GBps": busbw,
+            "value_with_gather_TFLOPs": dist.world * flops / ((compute_ms + ms) / 1e3) / 1e12,
+            "note": "ncclAllGather of the C shards after the step, timed separately"}
+
+
+def run_e2e(args, dist, flops):
+    """Same GEMM through the tt-foil runtime API with host buffers."""
+    import numpy as np
+    import torch
+    import ttfoil
+
+    Mt, Kt, Nt = M_PER_GPU // 32, K_DIM // 32, N_DIM // 32
+    a_bytes, b_bytes, c_bytes = Mt * Kt * 2048, Kt * Nt * 2048, Mt * Nt * 2048
+    pin = lambda n: torch.empty(n // 2, dtype=torch.int16, pin_memory=True)
+    a_h, b_h, c_h = pin(a_bytes), pin(b_bytes), pin(c_bytes)
+    g = torch.Generator().manual_seed(5 + dist.rank)
+    a_h.copy_(torch.randint(-16000, 16000, (a_bytes // 2,), dtype=torch.int16, generator=g) & 0x3fff)
+    b_h.copy_(torch.randint(-16000, 16000, (b_bytes // 2,), dtype=torch.int16, generator=g) & 0x3fff)
+    with ttfoil.Device(dist.local) as d:
+        ba = d.allocate(ttfoil.LOC_DRAM, a_bytes)
+        bb = d.allocate(ttfoil.LOC_DRAM, b_bytes)
+        bc = d.allocate(ttfoil.LOC_DRAM, c_bytes)
+        k = d.load_program("matmul_dram")
+        an, bn, cn = (d.noc_dram_addr(x.device_addr) for x in (ba, bb, bc))
+        d.set_runtime_args(k, ttfoil.BRISC, [ttfoil.lo(an), ttfoil.hi(an), ttfoil.lo(bn),
+                                             ttfoil.hi(bn), Mt, Kt, Nt])
+        d.set_runtime_args(k, ttfoil.NCRISC, [ttfoil.lo(cn), ttfoil.hi(cn), Mt * Nt])
+
+        def step():
+            d.write(ba, a_h.data_ptr(), a_bytes)
+            d.write(bb, b_h.data_ptr(), b_bytes)
+            d.execute(k)
+            d.read(bc, c_h.data_ptr(), c_bytes)
+
+        for _ in range(3):
+            step()
+        dist.barrier()
+        t0 = time.perf_counter()
+        for _ in range(args.e2e_steps):
+            step()
+        el = time.perf_counter() - t0
+        dist.barrier()
+    el = dist.max(el)
+    return {"value": dist.world * flops * args.e2e_steps / el / 1e12, "unit": "TFLOP/s",
+            "h2d_bytes_per_step": a_bytes + b_bytes, "d2h_bytes_per_step": c_bytes,
+            "steps": args.e2e_steps, "ms_per_step": el / args.e2e_steps * 1e3,
+            "path": "ttfoil.Device write_buffer x2 (pinned) + execute(matmul_dram) + read_buffer",
+            "timer": "host perf_counter around blocking API calls"}
+
+
+def main():
+    args = parse()
+    dist = Dist(args.gpus)
+    try:
+        if args.impl == "reference":
+            run_reference(args, dist)
+        else:
+            run_ours(args, dist)
+    finally:
+        dist.close()
+
+
+if __name__ == "__main__":
+    main()
