@@ -13,36 +13,40 @@
 // How the tile layout feeds tcgen05 without a relayout pass
 // ---------------------------------------------------------
 // A face row is 16 bf16 = 32 bytes, which is exactly one SWIZZLE_32B atom
-// row and one UMMA K-step (K = 16).  Two families of 5-D TMA tensor maps
-// describe the tile stream so that each TMA box lands in shared memory as a
-// canonical UMMA operand, with TMA applying the 32-byte swizzle on the way:
+// row and one UMMA K-step (K = 16).  Both operands are staged so that every
+// K-step is a canonical UMMA operand:
 //
-//  * A (rows = m, contiguous = k: K-major).  One map per face column fc:
-//      dims (c0:16 @2B, r0:16 @32B, fr:2 @1024B, kt:Kt @2048B, mt:Mt @Kt*2KiB)
-//      base A + fc*512B, box (16,16,2,1,4)  ->  128 rows x 32 B, 8-row groups
-//      256 B apart: K-major SW32 with SBO = 256 B.
-//  * B (rows = k, contiguous = n: MN-major).  One map per face row fr:
-//      dims (c0:16 @2B, r0:16 @32B, fc:2 @512B, nt:Nt @2KiB, kt:Kt @Nt*2KiB)
-//      base B + fr*1024B, box (16,16,2,8,2) -> per kt: 16 atoms of 16 n x 16 k
-//      (512 B each): MN-major SW32 with LBO = 512 B (next 16 n), SBO = 256 B
-//      (next 8 k).
+//  * A (rows = m, contiguous = k: K-major SW32).  K-step (kt, fc) of a stage
+//    holds face column fc of the 4 A tiles (mt0..mt0+3, kt): 128 rows x 32 B,
+//    8-row groups 256 B apart (SBO = 256 B).
+//  * B (rows = k, contiguous = n: MN-major SW32).  K-step (kt, fr) holds face
+//    row fr of the 8 B tiles (kt, nt0..nt0+7): 16 atoms of 16 n x 16 k
+//    (512 B each, LBO = 512 B between atoms along n, SBO = 256 B along k).
 //  A K-step (kt, f) pairs A face column f with B face row f, i.e. the K
 //  range kt*32 + f*16 + [0,16).
 //
+// In both cases a whole 16x16 face (512 contiguous bytes of the tile stream)
+// lands as one 512-byte block of shared memory, with the 32-byte swizzle
+// (16-byte halves of rows 4..7 of every 8-row group swapped) applied in the
+// destination address.  Producer warps therefore copy one face per warp
+// instruction with 16-byte cp.async: each warp access is 512 contiguous
+// global bytes, i.e. four full 128-byte L2 requests.  (A TMA tensor copy of
+// the same operand has a 32-byte inner box — one face row — and costs one L2
+// request per 32 bytes, which made L2 tag lookups the limiter.)
+//
 // Kernel organisation (persistent, warp-specialised, 1 CTA per SM)
 // ------------------------------------------------------------------
-//  warp 0      TMA producer  (4-stage smem ring, 48 KiB per stage)
-//  warp 1      MMA issuer    (tcgen05.mma 128x256x16, commits free stages)
-//  warps 2..5  epilogue      (tcgen05.ld -> bf16 (+bias, relu) -> global)
+//  warps 0..3  producers     (4-stage smem ring, 48 KiB per stage, 96 faces)
+//  warp 4      MMA issuer    (tcgen05.mma 128x256x16, commits free stages)
+//              and TMEM owner
+//  warps 5..8  epilogue      (tcgen05.ld -> bf16 (+bias, relu) -> global)
 //  TMEM holds two 128x256 fp32 accumulators (512 columns) so the epilogue of
 //  tile i overlaps the main loop of tile i+1.  Output tiles of 128x256 are
 //  visited in bands of 8 column-blocks for L2 reuse.
 //
 // Every mbarrier wait is bounded (2 s of wall time); on expiry the kernel
 // records kErrWaitTimeout in the error word, all roles leave their loops,
-// in-flight copies and MMAs are drained with bounded waits and TMEM is freed.
-#include <cuda.h>
-#include <cudaTypedefs.h>
+// in-flight copies and MMAs are drained and TMEM is freed.
 #include <mutex>
 #include <cstdio>
 #include <cstring>
@@ -119,14 +123,19 @@ __device__ __forceinline__ void mbar_drain(uint64_t* bar, uint32_t parity, uint6
     }
 }
 
-__device__ __forceinline__ void tma_load_5d(const CUtensorMap* map, uint64_t* bar, void* dst,
-                                            int c0, int c1, int c2, int c3, int c4) {
-    asm volatile(
-        "cp.async.bulk.tensor.5d.shared::cluster.global.mbarrier::complete_tx::bytes"
-        " [%0], [%1, {%3, %4, %5, %6, %7}], [%2];" ::"r"(smem_u32(dst)),
-        "l"(reinterpret_cast<uint64_t>(map)), "r"(smem_u32(bar)), "r"(c0), "r"(c1), "r"(c2),
-        "r"(c3), "r"(c4)
-        : "memory");
+// 16-byte global->shared copy; src_bytes = 0 writes zeros (out-of-range
+// tiles).  .cg: cached in L2 only.
+__device__ __forceinline__ void cp_async16(uint32_t dst, const void* src, uint32_t src_bytes) {
+    asm volatile("cp.async.cg.shared.global [%0], [%1], 16, %2;" ::"r"(dst), "l"(src),
+                 "r"(src_bytes)
+                 : "memory");
+}
+
+// Arrive on `bar` once every cp.async issued so far by this thread is done
+// (counts toward the barrier's expected arrivals).
+__device__ __forceinline__ void cp_async_arrive(uint64_t* bar) {
+    asm volatile("cp.async.mbarrier.arrive.noinc.shared::cta.b64 [%0];" ::"r"(smem_u32(bar))
+                 : "memory");
 }
 
 __device__ __forceinline__ void tc_fence_before() {
@@ -191,12 +200,19 @@ constexpr int kStages = 4;
 constexpr int kABytes = kBM * kBKT * 32 * 2;  // 16 KiB
 constexpr int kBBytes = kBN * kBKT * 32 * 2;  // 32 KiB
 constexpr int kStageBytes = kABytes + kBBytes;
-constexpr int kThreads = 192;
+constexpr int kProdWarps = 4;
+constexpr int kMmaWarp = 4;
+constexpr int kEpiWarp0 = 5;
+constexpr int kThreads = 9 * 32;
+static_assert(kThreads / 32 == kEpiWarp0 + 4, "four epilogue warps follow the MMA warp");
+constexpr int kFacesPerStage = 96;  // 32 A faces + 64 B faces
 constexpr int kTmemCols = 512;
 constexpr int kBandN = 8;           // column-blocks per raster band
 constexpr int kSmemBytes = kStages * kStageBytes + 1024 /*align*/ + 256 /*barriers*/;
 
 struct Params {
+    const uint16_t* a;
+    const uint16_t* b;
     uint16_t* c;
     const uint16_t* bias;
     uint32_t Mt, Kt, Nt;
@@ -226,9 +242,7 @@ __device__ __forceinline__ uint32_t epi1(uint32_t acc_bits, uint32_t bias_bits, 
 }
 
 __global__ void __launch_bounds__(kThreads, 1)
-gemm_tiles_kernel(const __grid_constant__ CUtensorMap tmA0, const __grid_constant__ CUtensorMap tmA1,
-                  const __grid_constant__ CUtensorMap tmB0, const __grid_constant__ CUtensorMap tmB1,
-                  const Params p) {
+gemm_tiles_kernel(const Params p) {
     extern __shared__ uint8_t smem_raw[];
     uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) &
                                                ~uintptr_t(1023));
@@ -244,7 +258,7 @@ gemm_tiles_kernel(const __grid_constant__ CUtensorMap tmA0, const __grid_constan
 
     if (threadIdx.x == 0) {
         for (int s = 0; s < kStages; ++s) {
-            mbar_init(&full[s], 1);
+            mbar_init(&full[s], kProdWarps * 32);
             mbar_init(&empty[s], 1);
         }
         for (int b = 0; b < 2; ++b) {
@@ -256,18 +270,12 @@ gemm_tiles_kernel(const __grid_constant__ CUtensorMap tmA0, const __grid_constan
         asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
         asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
     }
-    if (warp == 0) {
+    if (warp == kMmaWarp) {
         asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(
                          smem_u32(tmem_slot)),
                      "r"(kTmemCols)
                      : "memory");
         asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;" ::: "memory");
-    }
-    if (warp == 1 && lane == 0) {
-        asm volatile("prefetch.tensormap [%0];" ::"l"(reinterpret_cast<uint64_t>(&tmA0)) : "memory");
-        asm volatile("prefetch.tensormap [%0];" ::"l"(reinterpret_cast<uint64_t>(&tmA1)) : "memory");
-        asm volatile("prefetch.tensormap [%0];" ::"l"(reinterpret_cast<uint64_t>(&tmB0)) : "memory");
-        asm volatile("prefetch.tensormap [%0];" ::"l"(reinterpret_cast<uint64_t>(&tmB1)) : "memory");
     }
     tc_fence_before();
     __syncthreads();
@@ -277,48 +285,63 @@ gemm_tiles_kernel(const __grid_constant__ CUtensorMap tmA0, const __grid_constan
     const uint32_t num_tiles = p.m_blocks * p.n_blocks;
     const uint32_t num_kb = (p.Kt + kBKT - 1) / kBKT;
 
-    if (warp == 0) {
-        if (lane == 0) {
-            // ------------------------------------------------ TMA producer
-            uint32_t stage = 0, phase = 0;
-            uint32_t issued = 0;
+    if (warp < kProdWarps) {
+        // ---------------------------------------------------- producers
+        // Lane l copies bytes [16 l, 16 l + 16) of each face: face row
+        // r0 = l / 2, half h = l % 2, stored at r0 * 32 + 16 * (h ^ bit 2 of r0).
+        const uint32_t src_lane = lane * 16u;
+        const uint32_t dst_lane = (lane >> 1) * 32u + ((((lane & 1u) ^ ((lane >> 3) & 1u))) << 4);
+        const char* a_g = reinterpret_cast<const char*>(p.a);
+        const char* b_g = reinterpret_cast<const char*>(p.b);
+        uint32_t stage = 0, phase = 0;
+        for (uint32_t tile = blockIdx.x; tile < num_tiles; tile += gridDim.x) {
+            uint32_t mb, nb;
+            tile_coords(tile, p.m_blocks, p.n_blocks, mb, nb);
             bool ok = true;
-            for (uint32_t tile = blockIdx.x; ok && tile < num_tiles; tile += gridDim.x) {
-                uint32_t mb, nb;
-                tile_coords(tile, p.m_blocks, p.n_blocks, mb, nb);
-                for (uint32_t kb = 0; kb < num_kb; ++kb) {
-                    if (!mbar_wait(&empty[stage], phase ^ 1u, abort_flag, p.err)) {
-                        ok = false;
-                        break;
-                    }
-                    uint8_t* a_s = smem + stage * kStageBytes;
-                    uint8_t* b_s = a_s + kABytes;
-                    mbar_expect_tx(&full[stage], kStageBytes);
-                    const int kt0 = (int)(kb * kBKT);
+            for (uint32_t kb = 0; kb < num_kb; ++kb) {
+                bool w = true;
+                if (lane == 0) w = mbar_wait(&empty[stage], phase ^ 1u, abort_flag, p.err);
+                if (__shfl_sync(0xffffffffu, w ? 1 : 0, 0) == 0) {
+                    ok = false;
+                    break;
+                }
+                const uint32_t a_s = smem_u32(smem + stage * kStageBytes);
+                const uint32_t b_s = a_s + kABytes;
+                const uint32_t kt0 = kb * kBKT;
 #pragma unroll
-                    for (int ktl = 0; ktl < kBKT; ++ktl) {
-                        tma_load_5d(&tmA0, &full[stage], a_s + (ktl * 2 + 0) * 4096, 0, 0, 0,
-                                    kt0 + ktl, (int)(mb * 4));
-                        tma_load_5d(&tmA1, &full[stage], a_s + (ktl * 2 + 1) * 4096, 0, 0, 0,
-                                    kt0 + ktl, (int)(mb * 4));
+                for (int i = 0; i < kFacesPerStage / kProdWarps; ++i) {
+                    const uint32_t f = warp + kProdWarps * i;
+                    const char* src;
+                    uint32_t dst;
+                    bool valid;
+                    if (i < 32 / kProdWarps) {  // A face: (mt_l, ktl, fr, fc)
+                        const uint32_t mt_l = f >> 3, ktl = (f >> 2) & 1u, fr = (f >> 1) & 1u,
+                                       fc = f & 1u;
+                        const uint32_t mt = mb * 4u + mt_l, kt = kt0 + ktl;
+                        valid = mt < p.Mt && kt < p.Kt;
+                        src = a_g + (((uint64_t)mt * p.Kt + kt) * 1024u + (fr * 2u + fc) * 256u) * 2u;
+                        dst = a_s + (ktl * 2u + fc) * 4096u + (mt_l * 32u + fr * 16u) * 32u;
+                    } else {  // B face: (ktl, nt_l, fr, fc)
+                        const uint32_t g = f - 32u;
+                        const uint32_t ktl = g >> 5, nt_l = (g >> 2) & 7u, fr = (g >> 1) & 1u,
+                                       fc = g & 1u;
+                        const uint32_t kt = kt0 + ktl, nt = nb * 8u + nt_l;
+                        valid = kt < p.Kt && nt < p.Nt;
+                        src = b_g + (((uint64_t)kt * p.Nt + nt) * 1024u + (fr * 2u + fc) * 256u) * 2u;
+                        dst = b_s + fr * 16384u + ktl * 8192u + (nt_l * 2u + fc) * 512u;
                     }
-                    tma_load_5d(&tmB0, &full[stage], b_s, 0, 0, 0, (int)(nb * 8), kt0);
-                    tma_load_5d(&tmB1, &full[stage], b_s + 16384, 0, 0, 0, (int)(nb * 8), kt0);
-                    ++issued;
-                    if (++stage == kStages) {
-                        stage = 0;
-                        phase ^= 1u;
-                    }
+                    cp_async16(dst + dst_lane, valid ? src + src_lane : a_g, valid ? 16u : 0u);
+                }
+                cp_async_arrive(&full[stage]);
+                if (++stage == kStages) {
+                    stage = 0;
+                    phase ^= 1u;
                 }
             }
-            // Drain: wait (bounded) for the last fill of every stage.
-            uint32_t n_last = issued < (uint32_t)kStages ? issued : (uint32_t)kStages;
-            for (uint32_t i = 0; i < n_last; ++i) {
-                uint32_t fill = issued - 1 - i;
-                mbar_drain(&full[fill % kStages], (fill / kStages) & 1u, 100000000ull);
-            }
+            if (!ok) break;
         }
-    } else if (warp == 1) {
+        asm volatile("cp.async.wait_all;" ::: "memory");
+    } else if (warp == kMmaWarp) {
         if (lane == 0) {
             // ------------------------------------------------ MMA issuer
             constexpr uint32_t idesc = make_idesc(kBM, kBN);
@@ -335,6 +358,9 @@ gemm_tiles_kernel(const __grid_constant__ CUtensorMap tmA0, const __grid_constan
                         ok = false;
                         break;
                     }
+                    // The stage was written by cp.async (generic proxy); the MMA
+                    // reads it through the async proxy.
+                    asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
                     tc_fence_after();
                     const uint32_t a_addr = smem_u32(smem + stage * kStageBytes);
                     const uint32_t b_addr = a_addr + kABytes;
@@ -434,7 +460,7 @@ gemm_tiles_kernel(const __grid_constant__ CUtensorMap tmA0, const __grid_constan
 
     tc_fence_before();
     __syncthreads();
-    if (warp == 0) {
+    if (warp == kMmaWarp) {
         __syncwarp();
         tc_fence_after();
         asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem_base),
@@ -444,54 +470,9 @@ gemm_tiles_kernel(const __grid_constant__ CUtensorMap tmA0, const __grid_constan
 }
 
 // ------------------------------------------------------------------ host ---
-static PFN_cuTensorMapEncodeTiled_v12000 encode_fn() {
-    static PFN_cuTensorMapEncodeTiled_v12000 fn = nullptr;
-    static std::once_flag once;
-    std::call_once(once, [] {
-        cudaDriverEntryPointQueryResult q;
-        void* f = nullptr;
-        if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &f, cudaEnableDefault, &q) ==
-                cudaSuccess &&
-            q == cudaDriverEntryPointSuccess)
-            fn = reinterpret_cast<PFN_cuTensorMapEncodeTiled_v12000>(f);
-    });
-    return fn;
-}
-
-static bool make_map(CUtensorMap* m, const void* base, const cuuint64_t dims[5],
-                     const cuuint64_t strides[4], const cuuint32_t box[5]) {
-    auto fn = encode_fn();
-    if (!fn) return false;
-    const cuuint32_t estr[5] = {1, 1, 1, 1, 1};
-    CUresult r = fn(m, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 5, const_cast<void*>(base), dims, strides,
-                    box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_32B,
-                    CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
-    return r == CUDA_SUCCESS;
-}
-
-// Tensor maps of the A and B tile streams (see the file comment).
-bool make_operand_maps(const uint16_t* a, const uint16_t* b, uint32_t Mt, uint32_t Kt,
-                       uint32_t Nt, CUtensorMap maps[4]) {
-    const cuuint64_t a_dims[5] = {16, 16, 2, Kt, Mt};
-    const cuuint64_t a_str[4] = {32, 1024, 2048, (cuuint64_t)Kt * 2048};
-    const cuuint32_t a_box[5] = {16, 16, 2, 1, 4};
-    const cuuint64_t b_dims[5] = {16, 16, 2, Nt, Kt};
-    const cuuint64_t b_str[4] = {32, 512, 2048, (cuuint64_t)Nt * 2048};
-    const cuuint32_t b_box[5] = {16, 16, 2, 8, (cuuint32_t)kBKT};
-    return make_map(&maps[0], a, a_dims, a_str, a_box) &&
-           make_map(&maps[1], a + 256, a_dims, a_str, a_box) &&
-           make_map(&maps[2], b, b_dims, b_str, b_box) &&
-           make_map(&maps[3], b + 512, b_dims, b_str, b_box);
-}
-
 int launch(const uint16_t* a, const uint16_t* b, uint16_t* c, uint32_t Mt, uint32_t Kt,
            uint32_t Nt, const uint16_t* bias, int relu, uint32_t* err, cudaStream_t stream,
            int max_ctas) {
-    CUtensorMap maps[4];
-    if (!make_operand_maps(a, b, Mt, Kt, Nt, maps)) {
-        foil_set_error(FOIL_ERR_CUDA, "foil_matmul_tiles: cuTensorMapEncodeTiled failed");
-        return FOIL_ERR_CUDA;
-    }
     static std::once_flag attr_once;
     static cudaError_t attr_err = cudaSuccess;
     std::call_once(attr_once, [] {
@@ -503,6 +484,8 @@ int launch(const uint16_t* a, const uint16_t* b, uint16_t* c, uint32_t Mt, uint3
         return FOIL_ERR_CUDA;
     }
     Params p;
+    p.a = a;
+    p.b = b;
     p.c = c;
     p.bias = bias;
     p.Mt = Mt;
@@ -514,7 +497,7 @@ int launch(const uint16_t* a, const uint16_t* b, uint16_t* c, uint32_t Mt, uint3
     p.err = err;
     const uint32_t tiles = p.m_blocks * p.n_blocks;
     const uint32_t grid = tiles < (uint32_t)max_ctas ? tiles : (uint32_t)max_ctas;
-    gemm_tiles_kernel<<<grid, kThreads, kSmemBytes, stream>>>(maps[0], maps[1], maps[2], maps[3], p);
+    gemm_tiles_kernel<<<grid, kThreads, kSmemBytes, stream>>>(p);
     cudaError_t e = cudaGetLastError();
     if (e != cudaSuccess) {
         char buf[256];
