@@ -53,144 +53,13 @@
 
 #include "common.cuh"
 #include "gemm_tc.cuh"
+#include "gemm_ptx.cuh"
 #include "../../../include/foil_c.h"
 
 extern "C" void foil_set_error(int status, const char* msg);
 
 namespace foil {
 namespace gemm {
-
-// ---------------------------------------------------------------- PTX ---
-__device__ __forceinline__ uint32_t smem_u32(const void* p) {
-    return static_cast<uint32_t>(__cvta_generic_to_shared(p));
-}
-
-__device__ __forceinline__ void mbar_init(uint64_t* bar, uint32_t count) {
-    asm volatile("mbarrier.init.shared::cta.b64 [%0], %1;" ::"r"(smem_u32(bar)), "r"(count));
-}
-
-__device__ __forceinline__ void mbar_expect_tx(uint64_t* bar, uint32_t bytes) {
-    asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;" ::"r"(smem_u32(bar)),
-                 "r"(bytes)
-                 : "memory");
-}
-
-__device__ __forceinline__ void mbar_arrive(uint64_t* bar) {
-    asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];" ::"r"(smem_u32(bar)) : "memory");
-}
-
-__device__ __forceinline__ bool mbar_try_wait(uint64_t* bar, uint32_t parity) {
-    uint32_t done;
-    asm volatile(
-        "{\n\t.reg .pred p;\n\t"
-        "mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2;\n\t"
-        "selp.b32 %0, 1, 0, p;\n\t}"
-        : "=r"(done)
-        : "r"(smem_u32(bar)), "r"(parity)
-        : "memory");
-    return done != 0;
-}
-
-constexpr uint64_t kWaitLimitNs = 2000000000ull;  // 2 s per wait
-
-// Wait for completion of phase `parity`.  Returns false if the CTA is
-// aborting or this wait exceeded its wall-time limit (then it raises the
-// abort flag and records the error).
-__device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity,
-                                          volatile uint32_t* abort_flag, uint32_t* err) {
-#pragma unroll 1
-    for (int i = 0; i < 32; ++i)
-        if (mbar_try_wait(bar, parity)) return true;
-    const uint64_t t0 = global_ns();
-#pragma unroll 1
-    while (true) {
-        if (mbar_try_wait(bar, parity)) return true;
-        if (*abort_flag) return false;
-        if (global_ns() - t0 > kWaitLimitNs) {
-            *abort_flag = 1u;
-            if (err) atomicOr(err, kErrWaitTimeout);
-            return false;
-        }
-    }
-}
-
-// Bounded drain wait used on the way out (ignores the abort flag).
-__device__ __forceinline__ void mbar_drain(uint64_t* bar, uint32_t parity, uint64_t limit_ns) {
-    const uint64_t t0 = global_ns();
-#pragma unroll 1
-    while (!mbar_try_wait(bar, parity)) {
-        if (global_ns() - t0 > limit_ns) return;
-    }
-}
-
-// 16-byte global->shared copy; src_bytes = 0 writes zeros (out-of-range
-// tiles).  .cg: cached in L2 only.
-__device__ __forceinline__ void cp_async16(uint32_t dst, const void* src, uint32_t src_bytes) {
-    asm volatile("cp.async.cg.shared.global [%0], [%1], 16, %2;" ::"r"(dst), "l"(src),
-                 "r"(src_bytes)
-                 : "memory");
-}
-
-// Arrive on `bar` once every cp.async issued so far by this thread is done
-// (counts toward the barrier's expected arrivals).
-__device__ __forceinline__ void cp_async_arrive(uint64_t* bar) {
-    asm volatile("cp.async.mbarrier.arrive.noinc.shared::cta.b64 [%0];" ::"r"(smem_u32(bar))
-                 : "memory");
-}
-
-__device__ __forceinline__ void tc_fence_before() {
-    asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory");
-}
-__device__ __forceinline__ void tc_fence_after() {
-    asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
-}
-
-__device__ __forceinline__ void tc_mma(uint32_t d_tmem, uint64_t a_desc, uint64_t b_desc,
-                                       uint32_t idesc, uint32_t accumulate) {
-    asm volatile(
-        "{\n\t.reg .pred p;\n\t"
-        "setp.ne.b32 p, %4, 0;\n\t"
-        "tcgen05.mma.cta_group::1.kind::f16 [%0], %1, %2, %3, p;\n\t}" ::"r"(d_tmem),
-        "l"(a_desc), "l"(b_desc), "r"(idesc), "r"(accumulate)
-        : "memory");
-}
-
-__device__ __forceinline__ void tc_commit(uint64_t* bar) {
-    asm volatile(
-        "tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::"r"(
-            smem_u32(bar))
-        : "memory");
-}
-
-__device__ __forceinline__ void tmem_ld16(uint32_t taddr, uint32_t (&v)[16]) {
-    asm volatile(
-        "tcgen05.ld.sync.aligned.32x32b.x16.b32 "
-        "{%0,%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15}, [%16];"
-        : "=r"(v[0]), "=r"(v[1]), "=r"(v[2]), "=r"(v[3]), "=r"(v[4]), "=r"(v[5]), "=r"(v[6]),
-          "=r"(v[7]), "=r"(v[8]), "=r"(v[9]), "=r"(v[10]), "=r"(v[11]), "=r"(v[12]),
-          "=r"(v[13]), "=r"(v[14]), "=r"(v[15])
-        : "r"(taddr));
-}
-
-__device__ __forceinline__ void tmem_ld_wait() {
-    asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
-}
-
-// Shared-memory matrix descriptor (tcgen05 format): start >> 4 in [0,14),
-// LBO >> 4 in [16,30), SBO >> 4 in [32,46), fixed version bit 46, layout type
-// in [61,64) (6 = SWIZZLE_32B).
-__host__ __device__ constexpr uint64_t smem_desc_base(uint32_t lbo, uint32_t sbo) {
-    return ((uint64_t)((lbo >> 4) & 0x3fffu) << 16) | ((uint64_t)((sbo >> 4) & 0x3fffu) << 32) |
-           (1ull << 46) | (6ull << 61);
-}
-
-// Instruction descriptor for kind::f16: f32 accumulate (bits 4-5 = 1), bf16
-// A and B (bits 7-9, 10-12 = 1), A K-major (bit 15 = 0), B MN-major (bit 16
-// = 1), N >> 3 at bit 17, M >> 4 at bit 24.
-__host__ __device__ constexpr uint32_t make_idesc(uint32_t m, uint32_t n) {
-    return (1u << 4) | (1u << 7) | (1u << 10) | (0u << 15) | (1u << 16) | ((n >> 3) << 17) |
-           ((m >> 4) << 24);
-}
 
 // --------------------------------------------------------------- kernel ---
 constexpr int kBM = 128;           // rows per CTA tile (4 tile-rows)
@@ -239,6 +108,57 @@ __device__ __forceinline__ uint32_t epi1(uint32_t acc_bits, uint32_t bias_bits, 
     if (has_bias) o = f32_to_bf16_bits(host_add_f32(bf16_bits_to_f32(o), bf16_bits_to_f32(bias_bits)));
     if (relu && bf16_bits_to_f32(o) < 0.0f) o = 0u;
     return o;
+}
+
+// Epilogue of one warp: the 32 accumulator rows of TMEM lane quadrant `t_row`
+// (tile row mt) x 256 columns (tile columns nt0 .. nt0+7) -> bf16 (+bias,
+// relu) -> the tile stream.  Lane = row inside the tile: face row fr = lane/16,
+// row r0 = lane%16; each lane writes one 32-byte face row per face.
+__device__ __forceinline__ void store_tile_row(const Params& p, uint32_t t_row, uint32_t mt,
+                                               uint32_t nt0, uint32_t lane) {
+    const uint32_t fr = lane >> 4, r0 = lane & 15u;
+    const bool has_bias = p.bias != nullptr;
+    const bool relu = p.relu != 0;
+#pragma unroll 1
+    for (uint32_t nt_l = 0; nt_l < 8; ++nt_l) {
+        uint32_t v0[16], v1[16];
+        tmem_ld16(t_row + nt_l * 32u, v0);
+        tmem_ld16(t_row + nt_l * 32u + 16u, v1);
+        tmem_ld_wait();
+        const uint32_t nt = nt0 + nt_l;
+        if (mt < p.Mt && nt < p.Nt) {
+            uint32_t bias_w[16];
+            if (has_bias) {
+                const uint4* bp = reinterpret_cast<const uint4*>(p.bias + nt * 32u);
+                uint4 b0 = __ldg(bp), b1 = __ldg(bp + 1), b2 = __ldg(bp + 2), b3 = __ldg(bp + 3);
+                bias_w[0] = b0.x; bias_w[1] = b0.y; bias_w[2] = b0.z; bias_w[3] = b0.w;
+                bias_w[4] = b1.x; bias_w[5] = b1.y; bias_w[6] = b1.z; bias_w[7] = b1.w;
+                bias_w[8] = b2.x; bias_w[9] = b2.y; bias_w[10] = b2.z; bias_w[11] = b2.w;
+                bias_w[12] = b3.x; bias_w[13] = b3.y; bias_w[14] = b3.z; bias_w[15] = b3.w;
+            } else {
+#pragma unroll
+                for (int i = 0; i < 16; ++i) bias_w[i] = 0u;
+            }
+            uint32_t o[16];
+#pragma unroll
+            for (int i = 0; i < 8; ++i) {
+                // face column 0: columns 2i, 2i+1 ; face column 1: 16+2i, 17+2i
+                uint32_t bl0 = bias_w[i] & 0xffffu, bh0 = bias_w[i] >> 16;
+                uint32_t bl1 = bias_w[8 + i] & 0xffffu, bh1 = bias_w[8 + i] >> 16;
+                o[i] = pack_bf16x2(epi1(v0[2 * i], bl0, has_bias, relu),
+                                   epi1(v0[2 * i + 1], bh0, has_bias, relu));
+                o[8 + i] = pack_bf16x2(epi1(v1[2 * i], bl1, has_bias, relu),
+                                       epi1(v1[2 * i + 1], bh1, has_bias, relu));
+            }
+            uint16_t* tile_base = p.c + ((uint64_t)mt * p.Nt + nt) * 1024u;
+            uint4* d0 = reinterpret_cast<uint4*>(tile_base + (fr * 2u + 0u) * 256u + r0 * 16u);
+            uint4* d1 = reinterpret_cast<uint4*>(tile_base + (fr * 2u + 1u) * 256u + r0 * 16u);
+            d0[0] = make_uint4(o[0], o[1], o[2], o[3]);
+            d0[1] = make_uint4(o[4], o[5], o[6], o[7]);
+            d1[0] = make_uint4(o[8], o[9], o[10], o[11]);
+            d1[1] = make_uint4(o[12], o[13], o[14], o[15]);
+        }
+    }
 }
 
 __global__ void __launch_bounds__(kThreads, 1)
@@ -392,9 +312,6 @@ gemm_tiles_kernel(const Params p) {
     } else {
         // ---------------------------------------------------- epilogue
         const uint32_t q = warp & 3u;  // TMEM lane quadrant this warp may access
-        const uint32_t fr = lane >> 4, r0 = lane & 15u;
-        const bool has_bias = p.bias != nullptr;
-        const bool relu = p.relu != 0;
         uint32_t acc = 0, acc_phase = 0;
         for (uint32_t tile = blockIdx.x; tile < num_tiles; tile += gridDim.x) {
             uint32_t mb, nb;
@@ -406,48 +323,7 @@ gemm_tiles_kernel(const Params p) {
             ok = __shfl_sync(0xffffffffu, ok ? 1 : 0, 0) != 0;
             if (!ok) break;
             tc_fence_after();
-            const uint32_t mt = mb * 4 + q;
-            const uint32_t t_row = tmem_base + ((q * 32u) << 16) + acc * kBN;
-#pragma unroll 1
-            for (uint32_t nt_l = 0; nt_l < 8; ++nt_l) {
-                uint32_t v0[16], v1[16];
-                tmem_ld16(t_row + nt_l * 32u, v0);
-                tmem_ld16(t_row + nt_l * 32u + 16u, v1);
-                tmem_ld_wait();
-                const uint32_t nt = nb * 8 + nt_l;
-                if (mt < p.Mt && nt < p.Nt) {
-                    uint32_t bias_w[16];
-                    if (has_bias) {
-                        const uint4* bp = reinterpret_cast<const uint4*>(p.bias + nt * 32u);
-                        uint4 b0 = __ldg(bp), b1 = __ldg(bp + 1), b2 = __ldg(bp + 2), b3 = __ldg(bp + 3);
-                        bias_w[0] = b0.x; bias_w[1] = b0.y; bias_w[2] = b0.z; bias_w[3] = b0.w;
-                        bias_w[4] = b1.x; bias_w[5] = b1.y; bias_w[6] = b1.z; bias_w[7] = b1.w;
-                        bias_w[8] = b2.x; bias_w[9] = b2.y; bias_w[10] = b2.z; bias_w[11] = b2.w;
-                        bias_w[12] = b3.x; bias_w[13] = b3.y; bias_w[14] = b3.z; bias_w[15] = b3.w;
-                    } else {
-#pragma unroll
-                        for (int i = 0; i < 16; ++i) bias_w[i] = 0u;
-                    }
-                    uint32_t o[16];
-#pragma unroll
-                    for (int i = 0; i < 8; ++i) {
-                        // face column 0: columns 2i, 2i+1 ; face column 1: 16+2i, 17+2i
-                        uint32_t bl0 = bias_w[i] & 0xffffu, bh0 = bias_w[i] >> 16;
-                        uint32_t bl1 = bias_w[8 + i] & 0xffffu, bh1 = bias_w[8 + i] >> 16;
-                        o[i] = pack_bf16x2(epi1(v0[2 * i], bl0, has_bias, relu),
-                                           epi1(v0[2 * i + 1], bh0, has_bias, relu));
-                        o[8 + i] = pack_bf16x2(epi1(v1[2 * i], bl1, has_bias, relu),
-                                               epi1(v1[2 * i + 1], bh1, has_bias, relu));
-                    }
-                    uint16_t* tile_base = p.c + ((uint64_t)mt * p.Nt + nt) * 1024u;
-                    uint4* d0 = reinterpret_cast<uint4*>(tile_base + (fr * 2u + 0u) * 256u + r0 * 16u);
-                    uint4* d1 = reinterpret_cast<uint4*>(tile_base + (fr * 2u + 1u) * 256u + r0 * 16u);
-                    d0[0] = make_uint4(o[0], o[1], o[2], o[3]);
-                    d0[1] = make_uint4(o[4], o[5], o[6], o[7]);
-                    d1[0] = make_uint4(o[8], o[9], o[10], o[11]);
-                    d1[1] = make_uint4(o[12], o[13], o[14], o[15]);
-                }
-            }
+            store_tile_row(p, tmem_base + ((q * 32u) << 16) + acc * kBN, mb * 4 + q, nb * 8, lane);
             tc_fence_before();
             __syncwarp();
             if (lane == 0) mbar_arrive(&tempty[acc]);
@@ -469,7 +345,248 @@ gemm_tiles_kernel(const Params p) {
     }
 }
 
+// ============================================================ 2-SM kernel ===
+// The same tile-layout GEMM on CTA pairs (cluster of 2) with the 2-SM UMMA:
+// the even CTA issues tcgen05.mma.cta_group::2 (M = 256, N = 256, K = 16)
+// whose A rows 0..127 / 128..255 come from the even / odd CTA's shared memory
+// and whose B columns 0..127 / 128..255 likewise; each CTA's TMEM receives its
+// 128 rows x 256 columns.  Per k-block (K = 64) a CTA stages 16 KiB of A and
+// 16 KiB of B (a third less L2 traffic per FLOP than 128x256 on one SM), so
+// six stages fit in shared memory.
+//
+// Synchronisation: each CTA's producers arrive on their own full[s] through
+// cp.async.mbarrier.arrive; in the odd CTA a relay lane waits for it, fences
+// the async proxy and arrives (relaxed, cluster scope) on the even CTA's
+// full[s], which therefore counts 128 + 1 arrivals.  The even CTA's MMA commits are multicast to both CTAs'
+// empty[s] / tfull[b]; both CTAs' epilogue warps arrive on the even CTA's
+// tempty[b] (8 arrivals).  A cluster barrier after set-up and before exit
+// keeps both CTAs alive while the other may touch their shared memory.
+constexpr int kPStages = 6;
+constexpr int kPABytes = 128 * kBKT * 32 * 2;  // 16 KiB: 128 rows x K 64
+constexpr int kPBBytes = 128 * kBKT * 32 * 2;  // 16 KiB: 128 cols x K 64
+constexpr int kPStageBytes = kPABytes + kPBBytes;
+constexpr int kPFaces = 64;                    // 32 A + 32 B faces per CTA
+constexpr int kPSmemBytes = kPStages * kPStageBytes + 1024 + 256;
+
+__global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
+gemm_pair_kernel(const Params p) {
+    extern __shared__ uint8_t smem_raw[];
+    uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) &
+                                               ~uintptr_t(1023));
+    uint64_t* full = reinterpret_cast<uint64_t*>(smem + kPStages * kPStageBytes);
+    uint64_t* empty = full + kPStages;
+    uint64_t* tfull = empty + kPStages;
+    uint64_t* tempty = tfull + 2;
+    uint64_t* drain = tempty + 2;
+    uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(drain + 1);
+    volatile uint32_t* abort_flag = tmem_slot + 1;
+
+    const uint32_t warp = threadIdx.x >> 5, lane = threadIdx.x & 31u;
+    const uint32_t rank = cluster_ctarank();
+    const bool leader = rank == 0;
+    const uint32_t pair_id = blockIdx.x >> 1, num_pairs = gridDim.x >> 1;
+
+    if (threadIdx.x == 0) {
+        for (int s = 0; s < kPStages; ++s) {
+            mbar_init(&full[s], kProdWarps * 32 + (leader ? 1 : 0));
+            mbar_init(&empty[s], 1);
+        }
+        for (int b = 0; b < 2; ++b) {
+            mbar_init(&tfull[b], 1);
+            mbar_init(&tempty[b], 8);
+        }
+        mbar_init(drain, 1);
+        *abort_flag = 0u;
+        asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+        asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+    }
+    if (warp == kMmaWarp) {
+        asm volatile("tcgen05.alloc.cta_group::2.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(
+                         smem_u32(tmem_slot)),
+                     "r"(kTmemCols)
+                     : "memory");
+        asm volatile("tcgen05.relinquish_alloc_permit.cta_group::2.sync.aligned;" ::: "memory");
+    }
+    tc_fence_before();
+    __syncwarp();
+    cluster_sync();
+    tc_fence_after();
+    const uint32_t tmem_base = *tmem_slot;
+
+    const uint32_t num_tiles = p.m_blocks * p.n_blocks;  // m_blocks = 256-row pairs
+    const uint32_t num_kb = (p.Kt + kBKT - 1) / kBKT;
+
+    if (warp < kProdWarps) {
+        // ---------------------------------------------------- producers
+        const uint32_t src_lane = lane * 16u;
+        const uint32_t dst_lane = (lane >> 1) * 32u + ((((lane & 1u) ^ ((lane >> 3) & 1u))) << 4);
+        const char* a_g = reinterpret_cast<const char*>(p.a);
+        const char* b_g = reinterpret_cast<const char*>(p.b);
+        uint32_t stage = 0, phase = 0;
+        for (uint32_t tile = pair_id; tile < num_tiles; tile += num_pairs) {
+            uint32_t mp, nb;
+            tile_coords(tile, p.m_blocks, p.n_blocks, mp, nb);
+            const uint32_t mt0 = (mp * 2u + rank) * 4u;  // this CTA's 4 tile rows
+            const uint32_t nt0 = nb * 8u + rank * 4u;    // this CTA's 4 B tile columns
+            bool ok = true;
+            for (uint32_t kb = 0; kb < num_kb; ++kb) {
+                bool w = true;
+                if (lane == 0) w = mbar_wait_cluster(&empty[stage], phase ^ 1u, abort_flag, p.err);
+                if (__shfl_sync(0xffffffffu, w ? 1 : 0, 0) == 0) {
+                    ok = false;
+                    break;
+                }
+                const uint32_t a_s = smem_u32(smem + stage * kPStageBytes);
+                const uint32_t b_s = a_s + kPABytes;
+                const uint32_t kt0 = kb * kBKT;
+#pragma unroll
+                for (int i = 0; i < kPFaces / kProdWarps; ++i) {
+                    const uint32_t f = warp + kProdWarps * i;
+                    const char* src;
+                    uint32_t dst;
+                    bool valid;
+                    if (i < 32 / kProdWarps) {  // A face: (mt_l, ktl, fr, fc)
+                        const uint32_t mt_l = f >> 3, ktl = (f >> 2) & 1u, fr = (f >> 1) & 1u,
+                                       fc = f & 1u;
+                        const uint32_t mt = mt0 + mt_l, kt = kt0 + ktl;
+                        valid = mt < p.Mt && kt < p.Kt;
+                        src = a_g + (((uint64_t)mt * p.Kt + kt) * 1024u + (fr * 2u + fc) * 256u) * 2u;
+                        dst = a_s + (ktl * 2u + fc) * 4096u + (mt_l * 32u + fr * 16u) * 32u;
+                    } else {  // B face: (ktl, nt_l, fr, fc)
+                        const uint32_t g = f - 32u;
+                        const uint32_t ktl = g >> 4, nt_l = (g >> 2) & 3u, fr = (g >> 1) & 1u,
+                                       fc = g & 1u;
+                        const uint32_t kt = kt0 + ktl, nt = nt0 + nt_l;
+                        valid = kt < p.Kt && nt < p.Nt;
+                        src = b_g + (((uint64_t)kt * p.Nt + nt) * 1024u + (fr * 2u + fc) * 256u) * 2u;
+                        dst = b_s + fr * 8192u + ktl * 4096u + (nt_l * 2u + fc) * 512u;
+                    }
+                    cp_async16(dst + dst_lane, valid ? src + src_lane : a_g, valid ? 16u : 0u);
+                }
+                cp_async_arrive(&full[stage]);
+                if (++stage == kPStages) {
+                    stage = 0;
+                    phase ^= 1u;
+                }
+            }
+            if (!ok) break;
+        }
+        asm volatile("cp.async.wait_all;" ::: "memory");
+    } else if (warp == kMmaWarp) {
+        if (lane == 0 && !leader) {
+            // ---------------------------------- relay (odd CTA): full -> leader
+            const uint32_t remote_full0 = map_to_rank(&full[0], 0);
+            uint32_t stage = 0, phase = 0;
+            bool ok = true;
+            for (uint32_t tile = pair_id; ok && tile < num_tiles; tile += num_pairs) {
+                for (uint32_t kb = 0; kb < num_kb; ++kb) {
+                    if (!mbar_wait(&full[stage], phase, abort_flag, p.err)) {
+                        ok = false;
+                        break;
+                    }
+                    // Operands written by cp.async (generic proxy) are read by
+                    // the partner's tensor cores (async proxy).
+                    asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+                    mbar_arrive_remote_relaxed(remote_full0 + stage * 8u);
+                    if (++stage == kPStages) {
+                        stage = 0;
+                        phase ^= 1u;
+                    }
+                }
+            }
+        } else if (lane == 0) {
+            // ------------------------------------- MMA issuer (even CTA)
+            constexpr uint32_t idesc = make_idesc(256, kBN);
+            constexpr uint64_t a_base = smem_desc_base(16, 256);   // K-major SW32
+            constexpr uint64_t b_base = smem_desc_base(512, 256);  // MN-major SW32
+            uint32_t stage = 0, phase = 0, acc = 0, acc_phase = 0;
+            bool ok = true;
+            for (uint32_t tile = pair_id; ok && tile < num_tiles; tile += num_pairs) {
+                if (!mbar_wait_cluster(&tempty[acc], acc_phase ^ 1u, abort_flag, p.err)) break;
+                tc_fence_after();
+                const uint32_t d_tmem = tmem_base + acc * kBN;
+                for (uint32_t kb = 0; kb < num_kb; ++kb) {
+                    if (!mbar_wait_cluster(&full[stage], phase, abort_flag, p.err)) {
+                        ok = false;
+                        break;
+                    }
+                    asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+                    tc_fence_after();
+                    const uint32_t a_addr = smem_u32(smem + stage * kPStageBytes);
+                    const uint32_t b_addr = a_addr + kPABytes;
+#pragma unroll
+                    for (uint32_t s = 0; s < 4; ++s) {
+                        const uint32_t a_off = s * 4096u;
+                        const uint32_t b_off = (s & 1u) * 8192u + (s >> 1) * 4096u;
+                        const uint64_t ad = a_base | (uint64_t)(((a_addr + a_off) >> 4) & 0x3fffu);
+                        const uint64_t bd = b_base | (uint64_t)(((b_addr + b_off) >> 4) & 0x3fffu);
+                        tc_mma_pair(d_tmem, ad, bd, idesc, (kb | s) != 0u);
+                    }
+                    tc_commit_pair_mc(&empty[stage], 0x3);
+                    if (++stage == kPStages) {
+                        stage = 0;
+                        phase ^= 1u;
+                    }
+                }
+                if (!ok) break;
+                tc_commit_pair_mc(&tfull[acc], 0x3);
+                if (++acc == 2) {
+                    acc = 0;
+                    acc_phase ^= 1u;
+                }
+            }
+            tc_commit_pair(drain);
+            mbar_drain(drain, 0, 100000000ull);
+        }
+    } else {
+        // ---------------------------------------------------- epilogue
+        const uint32_t q = warp & 3u;
+        const uint32_t remote_tempty0 = map_to_rank(&tempty[0], 0);
+        uint32_t acc = 0, acc_phase = 0;
+        for (uint32_t tile = pair_id; tile < num_tiles; tile += num_pairs) {
+            uint32_t mp, nb;
+            tile_coords(tile, p.m_blocks, p.n_blocks, mp, nb);
+            bool ok = true;
+            if (lane == 0) ok = mbar_wait_cluster(&tfull[acc], acc_phase, abort_flag, p.err);
+            ok = __shfl_sync(0xffffffffu, ok ? 1 : 0, 0) != 0;
+            if (!ok) break;
+            tc_fence_after();
+            store_tile_row(p, tmem_base + ((q * 32u) << 16) + acc * kBN, (mp * 2u + rank) * 4u + q,
+                           nb * 8u, lane);
+            tc_fence_before();
+            __syncwarp();
+            if (lane == 0) mbar_arrive_remote(remote_tempty0 + acc * 8u);
+            if (++acc == 2) {
+                acc = 0;
+                acc_phase ^= 1u;
+            }
+        }
+    }
+
+    tc_fence_before();
+    __syncwarp();
+    cluster_sync();
+    if (warp == kMmaWarp) {
+        tc_fence_after();
+        asm volatile("tcgen05.dealloc.cta_group::2.sync.aligned.b32 %0, %1;" ::"r"(tmem_base),
+                     "r"(kTmemCols)
+                     : "memory");
+    }
+}
+
 // ------------------------------------------------------------------ host ---
+static int check_launch(const char* what) {
+    cudaError_t e = cudaGetLastError();
+    if (e != cudaSuccess) {
+        char buf[256];
+        snprintf(buf, sizeof buf, "%s: launch failed: %s", what, cudaGetErrorString(e));
+        foil_set_error(FOIL_ERR_CUDA, buf);
+        return FOIL_ERR_CUDA;
+    }
+    foil_count_launch();
+    return FOIL_OK;
+}
+
 int launch(const uint16_t* a, const uint16_t* b, uint16_t* c, uint32_t Mt, uint32_t Kt,
            uint32_t Nt, const uint16_t* bias, int relu, uint32_t* err, cudaStream_t stream,
            int max_ctas) {
@@ -478,6 +595,10 @@ int launch(const uint16_t* a, const uint16_t* b, uint16_t* c, uint32_t Mt, uint3
     std::call_once(attr_once, [] {
         attr_err = cudaFuncSetAttribute(gemm_tiles_kernel,
                                         cudaFuncAttributeMaxDynamicSharedMemorySize, kSmemBytes);
+        if (attr_err == cudaSuccess)
+            attr_err = cudaFuncSetAttribute(gemm_pair_kernel,
+                                            cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                            kPSmemBytes);
     });
     if (attr_err != cudaSuccess) {
         foil_set_error(FOIL_ERR_CUDA, "foil_matmul_tiles: cudaFuncSetAttribute failed");
@@ -491,22 +612,23 @@ int launch(const uint16_t* a, const uint16_t* b, uint16_t* c, uint32_t Mt, uint3
     p.Mt = Mt;
     p.Kt = Kt;
     p.Nt = Nt;
-    p.m_blocks = (Mt + 3) / 4;
     p.n_blocks = (Nt + 7) / 8;
     p.relu = relu;
     p.err = err;
-    const uint32_t tiles = p.m_blocks * p.n_blocks;
-    const uint32_t grid = tiles < (uint32_t)max_ctas ? tiles : (uint32_t)max_ctas;
-    gemm_tiles_kernel<<<grid, kThreads, kSmemBytes, stream>>>(p);
-    cudaError_t e = cudaGetLastError();
-    if (e != cudaSuccess) {
-        char buf[256];
-        snprintf(buf, sizeof buf, "foil_matmul_tiles: launch failed: %s", cudaGetErrorString(e));
-        foil_set_error(FOIL_ERR_CUDA, buf);
-        return FOIL_ERR_CUDA;
+    if (Mt <= 4 || max_ctas < 2) {
+        // One 128-row block: the single-SM kernel avoids an idle partner CTA.
+        p.m_blocks = (Mt + 3) / 4;
+        const uint32_t tiles = p.m_blocks * p.n_blocks;
+        const uint32_t grid = tiles < (uint32_t)max_ctas ? tiles : (uint32_t)max_ctas;
+        gemm_tiles_kernel<<<grid, kThreads, kSmemBytes, stream>>>(p);
+        return check_launch("foil_matmul_tiles");
     }
-    foil_count_launch();
-    return FOIL_OK;
+    p.m_blocks = (Mt + 7) / 8;  // 256-row blocks, one per CTA pair
+    const uint32_t tiles = p.m_blocks * p.n_blocks;
+    const uint32_t max_pairs = (uint32_t)max_ctas / 2;
+    const uint32_t pairs = tiles < max_pairs ? tiles : max_pairs;
+    gemm_pair_kernel<<<pairs * 2, kThreads, kPSmemBytes, stream>>>(p);
+    return check_launch("foil_matmul_tiles (2-SM)");
 }
 
 }  // namespace gemm
