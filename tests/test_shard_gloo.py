@@ -1,0 +1,103 @@
+"""Multi-rank host logic on CPU (gloo, world size 2 and 3): the M-shard of the
+tiled GEMM and the batch shard of the NHWC conv, reassembled with an
+all-gather, equal the unsharded result.  The GPU path (bench.py under
+torchrun) uses the same split_rows / contiguous-shard layout with NCCL.
+"""
+import os
+import socket
+
+import numpy as np
+import pytest
+import torch.distributed as dist
+import torch.multiprocessing as mp
+
+
+def free_port():
+    s = socket.socket()
+    s.bind(("127.0.0.1", 0))
+    p = s.getsockname()[1]
+    s.close()
+    return p
+
+
+def worker(rank, world, port, q):
+    import sys
+    import torch
+    repo = os.path.dirname(os.path.dirname(os.path.abspath(__file__)))
+    sys.path[:0] = [repo, os.path.join(repo, "tt-foil_b200")]
+    from oracle import oracle
+    from ttfoil import shard
+
+    os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port))
+    dist.init_process_group("gloo", rank=rank, world_size=world)
+    try:
+        # GEMM: 7 tile rows over `world` ranks (uneven split), Kt = 3, Nt = 2.
+        Mt, Kt, Nt = 7, 3, 2
+        a = oracle.rand_bf16((Mt * 32, Kt * 32), 1)
+        b = oracle.rand_bf16((Kt * 32, Nt * 32), 2)
+        r0, r1 = shard.split_rows(Mt, world, rank)
+        a_tiles = oracle.tilize(a)
+        mine = a_tiles[r0 * Kt * 1024:r1 * Kt * 1024]
+        c_part = oracle.matmul_tiles(mine, oracle.tilize(b), r1 - r0, Kt, Nt) if r1 > r0 else \
+            np.zeros(0, np.uint16)
+        # all-gather of uneven shards: pad to the largest share
+        # gloo has no 16-bit integer collectives: move bf16 bits as int32 pairs
+        cap = shard.shard_bytes(-(-Mt // world), Nt) // 2
+        buf = np.zeros(cap, np.uint16)
+        buf[:c_part.size] = c_part
+        parts = [torch.zeros(cap // 2, dtype=torch.int32) for _ in range(world)]
+        dist.all_gather(parts, torch.from_numpy(buf.view(np.int32)))
+        shards = []
+        for r in range(world):
+            s0, s1 = shard.split_rows(Mt, world, r)
+            shards.append(parts[r].numpy().view(np.uint16)[:(s1 - s0) * Nt * 1024])
+        c_all = shard.gather_tiles(shards)
+        ok_gemm = np.array_equal(c_all, oracle.matmul_tiles(a_tiles, oracle.tilize(b), Mt, Kt, Nt))
+
+        # conv: batch 4 split over ranks, NHWC images are contiguous.
+        x = oracle.rand_bf16((4, 6, 6, 8), 3)
+        w = oracle.randn_bf16((16, 3, 3, 8), 4, 0.2)
+        bias = oracle.rand_bf16((16,), 5, -0.1, 0.1)
+        n0, n1 = shard.split_rows(4, world, rank)
+        y_part = oracle.conv_nhwc(x[n0:n1], w, bias, 2, 1, relu=True)
+        per = y_part[0].size if n1 > n0 else 3 * 3 * 16
+        cap = -(-4 // world) * per
+        buf = np.zeros(cap, np.uint16)
+        buf[:y_part.size] = y_part.reshape(-1)
+        parts = [torch.zeros(cap // 2, dtype=torch.int32) for _ in range(world)]
+        dist.all_gather(parts, torch.from_numpy(buf.view(np.int32)))
+        ys = []
+        for r in range(world):
+            s0, s1 = shard.split_rows(4, world, r)
+            ys.append(parts[r].numpy().view(np.uint16)[:(s1 - s0) * per])
+        y_all = np.concatenate(ys).reshape(4, 3, 3, 16)
+        ok_conv = np.array_equal(y_all, oracle.conv_nhwc(x, w, bias, 2, 1, relu=True))
+        q.put((rank, bool(ok_gemm), bool(ok_conv)))
+    finally:
+        dist.destroy_process_group()
+
+
+@pytest.mark.parametrize("world", [2, 3])
+def test_sharded_results_reassemble(world):
+    ctx = mp.get_context("spawn")
+    q = ctx.Queue()
+    port = free_port()
+    procs = [ctx.Process(target=worker, args=(r, world, port, q)) for r in range(world)]
+    for p in procs:
+        p.start()
+    res = [q.get(timeout=90) for _ in range(world)]
+    for p in procs:
+        p.join(timeout=60)
+        assert p.exitcode == 0
+    assert all(g and c for _, g, c in res), res
+
+
+def test_split_rows_covers_range():
+    from ttfoil import shard
+    for total in [0, 1, 7, 64, 65]:
+        for world in [1, 2, 3, 8]:
+            spans = [shard.split_rows(total, world, r) for r in range(world)]
+            assert spans[0][0] == 0 and spans[-1][1] == total
+            assert all(spans[i][1] == spans[i + 1][0] for i in range(world - 1))
+            sizes = [e - b for b, e in spans]
+            assert max(sizes) - min(sizes) <= 1
