@@ -261,6 +261,25 @@ FOIL_API int foil_matmul_tiles_dev(const uint16_t* a, const uint16_t* b, uint16_
                           uint32_t Mt, uint32_t Kt, uint32_t Nt,
                           const uint16_t* bias, int32_t relu, void* stream);
 
+/* Allocation-free variant of foil_matmul_tiles_dev, for callers that cannot
+ * allocate device memory when they launch (allocator or memory-pool
+ * callbacks, processes whose GPU memory another allocator already owns,
+ * loops that forbid allocation after start-up).  No counterpart in the
+ * reference, which has no allocation-free launch path.  Same kernel and
+ * arguments; its 4-byte scratch (the device error word) lives in a 256-byte
+ * array compiled into the library, so the call makes no cudaMalloc, cudaFree
+ * or other allocating call; scratch needs beyond 256 bytes are rejected.  The
+ * first call on each device resolves the array's address (make it before any
+ * stream capture).  All calls on a device share the array and each clears it
+ * first, so calls that overlap on the GPU race on it.  If `status_out` is
+ * non-NULL (host memory; page-locked to stay allocation-free) the call
+ * synchronizes `stream` and stores the error word (0 = no bounded wait
+ * expired), returning FOIL_ERR_DEVICE when it is set. */
+FOIL_API int foil_matmul_tiles_noalloc_dev(const uint16_t* a, const uint16_t* b, uint16_t* c,
+                                           uint32_t Mt, uint32_t Kt, uint32_t Nt,
+                                           const uint16_t* bias, int32_t relu, void* stream,
+                                           uint32_t* status_out);
+
 /* Read and clear the device-side error word of the current device: 0 if no
  * kernel reported an error (bounded waits that gave up) since the last call.
  * Synchronizes `stream`. */

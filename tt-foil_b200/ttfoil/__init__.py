@@ -93,6 +93,10 @@ SIGNATURES = {
     "foil_matmul_tiles_dev": (ctypes.c_int, [_U16P, _U16P, _U16P, ctypes.c_uint32, ctypes.c_uint32,
                                              ctypes.c_uint32, _U16P, ctypes.c_int32, _P]),
     "foil_device_error_dev": (ctypes.c_int, [_P, ctypes.POINTER(ctypes.c_uint32)]),
+    "foil_matmul_tiles_noalloc_dev": (ctypes.c_int, [_U16P, _U16P, _U16P, ctypes.c_uint32,
+                                                     ctypes.c_uint32, ctypes.c_uint32, _U16P,
+                                                     ctypes.c_int32, _P,
+                                                     ctypes.POINTER(ctypes.c_uint32)]),
 }
 
 _lib = None
