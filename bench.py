@@ -341,10 +341,12 @@ def spot_check(ttfoil, a, b, c, Mt, Kt, Nt):
 
 def read_traffic():
     """DRAM bytes per GEMM launch from the committed ncu summary, if any."""
-    path = os.path.join(REPO, "profiles", "gemm_tc_8192_traffic.json")
+    path = os.path.join(REPO, "profiles", "gemm_tc_8192.md")
     if os.path.exists(path):
         with open(path) as f:
-            return json.load(f).get("dram_bytes_per_launch")
+            for line in f:
+                if line.startswith("traffic_bytes_per_launch"):
+                    return float(line.split("=")[1])
     return None
 
 

@@ -64,28 +64,30 @@ relu_kernel(const uint4* __restrict__ in, uint4* __restrict__ out, uint64_t n8) 
     for (; i < n8; i += stride) __stcs(out + i, relu_v(__ldcs(in + i)));
 }
 
-// Bias add over a tile-layout matrix with Nt tile-columns.  A 16-byte chunk
-// at element offset e covers 8 consecutive columns of one face row:
-//   tile t = e / 1024, face f = (e % 1024) / 256, column in face = e % 16,
-//   column = (t % Nt) * 32 + (f & 1) * 16 + e % 16.
-// The bias for column c sits in row 0 of bias tile c/32:
-//   bias element offset = (c / 32) * 1024 + ((c % 32) / 16) * 256 + c % 16.
+// Bias add over a tile-layout matrix with Nt tile-columns, one warp per
+// 2 KiB tile.  Lane l handles the 16-byte chunks l, l+32, l+64, l+96 of the
+// tile: chunk c lies in face c/32 (face column (c/32) & 1) and covers columns
+// ((c/32) & 1) * 16 + (l & 1) * 8 + [0, 8) of the tile.  The bias for column n
+// is in row 0 of bias tile n/32, i.e. at (n/32) * 1024 + ((n%32)/16) * 256 + n%16,
+// so each lane loads its two bias vectors once per tile.
 __global__ void __launch_bounds__(256)
 bias_kernel(const uint4* __restrict__ in, const uint16_t* __restrict__ bias_tiles,
-            uint4* __restrict__ out, uint64_t n8, uint32_t Nt) {
-    const uint64_t stride = (uint64_t)gridDim.x * blockDim.x;
-    for (uint64_t i = (uint64_t)blockIdx.x * blockDim.x + threadIdx.x; i < n8; i += stride) {
-        uint64_t e = i * 8;
-        uint32_t t = (uint32_t)(e >> 10);
-        uint32_t within = (uint32_t)(e & 1023u);
-        uint32_t nt = t % Nt;
-        uint32_t fc = (within >> 8) & 1u;
-        uint32_t c16 = within & 15u;  // 0 or 8
-        // Row 0 of face (0, fc) of bias tile nt, columns c16..c16+7.
-        const uint4 bv = __ldg(reinterpret_cast<const uint4*>(
-            bias_tiles + (uint64_t)nt * 1024 + fc * 256 + c16));
-        uint4 x = __ldcs(in + i);
-        __stcs(out + i, add_v(x, bv));
+            uint4* __restrict__ out, uint64_t num_tiles, uint32_t Nt) {
+    const uint32_t lane = threadIdx.x & 31u;
+    const uint64_t warps = (uint64_t)gridDim.x * (blockDim.x >> 5);
+    for (uint64_t t = (uint64_t)blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5); t < num_tiles;
+         t += warps) {
+        const uint32_t nt = (uint32_t)(t % Nt);
+        const uint16_t* bt = bias_tiles + (uint64_t)nt * 1024 + (lane & 1u) * 8u;
+        const uint4 b0 = __ldg(reinterpret_cast<const uint4*>(bt));        // face column 0
+        const uint4 b1 = __ldg(reinterpret_cast<const uint4*>(bt + 256));  // face column 1
+        const uint4* src = in + t * 128u + lane;
+        uint4* dst = out + t * 128u + lane;
+        uint4 x0 = __ldcs(src), x1 = __ldcs(src + 32), x2 = __ldcs(src + 64), x3 = __ldcs(src + 96);
+        __stcs(dst, add_v(x0, b0));
+        __stcs(dst + 32, add_v(x1, b1));
+        __stcs(dst + 64, add_v(x2, b0));
+        __stcs(dst + 96, add_v(x3, b1));
     }
 }
 
@@ -164,8 +166,8 @@ extern "C" int foil_bias_add_tiles_dev(const uint16_t* in, const uint16_t* bias_
         foil_set_error(FOIL_ERR_INVALID, "foil_bias_add_tiles_dev: null or misaligned pointer");
         return FOIL_ERR_INVALID;
     }
-    uint64_t n8 = (uint64_t)rows * cols / 8;
-    foil::bias_kernel<<<foil::grid_for(n8), 256, 0, (cudaStream_t)stream>>>(
-        (const uint4*)in, bias_tiles, (uint4*)out, n8, cols / 32);
+    const uint64_t tiles = (uint64_t)(rows / 32) * (cols / 32);
+    foil::bias_kernel<<<foil::grid_for(tiles * 32), 256, 0, (cudaStream_t)stream>>>(
+        (const uint4*)in, bias_tiles, (uint4*)out, tiles, cols / 32);
     return foil::check("foil_bias_add_tiles_dev");
 }
