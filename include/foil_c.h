@@ -261,6 +261,19 @@ FOIL_API int foil_matmul_tiles_dev(const uint16_t* a, const uint16_t* b, uint16_
                           uint32_t Mt, uint32_t Kt, uint32_t Nt,
                           const uint16_t* bias, int32_t relu, void* stream);
 
+/* NHWC convolution as an implicit GEMM on tcgen05 tensor cores, with fused
+ * bias and relu: y (N, Ho, Wo, Cout) = relu?(bf16(bf16(conv(x, w)) + bias)),
+ * x (N, H, W, Cin), w (Cout, KH, KW, Cin), bias (Cout) or NULL, fp32
+ * accumulation, Ho = (H + 2 pad - KH) / stride + 1.  Cin and Cout must be
+ * multiples of 16.  Replaces the reference's conv path — host im2col
+ * (tests/test_conv_3x3.cpp:108-127, test_conv_3x3_s2.cpp:114-133) feeding
+ * the tiled matmul (tests/test_conv_3x3.cpp:214-222) — followed by bias_add
+ * and relu. */
+FOIL_API int foil_conv2d_nhwc_dev(const uint16_t* x, const uint16_t* w, const uint16_t* bias,
+                                  uint16_t* y, uint32_t N, uint32_t H, uint32_t W, uint32_t Cin,
+                                  uint32_t Cout, uint32_t KH, uint32_t KW, uint32_t stride,
+                                  uint32_t pad, int32_t relu, void* stream);
+
 /* Allocation-free variant of foil_matmul_tiles_dev, for callers that cannot
  * allocate device memory when they launch (allocator or memory-pool
  * callbacks, processes whose GPU memory another allocator already owns,

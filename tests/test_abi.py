@@ -22,6 +22,16 @@ def declared_functions():
     return sorted(set(re.findall(r"FOIL_API\s+[\w\s\*]+?\b(foil_\w+)\s*\(", text)))
 
 
+def declared_arg_counts():
+    """Number of parameters of every FOIL_API function in the header."""
+    text = open(HEADER).read()
+    counts = {}
+    for m in re.finditer(r"FOIL_API\s+[\w\s\*]+?\b(foil_\w+)\s*\(([^)]*)\)", text):
+        args = m.group(2).strip()
+        counts[m.group(1)] = 0 if args in ("", "void") else args.count(",") + 1
+    return counts
+
+
 def exported(path):
     out = subprocess.run(["nm", "-D", "--defined-only", path], capture_output=True, text=True,
                          check=True).stdout
@@ -51,6 +61,12 @@ def test_library_loads_and_binding_matches_header():
         assert hasattr(L, name)
         assert name in ttfoil.SIGNATURES, f"ttfoil binding lacks {name}"
     assert b"sm_100a" in L.foil_version()
+
+
+def test_binding_argument_counts_match_header():
+    import ttfoil
+    for name, n in declared_arg_counts().items():
+        assert len(ttfoil.SIGNATURES[name][1]) == n, name
 
 
 def test_cpp_api_exports_tt_foil_functions():

@@ -32,6 +32,7 @@
 #include "../../include/foil_c.h"
 #include "host_logic.hpp"
 #include "kernels/gemm_tc.cuh"
+#include "kernels/conv_tc.cuh"
 
 namespace {
 
@@ -668,6 +669,29 @@ extern "C" int foil_matmul_tiles_dev(const uint16_t* a, const uint16_t* b, uint1
         uint32_t* err = error_word_for_current_device();
         throw_status(foil::gemm::launch(a, b, c, Mt, Kt, Nt, bias, relu, err, (cudaStream_t)stream,
                                         sm_count_current()));
+    });
+}
+
+extern "C" int foil_conv2d_nhwc_dev(const uint16_t* x, const uint16_t* w, const uint16_t* bias,
+                                    uint16_t* y, uint32_t N, uint32_t H, uint32_t W, uint32_t Cin,
+                                    uint32_t Cout, uint32_t KH, uint32_t KW, uint32_t stride,
+                                    uint32_t pad, int32_t relu, void* stream) {
+    return guarded([&] {
+        if (N == 0 || Cout == 0) return;
+        if (Cin == 0 || Cin % 16 || Cout % 16)
+            throw FoilError(FOIL_ERR_INVALID, "foil_conv2d_nhwc_dev: Cin and Cout must be non-zero multiples of 16");
+        if (H == 0 || W == 0 || KH == 0 || KW == 0 || stride == 0 || KH > 16 || KW > 16 || stride > 16 ||
+            pad >= KH || pad >= KW || H + 2 * pad < KH || W + 2 * pad < KW)
+            throw FoilError(FOIL_ERR_INVALID, "foil_conv2d_nhwc_dev: unsupported kernel / stride / padding");
+        const uint64_t Ho = (H + 2 * pad - KH) / stride + 1, Wo = (W + 2 * pad - KW) / stride + 1;
+        if ((uint64_t)N * H * W * Cin >= (1ull << 40) || (uint64_t)N * Ho * Wo >= (1ull << 31) ||
+            (uint64_t)N * H * W >= (1ull << 32))
+            throw FoilError(FOIL_ERR_INVALID, "foil_conv2d_nhwc_dev: tensor too large");
+        if (!x || !w || !y || !aligned16(x) || !aligned16(w) || !aligned16(y) || (bias && !aligned16(bias)))
+            throw FoilError(FOIL_ERR_INVALID, "foil_conv2d_nhwc_dev: null or misaligned pointer");
+        uint32_t* err = error_word_for_current_device();
+        throw_status(foil::conv::launch(x, w, bias, y, N, H, W, Cin, Cout, KH, KW, stride, pad, relu, err,
+                                        (cudaStream_t)stream, sm_count_current()));
     });
 }
 

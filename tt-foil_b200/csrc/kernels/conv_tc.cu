@@ -1,0 +1,371 @@
+// Implicit-GEMM NHWC convolution on tcgen05 tensor cores, fused bias + relu.
+//
+//   y[n, ho, wo, co] = relu( bf16( bf16( sum_{kh,kw,ci} x[n, ho*s+kh-p, wo*s+kw-p, ci]
+//                                                       * w[co, kh, kw, ci] ) + bias[co] ) )
+//
+// The reference runs convolutions as a host im2col followed by its tiled
+// matmul (tests/test_conv_3x3.cpp:108-127 and :214-222; stride only changes
+// the im2col, tests/test_conv_3x3_s2.cpp:11-15).  Here the im2col is implicit:
+// the GEMM rows are output pixels (M = N*Ho*Wo), the columns output channels
+// (N = Cout), K = (kh, kw, ci), and the producer warps gather A straight from
+// the NHWC input.  Padding taps are zero-filled by the copy itself.
+//
+// Operands in shared memory (canonical UMMA layouts, SWIZZLE_32B, K-major):
+//  * A: a k-block is one tap (kh, kw) x kc channels (kc = 64, 32 or 16).  Each
+//    output row's kc channels are one contiguous run of kc*2 bytes of one
+//    input pixel, so a warp copying four rows issues full 128-byte requests.
+//    K-step j (16 channels) holds 128 rows x 32 B, 8-row groups 256 B apart.
+//  * B: the weights, row co = w[co, kh, kw, cb*kc .. +kc] (also contiguous);
+//    K-step j holds BN rows x 32 B.
+//  Instruction: kind::f16, M = 128, N = BN, K = 16, A and B both K-major.
+//
+// Organisation: as the tiled GEMM (gemm_tc.cu): 4 producer warps (cp.async,
+// SW32 applied in the destination address), 1 MMA warp that owns TMEM
+// (2 x BN fp32 accumulator columns, double-buffered), 4 epilogue warps that
+// write row-major NHWC output (one 32-byte run of 16 channels per lane and
+// step).  Every wait is bounded (see gemm_ptx.cuh).
+#include <cstdio>
+#include <mutex>
+
+#include "common.cuh"
+#include "gemm_ptx.cuh"
+#include "conv_tc.cuh"
+#include "../../../include/foil_c.h"
+
+extern "C" void foil_set_error(int status, const char* msg);
+
+namespace foil {
+namespace conv {
+
+using namespace foil::gemm;
+
+constexpr int kProdWarps = 4;
+constexpr int kMmaWarp = 4;
+constexpr int kThreads = 9 * 32;
+
+struct Params {
+    const uint16_t* x;
+    const uint16_t* w;
+    const uint16_t* bias;
+    uint16_t* y;
+    uint32_t N, H, W, Cin, Cout, KH, KW, stride, pad, Ho, Wo;
+    uint32_t M;            // N * Ho * Wo
+    uint32_t kc;           // channels per k-block (16, 32 or 64)
+    uint32_t cblocks;      // Cin / kc
+    uint32_t num_kb;       // KH * KW * cblocks
+    uint32_t m_blocks, n_blocks;
+    int relu;
+    uint32_t* err;
+};
+
+template <int BN>
+struct Cfg {
+    static constexpr int kABytes = 128 * 128;               // 128 rows x 64 ch x 2 B (max kc)
+    static constexpr int kBBytes = BN * 128;                // BN rows x 64 ch x 2 B
+    static constexpr int kStageBytes = kABytes + kBBytes;
+    static constexpr int kStages = (200 * 1024) / kStageBytes > 8 ? 8 : (200 * 1024) / kStageBytes;
+    static constexpr int kSmemBytes = kStages * kStageBytes + 1024 + 256;
+    static constexpr int kTmemCols = 2 * BN < 32 ? 32 : 2 * BN;  // power of two for BN in {64,128,256}
+};
+
+__device__ __forceinline__ uint32_t epi_one(uint32_t acc_bits, uint32_t bias_bits, bool has_bias,
+                                            bool relu) {
+    uint32_t o = f32_to_bf16_bits(__uint_as_float(acc_bits));
+    if (has_bias) o = f32_to_bf16_bits(host_add_f32(bf16_bits_to_f32(o), bf16_bits_to_f32(bias_bits)));
+    if (relu && bf16_bits_to_f32(o) < 0.0f) o = 0u;
+    return o;
+}
+
+template <int BN>
+__global__ void __launch_bounds__(kThreads, 1) conv_kernel(const Params p) {
+    using C = Cfg<BN>;
+    extern __shared__ uint8_t smem_raw[];
+    uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) &
+                                               ~uintptr_t(1023));
+    uint64_t* full = reinterpret_cast<uint64_t*>(smem + C::kStages * C::kStageBytes);
+    uint64_t* empty = full + C::kStages;
+    uint64_t* tfull = empty + C::kStages;
+    uint64_t* tempty = tfull + 2;
+    uint64_t* drain = tempty + 2;
+    uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(drain + 1);
+    volatile uint32_t* abort_flag = tmem_slot + 1;
+
+    const uint32_t warp = threadIdx.x >> 5, lane = threadIdx.x & 31u;
+    if (threadIdx.x == 0) {
+        for (int s = 0; s < C::kStages; ++s) {
+            mbar_init(&full[s], kProdWarps * 32);
+            mbar_init(&empty[s], 1);
+        }
+        for (int b = 0; b < 2; ++b) {
+            mbar_init(&tfull[b], 1);
+            mbar_init(&tempty[b], 4);
+        }
+        mbar_init(drain, 1);
+        *abort_flag = 0u;
+        asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+        asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+    }
+    if (warp == kMmaWarp) {
+        asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(
+                         smem_u32(tmem_slot)),
+                     "r"(C::kTmemCols)
+                     : "memory");
+        asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;" ::: "memory");
+    }
+    tc_fence_before();
+    __syncthreads();
+    tc_fence_after();
+    const uint32_t tmem_base = *tmem_slot;
+    const uint32_t num_tiles = p.m_blocks * p.n_blocks;
+    const uint32_t ksteps = p.kc / 16;  // K-steps (16 channels) per k-block
+
+    if (warp < kProdWarps) {
+        // ---------------------------------------------------- producers
+        // A: lane covers chunk q = lane & 7 (8 channels) of row (lane >> 3) of
+        // each 4-row group; chunk q of a kc-channel run goes to K-step q/2,
+        // half q%2.  Rows with q >= kc/8 are idle for kc < 64.
+        const uint32_t q = lane & 7u, rsub = lane >> 3;
+        const bool chunk_used = q < p.kc / 8u;
+        const uint32_t j = q >> 1, h = q & 1u;
+        const char* xg = reinterpret_cast<const char*>(p.x);
+        const char* wg = reinterpret_cast<const char*>(p.w);
+        uint32_t stage = 0, phase = 0;
+        for (uint32_t tile = blockIdx.x; tile < num_tiles; tile += gridDim.x) {
+            const uint32_t mb = tile / p.n_blocks, nb = tile - mb * p.n_blocks;
+            // This lane's 8 A rows of the tile: r = (warp + 4 i) * 4 + rsub.
+            int32_t ih0[8], iw0[8];
+            uint32_t pix0[8];  // n * H * W
+            bool rvalid[8];
+#pragma unroll
+            for (int i = 0; i < 8; ++i) {
+                const uint32_t r = (warp + kProdWarps * i) * 4u + rsub;
+                const uint32_t m = mb * 128u + r;
+                rvalid[i] = m < p.M;
+                const uint32_t mm = rvalid[i] ? m : 0u;
+                const uint32_t n = mm / (p.Ho * p.Wo), rem = mm - n * p.Ho * p.Wo;
+                const uint32_t ho = rem / p.Wo, wo = rem - ho * p.Wo;
+                ih0[i] = (int32_t)(ho * p.stride) - (int32_t)p.pad;
+                iw0[i] = (int32_t)(wo * p.stride) - (int32_t)p.pad;
+                pix0[i] = n * p.H * p.W;
+            }
+            bool ok = true;
+            for (uint32_t kb = 0; kb < p.num_kb; ++kb) {
+                bool wt = true;
+                if (lane == 0) wt = mbar_wait(&empty[stage], phase ^ 1u, abort_flag, p.err);
+                if (__shfl_sync(0xffffffffu, wt ? 1 : 0, 0) == 0) {
+                    ok = false;
+                    break;
+                }
+                const uint32_t tap = kb / p.cblocks, cb = kb - tap * p.cblocks;
+                const uint32_t kh = tap / p.KW, kw = tap - kh * p.KW;
+                const uint32_t a_s = smem_u32(smem + stage * C::kStageBytes);
+                const uint32_t b_s = a_s + C::kABytes;
+                const uint32_t ch0 = cb * p.kc + q * 8u;  // first channel of this lane's chunk
+                if (chunk_used) {
+#pragma unroll
+                    for (int i = 0; i < 8; ++i) {
+                        const uint32_t r = (warp + kProdWarps * i) * 4u + rsub;
+                        const int32_t ih = ih0[i] + (int32_t)kh, iw = iw0[i] + (int32_t)kw;
+                        const bool v = rvalid[i] && ih >= 0 && ih < (int32_t)p.H && iw >= 0 &&
+                                       iw < (int32_t)p.W;
+                        const char* src =
+                            xg + ((uint64_t)(pix0[i] + (uint32_t)ih * p.W + (uint32_t)iw) * p.Cin + ch0) * 2u;
+                        const uint32_t dst =
+                            a_s + j * 4096u + r * 32u + ((h ^ ((r >> 2) & 1u)) << 4);
+                        cp_async16(dst, v ? src : xg, v ? 16u : 0u);
+                    }
+                    // B: BN rows, 4 rows per warp instruction, rows warp*4 + rsub + 16 i.
+#pragma unroll
+                    for (int i = 0; i < BN / 16; ++i) {
+                        const uint32_t r = (warp + kProdWarps * i) * 4u + rsub;
+                        const uint32_t co = nb * BN + r;
+                        const bool v = co < p.Cout;
+                        const char* src =
+                            wg + (((uint64_t)co * p.KH * p.KW + tap) * p.Cin + ch0) * 2u;
+                        const uint32_t dst =
+                            b_s + j * (uint32_t)(BN * 32) + r * 32u + ((h ^ ((r >> 2) & 1u)) << 4);
+                        cp_async16(dst, v ? src : wg, v ? 16u : 0u);
+                    }
+                }
+                cp_async_arrive(&full[stage]);
+                if (++stage == C::kStages) {
+                    stage = 0;
+                    phase ^= 1u;
+                }
+            }
+            if (!ok) break;
+        }
+        asm volatile("cp.async.wait_all;" ::: "memory");
+    } else if (warp == kMmaWarp) {
+        if (lane == 0) {
+            // ------------------------------------------------ MMA issuer
+            // kind::f16, f32 accumulate, bf16 A and B, both K-major.
+            const uint32_t idesc = (1u << 4) | (1u << 7) | (1u << 10) | ((uint32_t)(BN >> 3) << 17) |
+                                   ((128u >> 4) << 24);
+            constexpr uint64_t kmaj = smem_desc_base(16, 256);
+            uint32_t stage = 0, phase = 0, acc = 0, acc_phase = 0;
+            bool ok = true;
+            for (uint32_t tile = blockIdx.x; ok && tile < num_tiles; tile += gridDim.x) {
+                if (!mbar_wait(&tempty[acc], acc_phase ^ 1u, abort_flag, p.err)) break;
+                tc_fence_after();
+                const uint32_t d_tmem = tmem_base + acc * BN;
+                for (uint32_t kb = 0; kb < p.num_kb; ++kb) {
+                    if (!mbar_wait(&full[stage], phase, abort_flag, p.err)) {
+                        ok = false;
+                        break;
+                    }
+                    asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+                    tc_fence_after();
+                    const uint32_t a_addr = smem_u32(smem + stage * C::kStageBytes);
+                    const uint32_t b_addr = a_addr + C::kABytes;
+                    for (uint32_t s = 0; s < ksteps; ++s) {
+                        const uint64_t ad = kmaj | (uint64_t)(((a_addr + s * 4096u) >> 4) & 0x3fffu);
+                        const uint64_t bd =
+                            kmaj | (uint64_t)(((b_addr + s * (uint32_t)(BN * 32)) >> 4) & 0x3fffu);
+                        tc_mma(d_tmem, ad, bd, idesc, (kb | s) != 0u);
+                    }
+                    tc_commit(&empty[stage]);
+                    if (++stage == C::kStages) {
+                        stage = 0;
+                        phase ^= 1u;
+                    }
+                }
+                if (!ok) break;
+                tc_commit(&tfull[acc]);
+                if (++acc == 2) {
+                    acc = 0;
+                    acc_phase ^= 1u;
+                }
+            }
+            tc_commit(drain);
+            mbar_drain(drain, 0, 100000000ull);
+        }
+    } else {
+        // ---------------------------------------------------- epilogue
+        const uint32_t qd = warp & 3u;
+        const bool has_bias = p.bias != nullptr, relu = p.relu != 0;
+        uint32_t acc = 0, acc_phase = 0;
+        for (uint32_t tile = blockIdx.x; tile < num_tiles; tile += gridDim.x) {
+            const uint32_t mb = tile / p.n_blocks, nb = tile - mb * p.n_blocks;
+            bool ok = true;
+            if (lane == 0) ok = mbar_wait(&tfull[acc], acc_phase, abort_flag, p.err);
+            ok = __shfl_sync(0xffffffffu, ok ? 1 : 0, 0) != 0;
+            if (!ok) break;
+            tc_fence_after();
+            const uint32_t m = mb * 128u + qd * 32u + lane;
+            const uint32_t t_row = tmem_base + ((qd * 32u) << 16) + acc * BN;
+            uint16_t* yrow = p.y + (uint64_t)m * p.Cout;
+#pragma unroll 1
+            for (uint32_t c0 = 0; c0 < (uint32_t)BN; c0 += 16) {
+                uint32_t v[16];
+                tmem_ld16(t_row + c0, v);
+                tmem_ld_wait();
+                const uint32_t co = nb * BN + c0;
+                if (m < p.M && co < p.Cout) {
+                    uint32_t bw[8];
+                    if (has_bias) {
+                        const uint4 b0 = __ldg(reinterpret_cast<const uint4*>(p.bias + co));
+                        const uint4 b1 = __ldg(reinterpret_cast<const uint4*>(p.bias + co + 8));
+                        bw[0] = b0.x; bw[1] = b0.y; bw[2] = b0.z; bw[3] = b0.w;
+                        bw[4] = b1.x; bw[5] = b1.y; bw[6] = b1.z; bw[7] = b1.w;
+                    } else {
+#pragma unroll
+                        for (int i = 0; i < 8; ++i) bw[i] = 0u;
+                    }
+                    uint32_t o[8];
+#pragma unroll
+                    for (int i = 0; i < 8; ++i)
+                        o[i] = pack_bf16x2(epi_one(v[2 * i], bw[i] & 0xffffu, has_bias, relu),
+                                           epi_one(v[2 * i + 1], bw[i] >> 16, has_bias, relu));
+                    uint4* dst = reinterpret_cast<uint4*>(yrow + co);
+                    dst[0] = make_uint4(o[0], o[1], o[2], o[3]);
+                    dst[1] = make_uint4(o[4], o[5], o[6], o[7]);
+                }
+            }
+            tc_fence_before();
+            __syncwarp();
+            if (lane == 0) mbar_arrive(&tempty[acc]);
+            if (++acc == 2) {
+                acc = 0;
+                acc_phase ^= 1u;
+            }
+        }
+    }
+
+    tc_fence_before();
+    __syncthreads();
+    if (warp == kMmaWarp) {
+        __syncwarp();
+        tc_fence_after();
+        asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem_base),
+                     "r"(C::kTmemCols)
+                     : "memory");
+    }
+}
+
+template <int BN>
+static int launch_bn(const Params& p, cudaStream_t stream, int max_ctas) {
+    using C = Cfg<BN>;
+    static std::once_flag once;
+    static cudaError_t attr = cudaSuccess;
+    std::call_once(once, [] {
+        attr = cudaFuncSetAttribute(conv_kernel<BN>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                    C::kSmemBytes);
+    });
+    if (attr != cudaSuccess) {
+        foil_set_error(FOIL_ERR_CUDA, "foil_conv2d_nhwc: cudaFuncSetAttribute failed");
+        return FOIL_ERR_CUDA;
+    }
+    const uint32_t tiles = p.m_blocks * p.n_blocks;
+    const uint32_t grid = tiles < (uint32_t)max_ctas ? tiles : (uint32_t)max_ctas;
+    conv_kernel<BN><<<grid, kThreads, C::kSmemBytes, stream>>>(p);
+    cudaError_t e = cudaGetLastError();
+    if (e != cudaSuccess) {
+        char buf[200];
+        snprintf(buf, sizeof buf, "foil_conv2d_nhwc: launch failed: %s", cudaGetErrorString(e));
+        foil_set_error(FOIL_ERR_CUDA, buf);
+        return FOIL_ERR_CUDA;
+    }
+    foil_count_launch();
+    return FOIL_OK;
+}
+
+int launch(const uint16_t* x, const uint16_t* w, const uint16_t* bias, uint16_t* y, uint32_t N,
+           uint32_t H, uint32_t W, uint32_t Cin, uint32_t Cout, uint32_t KH, uint32_t KW,
+           uint32_t stride, uint32_t pad, int relu, uint32_t* err, cudaStream_t stream,
+           int max_ctas) {
+    Params p;
+    p.x = x;
+    p.w = w;
+    p.bias = bias;
+    p.y = y;
+    p.N = N;
+    p.H = H;
+    p.W = W;
+    p.Cin = Cin;
+    p.Cout = Cout;
+    p.KH = KH;
+    p.KW = KW;
+    p.stride = stride;
+    p.pad = pad;
+    p.Ho = (H + 2 * pad - KH) / stride + 1;
+    p.Wo = (W + 2 * pad - KW) / stride + 1;
+    p.M = N * p.Ho * p.Wo;
+    p.kc = Cin % 64 == 0 ? 64 : (Cin % 32 == 0 ? 32 : 16);
+    p.cblocks = Cin / p.kc;
+    p.num_kb = KH * KW * p.cblocks;
+    p.relu = relu;
+    p.err = err;
+    p.m_blocks = (p.M + 127) / 128;
+    // Column tile: the smallest of 64 / 128 / 256 covering Cout, else 256.
+    const int bn = Cout <= 64 ? 64 : (Cout <= 128 ? 128 : 256);
+    p.n_blocks = (Cout + bn - 1) / bn;
+    switch (bn) {
+        case 64: return launch_bn<64>(p, stream, max_ctas);
+        case 128: return launch_bn<128>(p, stream, max_ctas);
+        default: return launch_bn<256>(p, stream, max_ctas);
+    }
+}
+
+}  // namespace conv
+}  // namespace foil

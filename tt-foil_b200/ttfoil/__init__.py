@@ -93,6 +93,8 @@ SIGNATURES = {
     "foil_matmul_tiles_dev": (ctypes.c_int, [_U16P, _U16P, _U16P, ctypes.c_uint32, ctypes.c_uint32,
                                              ctypes.c_uint32, _U16P, ctypes.c_int32, _P]),
     "foil_device_error_dev": (ctypes.c_int, [_P, ctypes.POINTER(ctypes.c_uint32)]),
+    "foil_conv2d_nhwc_dev": (ctypes.c_int, [_U16P, _U16P, _U16P, _U16P] + [ctypes.c_uint32] * 9 +
+                             [ctypes.c_int32, _P]),
     "foil_matmul_tiles_noalloc_dev": (ctypes.c_int, [_U16P, _U16P, _U16P, ctypes.c_uint32,
                                                      ctypes.c_uint32, ctypes.c_uint32, _U16P,
                                                      ctypes.c_int32, _P,
@@ -175,6 +177,12 @@ def bias_add_tiles(x, bias_tiles, out, rows, cols, stream=None):
 def matmul_tiles(a, b, c, Mt, Kt, Nt, bias=None, relu=False, stream=None):
     check(lib().foil_matmul_tiles_dev(_ptr(a), _ptr(b), _ptr(c), Mt, Kt, Nt, _ptr(bias),
                                       1 if relu else 0, _stream(stream)))
+
+
+def conv2d_nhwc(x, w, bias, y, N, H, W, Cin, Cout, KH, KW, stride, pad, relu=False, stream=None):
+    """y (N,Ho,Wo,Cout) = relu?(conv(x (N,H,W,Cin), w (Cout,KH,KW,Cin)) + bias)."""
+    check(lib().foil_conv2d_nhwc_dev(_ptr(x), _ptr(w), _ptr(bias), _ptr(y), N, H, W, Cin, Cout, KH,
+                                     KW, stride, pad, 1 if relu else 0, _stream(stream)))
 
 
 def device_error(stream=None):
