@@ -38,6 +38,24 @@ __device__ __forceinline__ float host_add_f32(float a, float b) {
     return __uint_as_float(0xffc00000u);
 }
 
+// Round two fp32 values to bf16 (round to nearest even) and pack them, low
+// half = lo.  The hardware conversion gives the golden formula's result for
+// every non-NaN input (NaN becomes the canonical NaN); used where parity is
+// checked with a tolerance (GEMM / conv epilogues).
+__device__ __forceinline__ uint32_t cvt_bf16x2(float lo, float hi) {
+    uint32_t r;
+    asm("cvt.rn.bf16x2.f32 %0, %1, %2;" : "=r"(r) : "f"(hi), "f"(lo));
+    return r;
+}
+
+// relu(bf16(x)) of the goldens, decided on the fp32 x before rounding:
+// bf16(x) is negative and non-zero exactly when x < -2^-134 (half of the
+// smallest bf16 subnormal), so clamping those x to +0 and leaving the rest
+// (including values that round to -0.0) gives the same bits after rounding.
+__device__ __forceinline__ float relu_pre_round(float x) {
+    return x < -0x1p-134f ? 0.0f : x;
+}
+
 // Two bf16 in one 32-bit word (low half = first element).
 __device__ __forceinline__ uint32_t pack_bf16x2(uint32_t lo, uint32_t hi) {
     return (lo & 0xffffu) | (hi << 16);

@@ -7,6 +7,7 @@
     python -m ttfoil.kbench relu    --n 268435456
     python -m ttfoil.kbench bias    --rows 16384 --cols 16384
     python -m ttfoil.kbench copy    --bytes 1073741824
+    python -m ttfoil.kbench conv    --batch 32 --hw 112 --cin 64 --cout 128 --ksize 3 --stride 2
 
 Prints one JSON line: mean time per launch, TFLOP/s or GB/s of algorithmic
 traffic.  Used for the secondary numbers of bench.py and as the command line
@@ -81,6 +82,21 @@ def run(kind, args):
             nbytes = 4 * n
         ms = _time(torch, fn, args.iters)
         res.update(n=n, ms=ms, gbs=nbytes / ms / 1e6)
+    elif kind == "conv":
+        N, H, W, Cin, Cout, KH, stride, pad = (args.batch, args.hw, args.hw, args.cin, args.cout,
+                                               args.ksize, args.stride, args.pad)
+        Ho = (H + 2 * pad - KH) // stride + 1
+        Wo = (W + 2 * pad - KH) // stride + 1
+        x = rnd(N * H * W * Cin)
+        w = rnd(Cout * KH * KH * Cin) * 0.05
+        bias = rnd(Cout) * 0.1
+        y = torch.empty(N * Ho * Wo * Cout, dtype=torch.bfloat16, device=dev)
+        ms = _time(torch, lambda: ttfoil.conv2d_nhwc(x, w, bias, y, N, H, W, Cin, Cout, KH, KH,
+                                                       stride, pad, relu=True), args.iters)
+        flops = 2.0 * N * Ho * Wo * Cout * KH * KH * Cin
+        nbytes = 2.0 * (N * H * W * Cin + Cout * KH * KH * Cin + N * Ho * Wo * Cout)
+        res.update(N=N, H=H, W=W, Cin=Cin, Cout=Cout, k=KH, stride=stride, pad=pad, ms=ms,
+                   tflops=flops / ms / 1e9, gbs=nbytes / ms / 1e6)
     elif kind == "copy":
         nb = args.bytes
         x = torch.empty(nb // 2, dtype=torch.int16, device=dev).random_()
@@ -105,6 +121,13 @@ def main():
     ap.add_argument("--iters", type=int, default=20)
     ap.add_argument("--bias", action="store_true")
     ap.add_argument("--relu", action="store_true")
+    ap.add_argument("--batch", type=int, default=1)
+    ap.add_argument("--hw", type=int, default=56)
+    ap.add_argument("--cin", type=int, default=64)
+    ap.add_argument("--cout", type=int, default=64)
+    ap.add_argument("--ksize", type=int, default=3)
+    ap.add_argument("--stride", type=int, default=1)
+    ap.add_argument("--pad", type=int, default=1)
     args = ap.parse_args()
     if args.kernel in ("add", "relu") and args.n == 8192:
         args.n = 1 << 28
