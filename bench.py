@@ -103,6 +103,18 @@ class Dist:
 
 
 # ---------------------------------------------------------------- clocks ---
+def smi_id(cuda_index):
+    """nvidia-smi identifier of a CUDA device: its UUID (CUDA ordinals and
+    nvidia-smi indices differ when visible devices are remapped)."""
+    import torch
+    try:
+        u = str(torch.cuda.get_device_properties(cuda_index).uuid)
+        return u if u.startswith("GPU-") else "GPU-" + u
+    except Exception:
+        return str(cuda_index)
+
+
+
 class ClockSampler:
     """nvidia-smi samples of SM clock and throttle reasons during a region."""
     FIELDS = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
@@ -251,7 +263,7 @@ def run_ours(args, dist):
     torch.cuda.synchronize()
     assert ttfoil.device_error(stream) == 0
 
-    clocks = ClockSampler(dist.local)
+    clocks = ClockSampler(smi_id(dist.local))
     clocks.start()
     launches0 = ttfoil.launch_count()
     dist.barrier()
