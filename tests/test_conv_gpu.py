@@ -6,12 +6,18 @@ Tolerance (as for the GEMM): normalised error max|d| / (sqrt(K) max|x| max|w|)
 zero failures.  The fused epilogue is checked against the composition of the
 goldens relu(bf16(bf16(acc) + bias)).
 """
+import os
+import subprocess
+import sys
+
 import numpy as np
 import pytest
 
 from oracle import oracle
 
 pytestmark = pytest.mark.gpu
+
+PKG = os.path.join(os.path.dirname(os.path.dirname(os.path.abspath(__file__))), "tt-foil_b200")
 
 
 @pytest.fixture(scope="module")
@@ -112,6 +118,54 @@ def test_conv_shapes(env, N, H, W, Cin, Cout, k, stride, pad, bias, relu):
     got = run_conv(env, x, w, b, stride, pad, relu)
     exp = oracle.conv_nhwc(x, w, b, stride, pad, relu=relu, threads=8)
     check(got, exp, x, w)
+
+
+@pytest.mark.parametrize("N,H,W,Cin,Cout,kh,kw,stride,pad", [
+    (2, 12, 10, 64, 64, 3, 5, 1, 1),    # non-square kernel: W and H bounding boxes differ
+    (1, 20, 17, 64, 128, 3, 3, 3, 1),   # stride 3
+    (1, 9, 31, 192, 64, 1, 3, 2, 0),    # 1 x 3, three channel blocks
+])
+def test_conv_rectangular_and_strided(env, N, H, W, Cin, Cout, kh, kw, stride, pad):
+    x = oracle.rand_bf16((N, H, W, Cin), 11 + W)
+    w = oracle.randn_bf16((Cout, kh, kw, Cin), 12 + kw, np.sqrt(2.0 / (kh * kw * Cin)))
+    b = oracle.rand_bf16((Cout,), 13, -0.2, 0.2)
+    got = run_conv(env, x, w, b, stride, pad, relu=True)
+    exp = oracle.conv_nhwc(x, w, b, stride, pad, relu=True, threads=8)
+    check(got, exp, x, w)
+
+
+def test_producers_agree_bitwise(env, tmp_path):
+    """Cin a multiple of 64 runs the im2col tensor-copy producer; with
+    FOIL_CONV_PRODUCER=gather the same shape runs the cp.async gather
+    producer.  Both feed identical operand tiles in the same K order, so the
+    outputs are bit-identical (config-2 shape and a batch-2 stride-2 shape)."""
+    cases = [((1, 56, 56, 64), (64, 3, 3, 64), 1, 1), ((2, 30, 30, 128), (256, 3, 3, 128), 2, 1)]
+    script = tmp_path / "gather_run.py"
+    script.write_text(
+        "import sys, numpy as np, torch\n"
+        f"sys.path.insert(0, {PKG!r})\n"
+        "import ttfoil\n"
+        "d = np.load(sys.argv[1])\n"
+        "x, w, b = (torch.from_numpy(d[k].view(np.int16)).cuda() for k in ('x', 'w', 'b'))\n"
+        "N, H, W, Cin = d['x'].shape; Cout, KH, KW, _ = d['w'].shape; s, p = int(d['s']), int(d['p'])\n"
+        "Ho, Wo = (H + 2 * p - KH) // s + 1, (W + 2 * p - KW) // s + 1\n"
+        "y = torch.zeros(N * Ho * Wo * Cout, dtype=torch.int16, device='cuda')\n"
+        "ttfoil.conv2d_nhwc(x, w, b, y, N, H, W, Cin, Cout, KH, KW, s, p, relu=True)\n"
+        "torch.cuda.synchronize(); assert ttfoil.device_error() == 0\n"
+        "np.save(sys.argv[2], y.cpu().numpy())\n")
+    for i, (xs, ws, stride, pad) in enumerate(cases):
+        x = oracle.rand_bf16(xs, 40 + i)
+        w = oracle.randn_bf16(ws, 50 + i, np.sqrt(2.0 / (ws[1] * ws[2] * ws[3])))
+        b = oracle.rand_bf16((ws[0],), 60 + i, -0.1, 0.1)
+        got = run_conv(env, x, w, b, stride, pad, relu=True)
+        inp, out = tmp_path / f"in{i}.npz", tmp_path / f"out{i}.npy"
+        np.savez(inp, x=x, w=w, b=b, s=stride, p=pad)
+        env_vars = dict(os.environ, FOIL_CONV_PRODUCER="gather")
+        r = subprocess.run([sys.executable, str(script), str(inp), str(out)], env=env_vars,
+                           capture_output=True, text=True, timeout=300)
+        assert r.returncode == 0, r.stderr[-2000:]
+        ref = np.load(out).view(np.uint16).reshape(got.shape)
+        assert np.array_equal(got, ref), int(np.sum(got != ref))
 
 
 def test_conv_rejects_bad_shapes(env):

@@ -19,8 +19,18 @@
 //    K-step j holds BN rows x 32 B.
 //  Instruction: kind::f16, M = 128, N = BN, K = 16, A and B both K-major.
 //
-// Organisation: as the tiled GEMM (gemm_tc.cu): 4 producer warps (cp.async,
-// SW32 applied in the destination address), 1 MMA warp that owns TMEM
+// Two producers fill the same pipeline:
+//  * tensor-copy producer (Cin a multiple of 64): one thread issues, per
+//    k-block, an im2col tensor copy of A (128 output pixels x 64 channels of
+//    tap (kh, kw): the copy engine walks the output pixels of the tile through
+//    the bounding box [-pad, dim - 1 + pad - (k - 1)] with the conv stride as
+//    traversal stride, reads each at (w + kw, h + kh) and zero-fills padding)
+//    and a tiled copy of B (BN rows x 64 channels), both SWIZZLE_128B.  A and
+//    B are K-major with 128-byte rows; K-step j starts 32 j bytes into the
+//    1024-byte swizzle atom.
+//  * gather producer (other Cin): 4 warps of cp.async as described above,
+//    SW32 applied in the destination address.
+// Organisation otherwise as the tiled GEMM (gemm_tc.cu): 1 MMA warp that owns TMEM
 // (2 x BN fp32 accumulator columns, double-buffered).  Convolutions have short
 // K loops (9 k-blocks for 3x3x64, 2 for 1x1x128), so the epilogue sets the
 // pace: 8 epilogue warps (two per TMEM lane quadrant, each half the columns)
@@ -28,7 +38,12 @@
 // load has landed, stage their rows in padded shared memory and write each row
 // segment (contiguous in NHWC) with one bulk copy.  Every wait is bounded
 // (see gemm_ptx.cuh).
+#include <cuda.h>
+#include <cudaTypedefs.h>
+
 #include <cstdio>
+#include <cstdlib>
+#include <cstring>
 #include <mutex>
 
 #include "common.cuh"
@@ -95,8 +110,10 @@ __device__ __forceinline__ uint32_t epi_pair(uint32_t a0, uint32_t a1, uint32_t 
     return cvt_bf16x2(x0, x1);
 }
 
-template <int BN>
-__global__ void __launch_bounds__(kThreads, 1) conv_kernel(const Params p) {
+template <int BN, bool kTma>
+__global__ void __launch_bounds__(kThreads, 1)
+    conv_kernel(const Params p, const __grid_constant__ CUtensorMap tmap_x,
+                const __grid_constant__ CUtensorMap tmap_w) {
     using C = Cfg<BN>;
     extern __shared__ uint8_t smem_raw[];
     uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) &
@@ -113,7 +130,7 @@ __global__ void __launch_bounds__(kThreads, 1) conv_kernel(const Params p) {
     const uint32_t warp = threadIdx.x >> 5, lane = threadIdx.x & 31u;
     if (threadIdx.x == 0) {
         for (int s = 0; s < C::kStages; ++s) {
-            mbar_init(&full[s], kProdWarps * 32);
+            mbar_init(&full[s], kTma ? 1 : kProdWarps * 32);
             mbar_init(&empty[s], 1);
         }
         for (int b = 0; b < 2; ++b) {
@@ -139,7 +156,49 @@ __global__ void __launch_bounds__(kThreads, 1) conv_kernel(const Params p) {
     const uint32_t num_tiles = p.m_blocks * p.n_blocks;
     const uint32_t ksteps = p.kc / 16;  // K-steps (16 channels) per k-block
 
-    if (warp < kProdWarps) {
+    if (kTma && warp < kProdWarps) {
+        // ------------------------------------- tensor-copy producer (1 thread)
+        if (warp == 0 && lane == 0) {
+            tma_prefetch_map(&tmap_x);
+            tma_prefetch_map(&tmap_w);
+            const uint32_t hw = p.Ho * p.Wo;
+            uint32_t stage = 0, phase = 0;
+            bool ok = true;
+            for (uint32_t tile = blockIdx.x; ok && tile < num_tiles; tile += gridDim.x) {
+                const uint32_t mb = tile / p.n_blocks, nb = tile - mb * p.n_blocks;
+                // Base pixel (tap (0, 0)) of the tile's first output pixel.
+                const uint32_t m0 = mb * 128u, n = m0 / hw, rem = m0 - n * hw;
+                const uint32_t ho = rem / p.Wo, wo = rem - ho * p.Wo;
+                const int32_t w0 = (int32_t)(wo * p.stride) - (int32_t)p.pad;
+                const int32_t h0 = (int32_t)(ho * p.stride) - (int32_t)p.pad;
+                uint32_t kh = 0, kw = 0, cb = 0;
+                for (uint32_t kb = 0; kb < p.num_kb; ++kb) {
+                    if (!mbar_wait(&empty[stage], phase ^ 1u, abort_flag, p.err)) {
+                        ok = false;
+                        break;
+                    }
+                    const uint32_t a_s = smem_u32(smem + stage * C::kStageBytes);
+                    mbar_expect_tx(&full[stage], (uint32_t)C::kStageBytes);
+                    tma_load_im2col_4d(a_s, &tmap_x, (int32_t)(cb * 64u), w0, h0, (int32_t)n,
+                                       (uint16_t)kw, (uint16_t)kh, &full[stage]);
+                    tma_load_2d(a_s + C::kABytes, &tmap_w,
+                                (int32_t)((kh * p.KW + kw) * p.Cin + cb * 64u), (int32_t)(nb * BN),
+                                &full[stage]);
+                    if (++stage == C::kStages) {
+                        stage = 0;
+                        phase ^= 1u;
+                    }
+                    if (++cb == p.cblocks) {
+                        cb = 0;
+                        if (++kw == p.KW) {
+                            kw = 0;
+                            ++kh;
+                        }
+                    }
+                }
+            }
+        }
+    } else if (warp < kProdWarps) {
         // ---------------------------------------------------- producers
         // A: lane covers chunk q = lane & 7 (8 channels) of row (lane >> 3) of
         // each 4-row group; chunk q of a kc-channel run goes to K-step q/2,
@@ -229,7 +288,11 @@ __global__ void __launch_bounds__(kThreads, 1) conv_kernel(const Params p) {
             // kind::f16, f32 accumulate, bf16 A and B, both K-major.
             const uint32_t idesc = (1u << 4) | (1u << 7) | (1u << 10) | ((uint32_t)(BN >> 3) << 17) |
                                    ((128u >> 4) << 24);
-            constexpr uint64_t kmaj = smem_desc_base(16, 256);
+            constexpr uint64_t kmaj = kTma ? smem_desc_sw128_kmajor() : smem_desc_base(16, 256);
+            // Byte step between K-steps: 32 B inside the 128-byte swizzle rows
+            // (tensor copies) or one whole SW32 block of rows (gather).
+            constexpr uint32_t a_step = kTma ? 32u : 4096u;
+            constexpr uint32_t b_step = kTma ? 32u : (uint32_t)(BN * 32);
             uint32_t stage = 0, phase = 0, acc = 0, acc_phase = 0;
             bool ok = true;
             for (uint32_t tile = blockIdx.x; ok && tile < num_tiles; tile += gridDim.x) {
@@ -246,9 +309,8 @@ __global__ void __launch_bounds__(kThreads, 1) conv_kernel(const Params p) {
                     const uint32_t a_addr = smem_u32(smem + stage * C::kStageBytes);
                     const uint32_t b_addr = a_addr + C::kABytes;
                     for (uint32_t s = 0; s < ksteps; ++s) {
-                        const uint64_t ad = kmaj | (uint64_t)(((a_addr + s * 4096u) >> 4) & 0x3fffu);
-                        const uint64_t bd =
-                            kmaj | (uint64_t)(((b_addr + s * (uint32_t)(BN * 32)) >> 4) & 0x3fffu);
+                        const uint64_t ad = kmaj | (uint64_t)(((a_addr + s * a_step) >> 4) & 0x3fffu);
+                        const uint64_t bd = kmaj | (uint64_t)(((b_addr + s * b_step) >> 4) & 0x3fffu);
                         tc_mma(d_tmem, ad, bd, idesc, (kb | s) != 0u);
                     }
                     tc_commit(&empty[stage]);
@@ -349,13 +411,14 @@ __global__ void __launch_bounds__(kThreads, 1) conv_kernel(const Params p) {
     }
 }
 
-template <int BN>
-static int launch_bn(const Params& p, cudaStream_t stream, int max_ctas) {
+template <int BN, bool kTma>
+static int launch_bn(const Params& p, const CUtensorMap& mx, const CUtensorMap& mw,
+                     cudaStream_t stream, int max_ctas) {
     using C = Cfg<BN>;
     static std::once_flag once;
     static cudaError_t attr = cudaSuccess;
     std::call_once(once, [] {
-        attr = cudaFuncSetAttribute(conv_kernel<BN>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+        attr = cudaFuncSetAttribute(conv_kernel<BN, kTma>, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                     C::kSmemBytes);
     });
     if (attr != cudaSuccess) {
@@ -364,7 +427,7 @@ static int launch_bn(const Params& p, cudaStream_t stream, int max_ctas) {
     }
     const uint32_t tiles = p.m_blocks * p.n_blocks;
     const uint32_t grid = tiles < (uint32_t)max_ctas ? tiles : (uint32_t)max_ctas;
-    conv_kernel<BN><<<grid, kThreads, C::kSmemBytes, stream>>>(p);
+    conv_kernel<BN, kTma><<<grid, kThreads, C::kSmemBytes, stream>>>(p, mx, mw);
     cudaError_t e = cudaGetLastError();
     if (e != cudaSuccess) {
         char buf[200];
@@ -374,6 +437,79 @@ static int launch_bn(const Params& p, cudaStream_t stream, int max_ctas) {
     }
     foil_count_launch();
     return FOIL_OK;
+}
+
+template <bool kTma>
+static int launch_tiles(const Params& p, int bn, const CUtensorMap& mx, const CUtensorMap& mw,
+                        cudaStream_t stream, int max_ctas) {
+    switch (bn) {
+        case 64: return launch_bn<64, kTma>(p, mx, mw, stream, max_ctas);
+        case 128: return launch_bn<128, kTma>(p, mx, mw, stream, max_ctas);
+        default: return launch_bn<256, kTma>(p, mx, mw, stream, max_ctas);
+    }
+}
+
+// ------------------------------------------------- tensor-map encoding ---
+struct Encoders {
+    PFN_cuTensorMapEncodeIm2col im2col = nullptr;
+    PFN_cuTensorMapEncodeTiled tiled = nullptr;
+};
+
+static const Encoders& encoders() {
+    static Encoders e;
+    static std::once_flag once;
+    std::call_once(once, [] {
+        cudaDriverEntryPointQueryResult q;
+        if (cudaGetDriverEntryPoint("cuTensorMapEncodeIm2col", (void**)&e.im2col, cudaEnableDefault, &q) !=
+                cudaSuccess ||
+            q != cudaDriverEntryPointSuccess)
+            e.im2col = nullptr;
+        if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", (void**)&e.tiled, cudaEnableDefault, &q) !=
+                cudaSuccess ||
+            q != cudaDriverEntryPointSuccess)
+            e.tiled = nullptr;
+    });
+    return e;
+}
+
+// The tensor-copy producer serves Cin a multiple of 64 (one 128-byte channel
+// run per k-block) with a traversal stride the copy engine supports (<= 8)
+// and byte strides below 2^40; other shapes use the gather producer.
+// FOIL_CONV_PRODUCER=gather selects the gather producer for every shape
+// (A/B comparisons of the two producers).
+static bool use_tensor_copies(const Params& p) {
+    static const bool force_gather = [] {
+        const char* v = getenv("FOIL_CONV_PRODUCER");
+        return v && strcmp(v, "gather") == 0;
+    }();
+    return !force_gather && p.Cin % 64 == 0 && p.stride <= 8 &&
+           (uint64_t)p.H * p.W * p.Cin * 2 < (1ull << 40);
+}
+
+static bool encode_maps(const Params& p, int bn, CUtensorMap* mx, CUtensorMap* mw) {
+    const Encoders& e = encoders();
+    if (!e.im2col || !e.tiled) return false;
+    // Dims and byte strides innermost first: C, W, H, N.
+    const cuuint64_t xdim[4] = {p.Cin, p.W, p.H, p.N};
+    const cuuint64_t xstr[3] = {(cuuint64_t)p.Cin * 2, (cuuint64_t)p.W * p.Cin * 2,
+                                (cuuint64_t)p.H * p.W * p.Cin * 2};
+    // Bounding box of the base pixels (tap (0, 0)) per spatial dim, W first:
+    // [-pad, dim - 1 + pad - (k - 1)].
+    const int lower[2] = {-(int)p.pad, -(int)p.pad};
+    const int upper[2] = {(int)p.pad - (int)(p.KW - 1), (int)p.pad - (int)(p.KH - 1)};
+    const cuuint32_t trav[4] = {1, p.stride, p.stride, 1};
+    if (e.im2col(mx, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 4, const_cast<uint16_t*>(p.x), xdim, xstr, lower,
+                 upper, 64, 128, trav, CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
+                 CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) != CUDA_SUCCESS)
+        return false;
+    // Weights as a K x Cout matrix (K = KH * KW * Cin contiguous per row).
+    const cuuint64_t wdim[2] = {(cuuint64_t)p.KH * p.KW * p.Cin, p.Cout};
+    const cuuint64_t wstr[1] = {(cuuint64_t)p.KH * p.KW * p.Cin * 2};
+    const cuuint32_t box[2] = {64, (cuuint32_t)bn};
+    const cuuint32_t one[2] = {1, 1};
+    return e.tiled(mw, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, const_cast<uint16_t*>(p.w), wdim, wstr, box,
+                   one, CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
+                   CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
 }
 
 int launch(const uint16_t* x, const uint16_t* w, const uint16_t* bias, uint16_t* y, uint32_t N,
@@ -406,11 +542,15 @@ int launch(const uint16_t* x, const uint16_t* w, const uint16_t* bias, uint16_t*
     // Column tile: the smallest of 64 / 128 / 256 covering Cout, else 256.
     const int bn = Cout <= 64 ? 64 : (Cout <= 128 ? 128 : 256);
     p.n_blocks = (Cout + bn - 1) / bn;
-    switch (bn) {
-        case 64: return launch_bn<64>(p, stream, max_ctas);
-        case 128: return launch_bn<128>(p, stream, max_ctas);
-        default: return launch_bn<256>(p, stream, max_ctas);
+    alignas(64) CUtensorMap mx, mw;
+    memset(&mx, 0, sizeof mx);
+    memset(&mw, 0, sizeof mw);
+    if (!use_tensor_copies(p)) return launch_tiles<false>(p, bn, mx, mw, stream, max_ctas);
+    if (!encode_maps(p, bn, &mx, &mw)) {
+        foil_set_error(FOIL_ERR_CUDA, "foil_conv2d_nhwc: tensor-map encoding failed");
+        return FOIL_ERR_CUDA;
     }
+    return launch_tiles<true>(p, bn, mx, mw, stream, max_ctas);
 }
 
 }  // namespace conv

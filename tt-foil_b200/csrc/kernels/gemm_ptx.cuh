@@ -134,6 +134,45 @@ __host__ __device__ constexpr uint64_t smem_desc_base(uint32_t lbo, uint32_t sbo
            (1ull << 46) | (6ull << 61);
 }
 
+// K-major operand written by a SWIZZLE_128B tensor copy: rows of 128 bytes,
+// 8-row atoms 1024 bytes apart (SBO), layout type 2 = SWIZZLE_128B.  A
+// K-step of 16 bf16 (32 bytes) inside the atom advances the start address.
+__host__ __device__ constexpr uint64_t smem_desc_sw128_kmajor() {
+    return (1ull << 16) | ((uint64_t)(1024u >> 4) << 32) | (1ull << 46) | (2ull << 61);
+}
+
+// ------------------------------------------------ tensor copies (no multicast)
+// The tensor map is a __grid_constant__ kernel parameter; its generic address
+// is the operand.  Completion is signalled on `bar` as transaction bytes.
+__device__ __forceinline__ void tma_prefetch_map(const void* map) {
+    asm volatile("prefetch.tensormap [%0];" ::"l"(reinterpret_cast<uint64_t>(map)) : "memory");
+}
+
+// 2-D tiled load: box origin (x = inner element index, y = row).
+__device__ __forceinline__ void tma_load_2d(uint32_t dst, const void* map, int32_t x, int32_t y,
+                                            uint64_t* bar) {
+    asm volatile(
+        "cp.async.bulk.tensor.2d.shared::cluster.global.tile.mbarrier::complete_tx::bytes"
+        " [%0], [%1, {%2, %3}], [%4];" ::"r"(dst),
+        "l"(reinterpret_cast<uint64_t>(map)), "r"(x), "r"(y), "r"(smem_u32(bar))
+        : "memory");
+}
+
+// 4-D im2col load of an NHWC tensor (dims C, W, H, N): pixelsPerColumn
+// pixels, traversed from the base pixel (c, w, h, n) through the map's
+// bounding box, each read at (w + off_w, h + off_h); out-of-range pixels are
+// zero-filled.
+__device__ __forceinline__ void tma_load_im2col_4d(uint32_t dst, const void* map, int32_t c,
+                                                   int32_t w, int32_t h, int32_t n, uint16_t off_w,
+                                                   uint16_t off_h, uint64_t* bar) {
+    asm volatile(
+        "cp.async.bulk.tensor.4d.shared::cluster.global.im2col.mbarrier::complete_tx::bytes"
+        " [%0], [%1, {%2, %3, %4, %5}], [%6], {%7, %8};" ::"r"(dst),
+        "l"(reinterpret_cast<uint64_t>(map)), "r"(c), "r"(w), "r"(h), "r"(n), "r"(smem_u32(bar)),
+        "h"(off_w), "h"(off_h)
+        : "memory");
+}
+
 // Instruction descriptor for kind::f16: f32 accumulate (bits 4-5 = 1), bf16
 // A and B (bits 7-9, 10-12 = 1), A K-major (bit 15 = 0), B MN-major (bit 16
 // = 1), N >> 3 at bit 17, M >> 4 at bit 24.
