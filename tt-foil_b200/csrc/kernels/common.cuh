@@ -48,14 +48,6 @@ __device__ __forceinline__ uint32_t cvt_bf16x2(float lo, float hi) {
     return r;
 }
 
-// relu(bf16(x)) of the goldens, decided on the fp32 x before rounding:
-// bf16(x) is negative and non-zero exactly when x < -2^-134 (half of the
-// smallest bf16 subnormal), so clamping those x to +0 and leaving the rest
-// (including values that round to -0.0) gives the same bits after rounding.
-__device__ __forceinline__ float relu_pre_round(float x) {
-    return x < -0x1p-134f ? 0.0f : x;
-}
-
 // Two bf16 in one 32-bit word (low half = first element).
 __device__ __forceinline__ uint32_t pack_bf16x2(uint32_t lo, uint32_t hi) {
     return (lo & 0xffffu) | (hi << 16);

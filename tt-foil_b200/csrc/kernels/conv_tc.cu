@@ -35,8 +35,10 @@
 // K loops (9 k-blocks for 3x3x64, 2 for 1x1x128), so the epilogue sets the
 // pace: 8 epilogue warps (two per TMEM lane quadrant, each half the columns)
 // read 32 columns per TMEM load, release the accumulator as soon as their last
-// load has landed, stage their rows in padded shared memory and write each row
-// segment (contiguous in NHWC) with one bulk copy.  Every wait is bounded
+// load has landed, stage their 32 rows in swizzled shared memory and write
+// them with one 2-D tensor store per box.  (One bulk copy per output row, 256
+// per tile, queued behind each other on the copy engine and set the pace of
+// the 1x1 convolution at ~2.8 us per 128 x 256 tile.)  Every wait is bounded
 // (see gemm_ptx.cuh).
 #include <cuda.h>
 #include <cudaTypedefs.h>
@@ -83,8 +85,12 @@ struct Cfg {
     static constexpr int kABytes = 128 * 128;               // 128 rows x 64 ch x 2 B (max kc)
     static constexpr int kBBytes = BN * 128;                // BN rows x 64 ch x 2 B
     static constexpr int kStageBytes = kABytes + kBBytes;
-    static constexpr int kPitch = BN + 16;                  // staging row: BN/2 bf16 + 16 B pad
-    static constexpr int kStagingBytes = kEpiWarps * 32 * kPitch;
+    // Epilogue staging: per warp 32 rows x BN/2 columns, as boxes of kBoxC
+    // columns (128-byte rows, SWIZZLE_128B; 64-byte rows, SWIZZLE_64B for BN 64).
+    static constexpr int kBoxC = BN >= 128 ? 64 : 32;
+    static constexpr int kBoxBytes = 32 * kBoxC * 2;
+    static constexpr int kWarpStaging = 32 * BN;            // 32 rows x BN/2 bf16
+    static constexpr int kStagingBytes = kEpiWarps * kWarpStaging;
     static constexpr int kLimit = 220 * 1024;
     static constexpr int kFit = (kLimit - kStagingBytes - 1280) / kStageBytes;
     static constexpr int kStages = kFit > 8 ? 8 : kFit;
@@ -92,28 +98,32 @@ struct Cfg {
     static constexpr int kTmemCols = 2 * BN;                // power of two for BN in {64,128,256}
 };
 
-// Two accumulators (columns c, c+1 of one row) -> packed bf16x2 of
-// relu?(bf16(bf16(acc) + bias)), the composition of the reference goldens
-// (matmul, bias_add, relu), with hardware round-to-nearest-even conversions.
-__device__ __forceinline__ uint32_t epi_pair(uint32_t a0, uint32_t a1, uint32_t bias2,
-                                             bool has_bias, bool relu) {
-    float x0 = __uint_as_float(a0), x1 = __uint_as_float(a1);
-    if (has_bias) {
-        const uint32_t r = cvt_bf16x2(x0, x1);  // bf16(acc)
-        x0 = __fadd_rn(__uint_as_float(r << 16), __uint_as_float(bias2 << 16));
-        x1 = __fadd_rn(__uint_as_float(r & 0xffff0000u), __uint_as_float(bias2 & 0xffff0000u));
-    }
-    if (relu) {
-        x0 = relu_pre_round(x0);
-        x1 = relu_pre_round(x1);
-    }
-    return cvt_bf16x2(x0, x1);
+// Epilogue modes: 0 = bf16(acc); 1 = bf16(bf16(acc) + bias);
+// 2 = relu(bf16(bf16(acc) + bias)) (bias 0 when absent).
+//
+// Two accumulators (columns c, c+1 of one row) -> packed bf16x2, the
+// composition of the reference goldens (matmul, bias_add, relu).  bf16(acc) is
+// one round-to-nearest-even conversion; the bias add is a packed bf16 fma
+// r * 1 + bias, rounded once.  That equals the golden's fp32 add followed by
+// bf16 rounding: the sum of two bf16 values is either exact in fp32 or
+// differs from a bf16 value by far less than half a bf16 ulp, so the fp32
+// rounding never creates a bf16 tie.  The .relu form clamps negative results
+// to +0 (the golden's float comparison treats -0 and +0 alike).
+__device__ __forceinline__ uint32_t epi_pair(uint32_t a0, uint32_t a1, uint32_t bias2, int mode) {
+    const uint32_t r = cvt_bf16x2(__uint_as_float(a0), __uint_as_float(a1));
+    if (mode == 0) return r;
+    uint32_t d;
+    if (mode == 1)
+        asm("fma.rn.bf16x2 %0, %1, %2, %3;" : "=r"(d) : "r"(r), "r"(0x3f803f80u), "r"(bias2));
+    else
+        asm("fma.rn.relu.bf16x2 %0, %1, %2, %3;" : "=r"(d) : "r"(r), "r"(0x3f803f80u), "r"(bias2));
+    return d;
 }
 
 template <int BN, bool kTma>
 __global__ void __launch_bounds__(kThreads, 1)
     conv_kernel(const Params p, const __grid_constant__ CUtensorMap tmap_x,
-                const __grid_constant__ CUtensorMap tmap_w) {
+                const __grid_constant__ CUtensorMap tmap_w, const __grid_constant__ CUtensorMap tmap_y) {
     using C = Cfg<BN>;
     extern __shared__ uint8_t smem_raw[];
     uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) &
@@ -333,12 +343,15 @@ __global__ void __launch_bounds__(kThreads, 1)
         // ---------------------------------------------------- epilogue
         // Warp e (0..7) reads TMEM lane quadrant warp % 4 (rows qd*32 + lane)
         // and columns [half * BN/2, (half + 1) * BN/2).  Each lane converts its
-        // row into a padded staging row in shared memory, then writes the row
-        // segment with one bulk copy (contiguous in NHWC).
+        // row into swizzled staging boxes (32 rows x kBoxC columns) and lane 0
+        // writes each box with one 2-D tensor store into y viewed as an
+        // M x Cout matrix; the copy engine clips rows >= M and columns >= Cout.
         const uint32_t e = warp - 5u, qd = warp & 3u, half = e >> 2;
         const uint32_t col0 = half * (uint32_t)(BN / 2);
-        const uint32_t stg_row = smem_u32(staging) + (e * 32u + lane) * (uint32_t)C::kPitch;
-        const bool has_bias = p.bias != nullptr, relu = p.relu != 0;
+        const uint32_t stg = smem_u32(staging) + e * (uint32_t)C::kWarpStaging;
+        const bool has_bias = p.bias != nullptr;
+        const int mode = p.relu ? 2 : (has_bias ? 1 : 0);
+        if (lane == 0) tma_prefetch_map(&tmap_y);
         uint32_t acc = 0, acc_phase = 0;
         for (uint32_t tile = blockIdx.x; tile < num_tiles; tile += gridDim.x) {
             const uint32_t mb = tile / p.n_blocks, nb = tile - mb * p.n_blocks;
@@ -347,8 +360,10 @@ __global__ void __launch_bounds__(kThreads, 1)
             ok = __shfl_sync(0xffffffffu, ok ? 1 : 0, 0) != 0;
             if (!ok) break;
             tc_fence_after();
-            bulk_wait_read();  // the previous tile's stores no longer read the staging row
-            const uint32_t m = mb * 128u + qd * 32u + lane;
+            // The previous tile's stores (issued by lane 0) no longer read the staging.
+            if (lane == 0) bulk_wait_read();
+            __syncwarp();
+            const uint32_t m0 = mb * 128u + qd * 32u;
             const uint32_t t_row = tmem_base + ((qd * 32u) << 16) + acc * BN + col0;
             const uint32_t co0 = nb * BN + col0;
 #pragma unroll 1
@@ -376,28 +391,47 @@ __global__ void __launch_bounds__(kThreads, 1)
                     for (int i = 0; i < 16; ++i) bw[i] = 0u;
                 }
                 uint32_t o[16];
+                if (mode == 0) {
 #pragma unroll
-                for (int i = 0; i < 16; ++i) o[i] = epi_pair(v[2 * i], v[2 * i + 1], bw[i], has_bias, relu);
-                const uint32_t sdst = stg_row + c * 2u;
+                    for (int i = 0; i < 16; ++i) o[i] = epi_pair(v[2 * i], v[2 * i + 1], 0u, 0);
+                } else if (mode == 1) {
+#pragma unroll
+                    for (int i = 0; i < 16; ++i) o[i] = epi_pair(v[2 * i], v[2 * i + 1], bw[i], 1);
+                } else {
+#pragma unroll
+                    for (int i = 0; i < 16; ++i) o[i] = epi_pair(v[2 * i], v[2 * i + 1], bw[i], 2);
+                }
+                // Row `lane` of box c / kBoxC; 16-byte chunk k of the row lands at
+                // chunk k ^ (row bits) of the swizzle atom (128B: lane & 7;
+                // 64B: (lane >> 1) & 3).
+                const uint32_t box = stg + (c / (uint32_t)C::kBoxC) * (uint32_t)C::kBoxBytes;
+                const uint32_t k0 = ((c % (uint32_t)C::kBoxC) * 2u) >> 4;
+                const uint32_t row = box + lane * (uint32_t)(C::kBoxC * 2);
+                const uint32_t sw = C::kBoxC == 64 ? (lane & 7u) : ((lane >> 1) & 3u);
 #pragma unroll
                 for (int i = 0; i < 4; ++i)
-                    asm volatile("st.shared.v4.b32 [%0], {%1, %2, %3, %4};" ::"r"(sdst + 16u * i),
+                    asm volatile("st.shared.v4.b32 [%0], {%1, %2, %3, %4};" ::"r"(
+                                     row + (((k0 + i) ^ sw) << 4)),
                                  "r"(o[4 * i]), "r"(o[4 * i + 1]), "r"(o[4 * i + 2]), "r"(o[4 * i + 3])
                                  : "memory");
             }
-            // Generic-proxy writes above, async-proxy (bulk copy) read below.
+            // Generic-proxy writes above, async-proxy (tensor store) reads below.
             asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
-            if (m < p.M && co0 < p.Cout) {
-                const uint32_t cols = min((uint32_t)(BN / 2), p.Cout - co0);
-                bulk_store(p.y + (uint64_t)m * p.Cout + co0, stg_row, cols * 2u);
+            __syncwarp();
+            if (lane == 0 && m0 < p.M) {
+#pragma unroll 1
+                for (uint32_t b = 0; b < (uint32_t)(BN / 2 / C::kBoxC); ++b) {
+                    const uint32_t x = co0 + b * (uint32_t)C::kBoxC;
+                    if (x < p.Cout) tma_store_2d(&tmap_y, (int32_t)x, (int32_t)m0, stg + b * (uint32_t)C::kBoxBytes);
+                }
             }
-            bulk_commit();
+            if (lane == 0) bulk_commit();
             if (++acc == 2) {
                 acc = 0;
                 acc_phase ^= 1u;
             }
         }
-        bulk_wait_all();
+        if (lane == 0) bulk_wait_all();
     }
 
     tc_fence_before();
@@ -413,7 +447,7 @@ __global__ void __launch_bounds__(kThreads, 1)
 
 template <int BN, bool kTma>
 static int launch_bn(const Params& p, const CUtensorMap& mx, const CUtensorMap& mw,
-                     cudaStream_t stream, int max_ctas) {
+                     const CUtensorMap& my, cudaStream_t stream, int max_ctas) {
     using C = Cfg<BN>;
     static std::once_flag once;
     static cudaError_t attr = cudaSuccess;
@@ -427,7 +461,7 @@ static int launch_bn(const Params& p, const CUtensorMap& mx, const CUtensorMap& 
     }
     const uint32_t tiles = p.m_blocks * p.n_blocks;
     const uint32_t grid = tiles < (uint32_t)max_ctas ? tiles : (uint32_t)max_ctas;
-    conv_kernel<BN, kTma><<<grid, kThreads, C::kSmemBytes, stream>>>(p, mx, mw);
+    conv_kernel<BN, kTma><<<grid, kThreads, C::kSmemBytes, stream>>>(p, mx, mw, my);
     cudaError_t e = cudaGetLastError();
     if (e != cudaSuccess) {
         char buf[200];
@@ -441,11 +475,11 @@ static int launch_bn(const Params& p, const CUtensorMap& mx, const CUtensorMap& 
 
 template <bool kTma>
 static int launch_tiles(const Params& p, int bn, const CUtensorMap& mx, const CUtensorMap& mw,
-                        cudaStream_t stream, int max_ctas) {
+                        const CUtensorMap& my, cudaStream_t stream, int max_ctas) {
     switch (bn) {
-        case 64: return launch_bn<64, kTma>(p, mx, mw, stream, max_ctas);
-        case 128: return launch_bn<128, kTma>(p, mx, mw, stream, max_ctas);
-        default: return launch_bn<256, kTma>(p, mx, mw, stream, max_ctas);
+        case 64: return launch_bn<64, kTma>(p, mx, mw, my, stream, max_ctas);
+        case 128: return launch_bn<128, kTma>(p, mx, mw, my, stream, max_ctas);
+        default: return launch_bn<256, kTma>(p, mx, mw, my, stream, max_ctas);
     }
 }
 
@@ -484,6 +518,22 @@ static bool use_tensor_copies(const Params& p) {
     }();
     return !force_gather && p.Cin % 64 == 0 && p.stride <= 8 &&
            (uint64_t)p.H * p.W * p.Cin * 2 < (1ull << 40);
+}
+
+// Output y as an M x Cout matrix, stored in boxes of 32 rows x (64 or 32)
+// columns from the epilogue's swizzled staging.
+static bool encode_output_map(const Params& p, int bn, CUtensorMap* my) {
+    const Encoders& e = encoders();
+    if (!e.tiled) return false;
+    const uint32_t boxc = bn >= 128 ? 64 : 32;
+    const cuuint64_t ydim[2] = {p.Cout, p.M};
+    const cuuint64_t ystr[1] = {(cuuint64_t)p.Cout * 2};
+    const cuuint32_t box[2] = {boxc, 32};
+    const cuuint32_t one[2] = {1, 1};
+    return e.tiled(my, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, p.y, ydim, ystr, box, one,
+                   CU_TENSOR_MAP_INTERLEAVE_NONE,
+                   boxc == 64 ? CU_TENSOR_MAP_SWIZZLE_128B : CU_TENSOR_MAP_SWIZZLE_64B,
+                   CU_TENSOR_MAP_L2_PROMOTION_NONE, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
 }
 
 static bool encode_maps(const Params& p, int bn, CUtensorMap* mx, CUtensorMap* mw) {
@@ -542,15 +592,16 @@ int launch(const uint16_t* x, const uint16_t* w, const uint16_t* bias, uint16_t*
     // Column tile: the smallest of 64 / 128 / 256 covering Cout, else 256.
     const int bn = Cout <= 64 ? 64 : (Cout <= 128 ? 128 : 256);
     p.n_blocks = (Cout + bn - 1) / bn;
-    alignas(64) CUtensorMap mx, mw;
+    alignas(64) CUtensorMap mx, mw, my;
     memset(&mx, 0, sizeof mx);
     memset(&mw, 0, sizeof mw);
-    if (!use_tensor_copies(p)) return launch_tiles<false>(p, bn, mx, mw, stream, max_ctas);
-    if (!encode_maps(p, bn, &mx, &mw)) {
+    const bool tc = use_tensor_copies(p);
+    if (!encode_output_map(p, bn, &my) || (tc && !encode_maps(p, bn, &mx, &mw))) {
         foil_set_error(FOIL_ERR_CUDA, "foil_conv2d_nhwc: tensor-map encoding failed");
         return FOIL_ERR_CUDA;
     }
-    return launch_tiles<true>(p, bn, mx, mw, stream, max_ctas);
+    if (!tc) return launch_tiles<false>(p, bn, mx, mw, my, stream, max_ctas);
+    return launch_tiles<true>(p, bn, mx, mw, my, stream, max_ctas);
 }
 
 }  // namespace conv

@@ -173,6 +173,15 @@ __device__ __forceinline__ void tma_load_im2col_4d(uint32_t dst, const void* map
         : "memory");
 }
 
+// 2-D tiled store from shared memory (bulk group of this thread); elements of
+// the box outside the tensor are not written.  Coordinates must be >= 0.
+__device__ __forceinline__ void tma_store_2d(const void* map, int32_t x, int32_t y, uint32_t src) {
+    asm volatile("cp.async.bulk.tensor.2d.global.shared::cta.bulk_group [%0, {%1, %2}], [%3];" ::"l"(
+                     reinterpret_cast<uint64_t>(map)),
+                 "r"(x), "r"(y), "r"(src)
+                 : "memory");
+}
+
 // Instruction descriptor for kind::f16: f32 accumulate (bits 4-5 = 1), bf16
 // A and B (bits 7-9, 10-12 = 1), A K-major (bit 15 = 0), B MN-major (bit 16
 // = 1), N >> 3 at bit 17, M >> 4 at bit 24.
