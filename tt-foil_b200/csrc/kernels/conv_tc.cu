@@ -35,8 +35,8 @@
 // K loops (9 k-blocks for 3x3x64, 2 for 1x1x128), so the epilogue sets the
 // pace: 8 epilogue warps (two per TMEM lane quadrant, each half the columns)
 // read 32 columns per TMEM load, release the accumulator as soon as their last
-// load has landed, stage their 32 rows in swizzled shared memory and write
-// them with one 2-D tensor store per box.  (One bulk copy per output row, 256
+// load has landed, stage each 32 x 32 chunk in swizzled shared memory and
+// write it at once with one 2-D tensor store.  (One bulk copy per output row, 256
 // per tile, queued behind each other on the copy engine and set the pace of
 // the 1x1 convolution at ~2.8 us per 128 x 256 tile.)  Every wait is bounded
 // (see gemm_ptx.cuh).
@@ -85,11 +85,11 @@ struct Cfg {
     static constexpr int kABytes = 128 * 128;               // 128 rows x 64 ch x 2 B (max kc)
     static constexpr int kBBytes = BN * 128;                // BN rows x 64 ch x 2 B
     static constexpr int kStageBytes = kABytes + kBBytes;
-    // Epilogue staging: per warp 32 rows x BN/2 columns, as boxes of kBoxC
-    // columns (128-byte rows, SWIZZLE_128B; 64-byte rows, SWIZZLE_64B for BN 64).
-    static constexpr int kBoxC = BN >= 128 ? 64 : 32;
-    static constexpr int kBoxBytes = 32 * kBoxC * 2;
-    static constexpr int kWarpStaging = 32 * BN;            // 32 rows x BN/2 bf16
+    // Epilogue staging: per warp 32 rows x BN/2 columns, as kChunks boxes of
+    // 32 rows x 32 columns (64-byte rows, SWIZZLE_64B), one per TMEM load.
+    static constexpr int kChunks = BN / 64;
+    static constexpr int kBoxBytes = 32 * 32 * 2;
+    static constexpr int kWarpStaging = kChunks * kBoxBytes;  // 32 rows x BN/2 bf16
     static constexpr int kStagingBytes = kEpiWarps * kWarpStaging;
     static constexpr int kLimit = 220 * 1024;
     static constexpr int kFit = (kLimit - kStagingBytes - 1280) / kStageBytes;
@@ -342,15 +342,20 @@ __global__ void __launch_bounds__(kThreads, 1)
     } else {
         // ---------------------------------------------------- epilogue
         // Warp e (0..7) reads TMEM lane quadrant warp % 4 (rows qd*32 + lane)
-        // and columns [half * BN/2, (half + 1) * BN/2).  Each lane converts its
-        // row into swizzled staging boxes (32 rows x kBoxC columns) and lane 0
-        // writes each box with one 2-D tensor store into y viewed as an
-        // M x Cout matrix; the copy engine clips rows >= M and columns >= Cout.
+        // and columns [half * BN/2, (half + 1) * BN/2), 32 at a time.  Each
+        // chunk is converted into its own swizzled staging box (32 rows x 32
+        // columns) and stored at once by lane 0 with a 2-D tensor store into y
+        // viewed as an M x Cout matrix (the copy engine clips rows >= M and
+        // columns >= Cout), one bulk group per chunk.  Box j is rewritten one
+        // tile later, after waiting until at most kChunks - 1 newer groups are
+        // still reading shared memory, i.e. box j's previous store has.
         const uint32_t e = warp - 5u, qd = warp & 3u, half = e >> 2;
         const uint32_t col0 = half * (uint32_t)(BN / 2);
         const uint32_t stg = smem_u32(staging) + e * (uint32_t)C::kWarpStaging;
         const bool has_bias = p.bias != nullptr;
         const int mode = p.relu ? 2 : (has_bias ? 1 : 0);
+        // Swizzle of row `lane` in a 64-byte-row box: 16-byte chunk k lands at k ^ sw.
+        const uint32_t row_off = lane * 64u, sw = (lane >> 1) & 3u;
         if (lane == 0) tma_prefetch_map(&tmap_y);
         uint32_t acc = 0, acc_phase = 0;
         for (uint32_t tile = blockIdx.x; tile < num_tiles; tile += gridDim.x) {
@@ -360,26 +365,15 @@ __global__ void __launch_bounds__(kThreads, 1)
             ok = __shfl_sync(0xffffffffu, ok ? 1 : 0, 0) != 0;
             if (!ok) break;
             tc_fence_after();
-            // The previous tile's stores (issued by lane 0) no longer read the staging.
-            if (lane == 0) bulk_wait_read();
-            __syncwarp();
             const uint32_t m0 = mb * 128u + qd * 32u;
             const uint32_t t_row = tmem_base + ((qd * 32u) << 16) + acc * BN + col0;
             const uint32_t co0 = nb * BN + col0;
-#pragma unroll 1
-            for (uint32_t c = 0; c < (uint32_t)(BN / 2); c += 32) {
-                uint32_t v[32];
-                tmem_ld32(t_row + c, v);
-                tmem_ld_wait();
-                if (c + 32 >= (uint32_t)(BN / 2)) {
-                    // Last TMEM read of this tile by this warp: release the accumulator.
-                    tc_fence_before();
-                    __syncwarp();
-                    if (lane == 0) mbar_arrive(&tempty[acc]);
-                }
-                const uint32_t co = co0 + c;
+#pragma unroll
+            for (int ci = 0; ci < C::kChunks; ++ci) {
+                const uint32_t co = co0 + 32u * ci;
+                // Bias first: its load latency overlaps the TMEM load.
                 uint32_t bw[16];
-                if (has_bias && co < p.Cout) {
+                if (mode != 0 && has_bias && co < p.Cout) {
                     const uint4* bp = reinterpret_cast<const uint4*>(p.bias + co);
 #pragma unroll
                     for (int i = 0; i < 4; ++i) {
@@ -389,6 +383,15 @@ __global__ void __launch_bounds__(kThreads, 1)
                 } else {
 #pragma unroll
                     for (int i = 0; i < 16; ++i) bw[i] = 0u;
+                }
+                uint32_t v[32];
+                tmem_ld32(t_row + 32u * ci, v);
+                tmem_ld_wait();
+                if (ci + 1 == C::kChunks) {
+                    // Last TMEM read of this tile by this warp: release the accumulator.
+                    tc_fence_before();
+                    __syncwarp();
+                    if (lane == 0) mbar_arrive(&tempty[acc]);
                 }
                 uint32_t o[16];
                 if (mode == 0) {
@@ -401,31 +404,23 @@ __global__ void __launch_bounds__(kThreads, 1)
 #pragma unroll
                     for (int i = 0; i < 16; ++i) o[i] = epi_pair(v[2 * i], v[2 * i + 1], bw[i], 2);
                 }
-                // Row `lane` of box c / kBoxC; 16-byte chunk k of the row lands at
-                // chunk k ^ (row bits) of the swizzle atom (128B: lane & 7;
-                // 64B: (lane >> 1) & 3).
-                const uint32_t box = stg + (c / (uint32_t)C::kBoxC) * (uint32_t)C::kBoxBytes;
-                const uint32_t k0 = ((c % (uint32_t)C::kBoxC) * 2u) >> 4;
-                const uint32_t row = box + lane * (uint32_t)(C::kBoxC * 2);
-                const uint32_t sw = C::kBoxC == 64 ? (lane & 7u) : ((lane >> 1) & 3u);
+                const uint32_t box = stg + (uint32_t)(ci * C::kBoxBytes);
+                if (lane == 0) bulk_wait_read_n<C::kChunks - 1>();
+                __syncwarp();
 #pragma unroll
                 for (int i = 0; i < 4; ++i)
                     asm volatile("st.shared.v4.b32 [%0], {%1, %2, %3, %4};" ::"r"(
-                                     row + (((k0 + i) ^ sw) << 4)),
+                                     box + row_off + (((uint32_t)i ^ sw) << 4)),
                                  "r"(o[4 * i]), "r"(o[4 * i + 1]), "r"(o[4 * i + 2]), "r"(o[4 * i + 3])
                                  : "memory");
-            }
-            // Generic-proxy writes above, async-proxy (tensor store) reads below.
-            asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
-            __syncwarp();
-            if (lane == 0 && m0 < p.M) {
-#pragma unroll 1
-                for (uint32_t b = 0; b < (uint32_t)(BN / 2 / C::kBoxC); ++b) {
-                    const uint32_t x = co0 + b * (uint32_t)C::kBoxC;
-                    if (x < p.Cout) tma_store_2d(&tmap_y, (int32_t)x, (int32_t)m0, stg + b * (uint32_t)C::kBoxBytes);
+                // Generic-proxy writes above, async-proxy (tensor store) reads below.
+                asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+                __syncwarp();
+                if (lane == 0) {
+                    if (m0 < p.M && co < p.Cout) tma_store_2d(&tmap_y, (int32_t)co, (int32_t)m0, box);
+                    bulk_commit();
                 }
             }
-            if (lane == 0) bulk_commit();
             if (++acc == 2) {
                 acc = 0;
                 acc_phase ^= 1u;
@@ -520,19 +515,17 @@ static bool use_tensor_copies(const Params& p) {
            (uint64_t)p.H * p.W * p.Cin * 2 < (1ull << 40);
 }
 
-// Output y as an M x Cout matrix, stored in boxes of 32 rows x (64 or 32)
-// columns from the epilogue's swizzled staging.
-static bool encode_output_map(const Params& p, int bn, CUtensorMap* my) {
+// Output y as an M x Cout matrix, stored in boxes of 32 rows x 32 columns
+// from the epilogue's swizzled staging.
+static bool encode_output_map(const Params& p, CUtensorMap* my) {
     const Encoders& e = encoders();
     if (!e.tiled) return false;
-    const uint32_t boxc = bn >= 128 ? 64 : 32;
     const cuuint64_t ydim[2] = {p.Cout, p.M};
     const cuuint64_t ystr[1] = {(cuuint64_t)p.Cout * 2};
-    const cuuint32_t box[2] = {boxc, 32};
+    const cuuint32_t box[2] = {32, 32};
     const cuuint32_t one[2] = {1, 1};
     return e.tiled(my, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, p.y, ydim, ystr, box, one,
-                   CU_TENSOR_MAP_INTERLEAVE_NONE,
-                   boxc == 64 ? CU_TENSOR_MAP_SWIZZLE_128B : CU_TENSOR_MAP_SWIZZLE_64B,
+                   CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_64B,
                    CU_TENSOR_MAP_L2_PROMOTION_NONE, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
 }
 
@@ -596,7 +589,7 @@ int launch(const uint16_t* x, const uint16_t* w, const uint16_t* bias, uint16_t*
     memset(&mx, 0, sizeof mx);
     memset(&mw, 0, sizeof mw);
     const bool tc = use_tensor_copies(p);
-    if (!encode_output_map(p, bn, &my) || (tc && !encode_maps(p, bn, &mx, &mw))) {
+    if (!encode_output_map(p, &my) || (tc && !encode_maps(p, bn, &mx, &mw))) {
         foil_set_error(FOIL_ERR_CUDA, "foil_conv2d_nhwc: tensor-map encoding failed");
         return FOIL_ERR_CUDA;
     }

@@ -219,6 +219,12 @@ __device__ __forceinline__ void bulk_commit() {
 __device__ __forceinline__ void bulk_wait_read() {
     asm volatile("cp.async.bulk.wait_group.read 0;" ::: "memory");
 }
+// Wait until at most N of this thread's most recent bulk groups still read
+// their shared source.
+template <int N>
+__device__ __forceinline__ void bulk_wait_read_n() {
+    asm volatile("cp.async.bulk.wait_group.read %0;" ::"n"(N) : "memory");
+}
 // Wait until this thread's bulk copies are complete.
 __device__ __forceinline__ void bulk_wait_all() {
     asm volatile("cp.async.bulk.wait_group 0;" ::: "memory");
