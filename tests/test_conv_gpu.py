@@ -124,6 +124,10 @@ def test_conv_shapes(env, N, H, W, Cin, Cout, k, stride, pad, bias, relu):
     (2, 12, 10, 64, 64, 3, 5, 1, 1),    # non-square kernel: W and H bounding boxes differ
     (1, 20, 17, 64, 128, 3, 3, 3, 1),   # stride 3
     (1, 9, 31, 192, 64, 1, 3, 2, 0),    # 1 x 3, three channel blocks
+    # 2-SM weight-stationary kernel (Cin % 64 == 0, Cout <= 256, M > 128):
+    (3, 10, 10, 64, 192, 3, 3, 1, 1),   # M = 300: the second pair's odd CTA has no valid row
+    (2, 14, 14, 256, 64, 3, 3, 1, 1),   # K = 2304: 144 KiB of resident weights, 4 A stages
+    (1, 23, 29, 128, 128, 3, 3, 2, 1),  # M = 180, stride 2, odd sizes
 ])
 def test_conv_rectangular_and_strided(env, N, H, W, Cin, Cout, kh, kw, stride, pad):
     x = oracle.rand_bf16((N, H, W, Cin), 11 + W)
@@ -134,11 +138,14 @@ def test_conv_rectangular_and_strided(env, N, H, W, Cin, Cout, kh, kw, stride, p
     check(got, exp, x, w)
 
 
-def test_producers_agree_bitwise(env, tmp_path):
-    """Cin a multiple of 64 runs the im2col tensor-copy producer; with
-    FOIL_CONV_PRODUCER=gather the same shape runs the cp.async gather
-    producer.  Both feed identical operand tiles in the same K order, so the
-    outputs are bit-identical (config-2 shape and a batch-2 stride-2 shape)."""
+@pytest.mark.parametrize("variant", ["gather", "single"])
+def test_kernel_variants_agree_bitwise(env, tmp_path, variant):
+    """Cin a multiple of 64 and Cout <= 256 runs the 2-SM weight-stationary
+    kernel with tensor copies; FOIL_CONV_PRODUCER=single runs the same shape
+    on the single-CTA kernel with tensor copies, =gather with the cp.async
+    gather producer.  All feed identical operand tiles in the same K order, so
+    the outputs are bit-identical (config-2 shape and a batch-2 stride-2
+    shape)."""
     cases = [((1, 56, 56, 64), (64, 3, 3, 64), 1, 1), ((2, 30, 30, 128), (256, 3, 3, 128), 2, 1)]
     script = tmp_path / "gather_run.py"
     script.write_text(
@@ -160,7 +167,7 @@ def test_producers_agree_bitwise(env, tmp_path):
         got = run_conv(env, x, w, b, stride, pad, relu=True)
         inp, out = tmp_path / f"in{i}.npz", tmp_path / f"out{i}.npy"
         np.savez(inp, x=x, w=w, b=b, s=stride, p=pad)
-        env_vars = dict(os.environ, FOIL_CONV_PRODUCER="gather")
+        env_vars = dict(os.environ, FOIL_CONV_PRODUCER=variant)
         r = subprocess.run([sys.executable, str(script), str(inp), str(out)], env=env_vars,
                            capture_output=True, text=True, timeout=300)
         assert r.returncode == 0, r.stderr[-2000:]

@@ -32,14 +32,19 @@
 //    SW32 applied in the destination address.
 // Organisation otherwise as the tiled GEMM (gemm_tc.cu): 1 MMA warp that owns TMEM
 // (2 x BN fp32 accumulator columns, double-buffered).  Convolutions have short
-// K loops (9 k-blocks for 3x3x64, 2 for 1x1x128), so the epilogue sets the
-// pace: 8 epilogue warps (two per TMEM lane quadrant, each half the columns)
-// read 32 columns per TMEM load, release the accumulator as soon as their last
-// load has landed, stage each 32 x 32 chunk in swizzled shared memory and
-// write it at once with one 2-D tensor store.  (One bulk copy per output row, 256
-// per tile, queued behind each other on the copy engine and set the pace of
-// the 1x1 convolution at ~2.8 us per 128 x 256 tile.)  Every wait is bounded
-// (see gemm_ptx.cuh).
+// K loops (9 k-blocks for 3x3x64, 2 for 1x1x128), so the epilogue matters:
+// 8 epilogue warps (two per TMEM lane quadrant, each half the columns) read 32
+// columns per TMEM load, release the accumulator as soon as their last load
+// has landed, and write through shared memory with coalesced stores (see
+// epilogue_rows).
+//
+// Throughput limits measured on B200 that shaped this file: the tensor-copy
+// engine of an SM issues about one row request (<= 128 bytes) per 3 cycles
+// for tiled copies (~81 GB/s per SM with 128-byte rows, independent of how
+// many SMs run or how many copies are in flight) and one per ~4.3 cycles for
+// im2col copies (~56 GB/s per SM).  Weights are therefore kept resident where
+// they fit (conv_pair_kernel), so that only A crosses per k-block.  Every
+// wait is bounded (see gemm_ptx.cuh).
 #include <cuda.h>
 #include <cudaTypedefs.h>
 
@@ -85,11 +90,8 @@ struct Cfg {
     static constexpr int kABytes = 128 * 128;               // 128 rows x 64 ch x 2 B (max kc)
     static constexpr int kBBytes = BN * 128;                // BN rows x 64 ch x 2 B
     static constexpr int kStageBytes = kABytes + kBBytes;
-    // Epilogue staging: per warp 32 rows x BN/2 columns, as kChunks boxes of
-    // 32 rows x 32 columns (64-byte rows, SWIZZLE_64B), one per TMEM load.
-    static constexpr int kChunks = BN / 64;
-    static constexpr int kBoxBytes = 32 * 32 * 2;
-    static constexpr int kWarpStaging = kChunks * kBoxBytes;  // 32 rows x BN/2 bf16
+    // Epilogue staging: per warp BN/64 boxes of 32 rows x 32 columns.
+    static constexpr int kWarpStaging = (BN / 64) * 2048;
     static constexpr int kStagingBytes = kEpiWarps * kWarpStaging;
     static constexpr int kLimit = 220 * 1024;
     static constexpr int kFit = (kLimit - kStagingBytes - 1280) / kStageBytes;
@@ -118,6 +120,85 @@ __device__ __forceinline__ uint32_t epi_pair(uint32_t a0, uint32_t a1, uint32_t 
     else
         asm("fma.rn.relu.bf16x2 %0, %1, %2, %3;" : "=r"(d) : "r"(r), "r"(0x3f803f80u), "r"(bias2));
     return d;
+}
+
+// 0 = bf16(acc), 1 = + bias, 2 = + bias (if any), relu.
+__device__ __forceinline__ int epi_mode(const Params& p) {
+    return p.relu ? 2 : (p.bias != nullptr ? 1 : 0);
+}
+
+// One epilogue warp's share of an accumulator tile: 32 rows (its TMEM lane
+// quadrant; t_row addresses lane 0 of the quadrant at the first column) x
+// BN/2 columns from output channel co0, output rows m0 .. m0 + 31.  The
+// columns are read 32 at a time (lane = row), the load of chunk ci + 1 in
+// flight while chunk ci is converted.  Each chunk is staged in its own box
+// (32 rows x 64 bytes, SWIZZLE_64B: 16-byte piece k of row r at k ^ ((r >> 1)
+// & 3), conflict-free for row-per-lane writes) and stored at once by lane 0
+// with a 2-D tensor store into y viewed as an M x Cout matrix (the copy
+// engine clips rows >= M and columns >= Cout), one bulk group per chunk.  Box
+// j is rewritten one tile later, after waiting until at most kChunks - 1
+// newer groups still read shared memory, i.e. box j's previous store has.
+// (Stores through the load/store units, staged the same way and read back as
+// 8 rows x 64 bytes per instruction, measured 24% slower on the 1x1
+// convolution.)  `release` runs after the last TMEM load.
+template <int BN, class Release>
+__device__ __forceinline__ void epilogue_rows(const Params& p, const CUtensorMap* tmap_y, uint32_t t_row,
+                                              uint32_t m0, uint32_t co0, uint32_t stg, int mode,
+                                              uint32_t lane, Release release) {
+    constexpr int kChunks = BN / 64;
+    constexpr uint32_t kBoxBytes = 32 * 32 * 2;
+    const uint32_t row_off = lane * 64u, sw = (lane >> 1) & 3u;
+    const bool has_bias = p.bias != nullptr;
+    // TMEM loads run one chunk ahead of the conversion: chunk ci + 1 is in
+    // flight while chunk ci is converted and stored.
+    uint32_t v[2][32];
+    tmem_ld32(t_row, v[0]);
+#pragma unroll
+    for (int ci = 0; ci < kChunks; ++ci) {
+        const uint32_t co = co0 + 32u * ci;
+        uint32_t bw[16];
+        if (mode != 0 && has_bias && co < p.Cout) {
+            const uint4* bp = reinterpret_cast<const uint4*>(p.bias + co);
+#pragma unroll
+            for (int i = 0; i < 4; ++i) {
+                const uint4 bv = __ldg(bp + i);
+                bw[4 * i] = bv.x; bw[4 * i + 1] = bv.y; bw[4 * i + 2] = bv.z; bw[4 * i + 3] = bv.w;
+            }
+        } else {
+#pragma unroll
+            for (int i = 0; i < 16; ++i) bw[i] = 0u;
+        }
+        tmem_ld_wait();  // chunk ci has landed (no other load is in flight)
+        if (ci + 1 < kChunks) tmem_ld32(t_row + 32u * (ci + 1), v[(ci + 1) & 1]);
+        if (ci + 1 == kChunks) release();
+        const uint32_t* c = v[ci & 1];
+        uint32_t o[16];
+        if (mode == 0) {
+#pragma unroll
+            for (int i = 0; i < 16; ++i) o[i] = epi_pair(c[2 * i], c[2 * i + 1], 0u, 0);
+        } else if (mode == 1) {
+#pragma unroll
+            for (int i = 0; i < 16; ++i) o[i] = epi_pair(c[2 * i], c[2 * i + 1], bw[i], 1);
+        } else {
+#pragma unroll
+            for (int i = 0; i < 16; ++i) o[i] = epi_pair(c[2 * i], c[2 * i + 1], bw[i], 2);
+        }
+        const uint32_t box = stg + ci * kBoxBytes;
+        if (lane == 0) bulk_wait_read_n<kChunks - 1>();
+        __syncwarp();
+#pragma unroll
+        for (int i = 0; i < 4; ++i)
+            asm volatile("st.shared.v4.b32 [%0], {%1, %2, %3, %4};" ::"r"(box + row_off + (((uint32_t)i ^ sw) << 4)),
+                         "r"(o[4 * i]), "r"(o[4 * i + 1]), "r"(o[4 * i + 2]), "r"(o[4 * i + 3])
+                         : "memory");
+        // Generic-proxy writes above, async-proxy (tensor store) reads below.
+        asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+        __syncwarp();
+        if (lane == 0) {
+            if (m0 < p.M && co < p.Cout) tma_store_2d(tmap_y, (int32_t)co, (int32_t)m0, box);
+            bulk_commit();
+        }
+    }
 }
 
 template <int BN, bool kTma>
@@ -341,21 +422,12 @@ __global__ void __launch_bounds__(kThreads, 1)
         }
     } else {
         // ---------------------------------------------------- epilogue
-        // Warp e (0..7) reads TMEM lane quadrant warp % 4 (rows qd*32 + lane)
-        // and columns [half * BN/2, (half + 1) * BN/2), 32 at a time.  Each
-        // chunk is converted into its own swizzled staging box (32 rows x 32
-        // columns) and stored at once by lane 0 with a 2-D tensor store into y
-        // viewed as an M x Cout matrix (the copy engine clips rows >= M and
-        // columns >= Cout), one bulk group per chunk.  Box j is rewritten one
-        // tile later, after waiting until at most kChunks - 1 newer groups are
-        // still reading shared memory, i.e. box j's previous store has.
+        // Warp e (0..7) drains TMEM lane quadrant warp % 4 (rows qd*32 + lane),
+        // columns [half * BN/2, (half + 1) * BN/2).
         const uint32_t e = warp - 5u, qd = warp & 3u, half = e >> 2;
         const uint32_t col0 = half * (uint32_t)(BN / 2);
         const uint32_t stg = smem_u32(staging) + e * (uint32_t)C::kWarpStaging;
-        const bool has_bias = p.bias != nullptr;
-        const int mode = p.relu ? 2 : (has_bias ? 1 : 0);
-        // Swizzle of row `lane` in a 64-byte-row box: 16-byte chunk k lands at k ^ sw.
-        const uint32_t row_off = lane * 64u, sw = (lane >> 1) & 3u;
+        const int mode = epi_mode(p);
         if (lane == 0) tma_prefetch_map(&tmap_y);
         uint32_t acc = 0, acc_phase = 0;
         for (uint32_t tile = blockIdx.x; tile < num_tiles; tile += gridDim.x) {
@@ -365,62 +437,13 @@ __global__ void __launch_bounds__(kThreads, 1)
             ok = __shfl_sync(0xffffffffu, ok ? 1 : 0, 0) != 0;
             if (!ok) break;
             tc_fence_after();
-            const uint32_t m0 = mb * 128u + qd * 32u;
-            const uint32_t t_row = tmem_base + ((qd * 32u) << 16) + acc * BN + col0;
-            const uint32_t co0 = nb * BN + col0;
-#pragma unroll
-            for (int ci = 0; ci < C::kChunks; ++ci) {
-                const uint32_t co = co0 + 32u * ci;
-                // Bias first: its load latency overlaps the TMEM load.
-                uint32_t bw[16];
-                if (mode != 0 && has_bias && co < p.Cout) {
-                    const uint4* bp = reinterpret_cast<const uint4*>(p.bias + co);
-#pragma unroll
-                    for (int i = 0; i < 4; ++i) {
-                        const uint4 bv = __ldg(bp + i);
-                        bw[4 * i] = bv.x; bw[4 * i + 1] = bv.y; bw[4 * i + 2] = bv.z; bw[4 * i + 3] = bv.w;
-                    }
-                } else {
-#pragma unroll
-                    for (int i = 0; i < 16; ++i) bw[i] = 0u;
-                }
-                uint32_t v[32];
-                tmem_ld32(t_row + 32u * ci, v);
-                tmem_ld_wait();
-                if (ci + 1 == C::kChunks) {
-                    // Last TMEM read of this tile by this warp: release the accumulator.
-                    tc_fence_before();
-                    __syncwarp();
-                    if (lane == 0) mbar_arrive(&tempty[acc]);
-                }
-                uint32_t o[16];
-                if (mode == 0) {
-#pragma unroll
-                    for (int i = 0; i < 16; ++i) o[i] = epi_pair(v[2 * i], v[2 * i + 1], 0u, 0);
-                } else if (mode == 1) {
-#pragma unroll
-                    for (int i = 0; i < 16; ++i) o[i] = epi_pair(v[2 * i], v[2 * i + 1], bw[i], 1);
-                } else {
-#pragma unroll
-                    for (int i = 0; i < 16; ++i) o[i] = epi_pair(v[2 * i], v[2 * i + 1], bw[i], 2);
-                }
-                const uint32_t box = stg + (uint32_t)(ci * C::kBoxBytes);
-                if (lane == 0) bulk_wait_read_n<C::kChunks - 1>();
-                __syncwarp();
-#pragma unroll
-                for (int i = 0; i < 4; ++i)
-                    asm volatile("st.shared.v4.b32 [%0], {%1, %2, %3, %4};" ::"r"(
-                                     box + row_off + (((uint32_t)i ^ sw) << 4)),
-                                 "r"(o[4 * i]), "r"(o[4 * i + 1]), "r"(o[4 * i + 2]), "r"(o[4 * i + 3])
-                                 : "memory");
-                // Generic-proxy writes above, async-proxy (tensor store) reads below.
-                asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
-                __syncwarp();
-                if (lane == 0) {
-                    if (m0 < p.M && co < p.Cout) tma_store_2d(&tmap_y, (int32_t)co, (int32_t)m0, box);
-                    bulk_commit();
-                }
-            }
+            uint64_t* te = &tempty[acc];
+            epilogue_rows<BN>(p, &tmap_y, tmem_base + ((qd * 32u) << 16) + acc * BN + col0,
+                              mb * 128u + qd * 32u, nb * BN + col0, stg, mode, lane, [&] {
+                                  tc_fence_before();
+                                  __syncwarp();
+                                  if (lane == 0) mbar_arrive(te);
+                              });
             if (++acc == 2) {
                 acc = 0;
                 acc_phase ^= 1u;
@@ -436,6 +459,223 @@ __global__ void __launch_bounds__(kThreads, 1)
         tc_fence_after();
         asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem_base),
                      "r"(C::kTmemCols)
+                     : "memory");
+    }
+}
+
+// ------------------------------------------------------------------------
+// Weight-stationary 2-SM variant (tensor copies, Cout <= 256).  A CTA pair
+// (cluster of 2) computes 256-row tiles with tcgen05.mma.cta_group::2
+// (M = 256, N = BN): each CTA stages its own 128 output pixels of A per
+// k-block, and keeps its half of the weights (BN/2 output channels x all of
+// K) resident in shared memory for the whole kernel, loaded once.  Per
+// k-block only 16 KiB of A crosses L2 -> SM, against 16 KiB + BN x 128 B in
+// the streaming kernel above, whose feed (not the tensor pipe) bounds the
+// 3x3 stride-2 convolution.  Both CTAs' tensor copies complete on the
+// leader's barriers (cta_group::2 form); the leader issues the MMAs and
+// multicasts its commits to both CTAs; each CTA drains its own TMEM rows.
+constexpr int kPairMaxStages = 8;
+
+template <int BN>
+__global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
+    conv_pair_kernel(const Params p, const __grid_constant__ CUtensorMap tmap_x,
+                     const __grid_constant__ CUtensorMap tmap_w, const __grid_constant__ CUtensorMap tmap_y,
+                     uint32_t stages) {
+    constexpr uint32_t kHalfB = (BN / 2) * 128;  // this CTA's weight rows of one k-block
+    constexpr uint32_t kABytes = 128 * 128;
+    constexpr uint32_t kWarpStaging = (BN / 64) * 2048;
+    constexpr uint32_t kTmemCols = 2 * BN;
+    extern __shared__ uint8_t smem_raw[];
+    uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) &
+                                               ~uintptr_t(1023));
+    uint8_t* b_res = smem;
+    uint8_t* a_st = b_res + p.num_kb * kHalfB;
+    uint8_t* staging = a_st + stages * kABytes;
+    uint64_t* full = reinterpret_cast<uint64_t*>(staging + kEpiWarps * kWarpStaging);
+    uint64_t* empty = full + kPairMaxStages;
+    uint64_t* tfull = empty + kPairMaxStages;
+    uint64_t* tempty = tfull + 2;
+    uint64_t* bfull = tempty + 2;
+    uint64_t* drain = bfull + 1;
+    uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(drain + 1);
+    volatile uint32_t* abort_flag = tmem_slot + 1;
+
+    const uint32_t warp = threadIdx.x >> 5, lane = threadIdx.x & 31u;
+    const uint32_t rank = cluster_ctarank();
+    const bool leader = rank == 0;
+    const uint32_t pair_id = blockIdx.x >> 1, num_pairs = gridDim.x >> 1;
+    if (threadIdx.x == 0) {
+        for (uint32_t s = 0; s < stages; ++s) {
+            mbar_init(&full[s], 1);
+            mbar_init(&empty[s], 1);
+        }
+        for (int b = 0; b < 2; ++b) {
+            mbar_init(&tfull[b], 1);
+            mbar_init(&tempty[b], 2 * kEpiWarps);
+        }
+        mbar_init(bfull, 1);
+        mbar_init(drain, 1);
+        *abort_flag = 0u;
+        asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+        asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+    }
+    if (warp == kMmaWarp) {
+        asm volatile("tcgen05.alloc.cta_group::2.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(
+                         smem_u32(tmem_slot)),
+                     "r"(kTmemCols)
+                     : "memory");
+        asm volatile("tcgen05.relinquish_alloc_permit.cta_group::2.sync.aligned;" ::: "memory");
+    }
+    tc_fence_before();
+    __syncthreads();
+    cluster_sync();
+    tc_fence_after();
+    const uint32_t tmem_base = *tmem_slot;
+    const uint32_t num_tiles = p.m_blocks;  // 256-row blocks
+
+    if (warp == 0) {
+        if (lane == 0) {
+            // ------------------------------------ tensor-copy producer
+            tma_prefetch_map(&tmap_x);
+            tma_prefetch_map(&tmap_w);
+            const uint32_t lead_full0 = map_to_rank(&full[0], 0);
+            // Resident weights: rows [rank * BN/2, (rank + 1) * BN/2) of the
+            // K x Cout weight matrix, one box per k-block.
+            if (leader) mbar_expect_tx(bfull, 2u * p.num_kb * kHalfB);
+            {
+                const uint32_t lead_bfull = map_to_rank(bfull, 0);
+                uint32_t kh = 0, kw = 0, cb = 0;
+                for (uint32_t kb = 0; kb < p.num_kb; ++kb) {
+                    tma_load_2d_pair(smem_u32(b_res) + kb * kHalfB, &tmap_w,
+                                     (int32_t)((kh * p.KW + kw) * p.Cin + cb * 64u), (int32_t)(rank * (BN / 2)),
+                                     lead_bfull);
+                    if (++cb == p.cblocks) {
+                        cb = 0;
+                        if (++kw == p.KW) {
+                            kw = 0;
+                            ++kh;
+                        }
+                    }
+                }
+            }
+            const uint32_t hw = p.Ho * p.Wo;
+            uint32_t stage = 0, phase = 0;
+            bool ok = true;
+            for (uint32_t tile = pair_id; ok && tile < num_tiles; tile += num_pairs) {
+                // Base pixel (tap (0, 0)) of this CTA's first output pixel; past
+                // the last image it lies outside the tensor and reads zeros.
+                const uint32_t m0 = tile * 256u + rank * 128u, n = m0 / hw, rem = m0 - n * hw;
+                const uint32_t ho = rem / p.Wo, wo = rem - ho * p.Wo;
+                const int32_t w0 = (int32_t)(wo * p.stride) - (int32_t)p.pad;
+                const int32_t h0 = (int32_t)(ho * p.stride) - (int32_t)p.pad;
+                uint32_t kh = 0, kw = 0, cb = 0;
+                for (uint32_t kb = 0; kb < p.num_kb; ++kb) {
+                    if (!mbar_wait_cluster(&empty[stage], phase ^ 1u, abort_flag, p.err)) {
+                        ok = false;
+                        break;
+                    }
+                    if (leader) mbar_expect_tx(&full[stage], 2u * kABytes);
+                    tma_load_im2col_4d_pair(smem_u32(a_st + stage * kABytes), &tmap_x, (int32_t)(cb * 64u), w0,
+                                            h0, (int32_t)n, (uint16_t)kw, (uint16_t)kh, lead_full0 + stage * 8u);
+                    if (++stage == stages) {
+                        stage = 0;
+                        phase ^= 1u;
+                    }
+                    if (++cb == p.cblocks) {
+                        cb = 0;
+                        if (++kw == p.KW) {
+                            kw = 0;
+                            ++kh;
+                        }
+                    }
+                }
+            }
+        }
+    } else if (warp == kMmaWarp) {
+        if (leader && lane == 0) {
+            // ------------------------------------------------ MMA issuer
+            // kind::f16, f32 accumulate, bf16 A and B, both K-major, M = 256.
+            const uint32_t idesc = (1u << 4) | (1u << 7) | (1u << 10) | ((uint32_t)(BN >> 3) << 17) |
+                                   ((256u >> 4) << 24);
+            constexpr uint64_t kmaj = smem_desc_sw128_kmajor();
+            const uint32_t a0 = smem_u32(a_st), b0 = smem_u32(b_res);
+            uint32_t stage = 0, phase = 0, acc = 0, acc_phase = 0;
+            bool ok = mbar_wait_cluster(bfull, 0, abort_flag, p.err);
+            for (uint32_t tile = pair_id; ok && tile < num_tiles; tile += num_pairs) {
+                if (!mbar_wait_cluster(&tempty[acc], acc_phase ^ 1u, abort_flag, p.err)) break;
+                tc_fence_after();
+                const uint32_t d_tmem = tmem_base + acc * BN;
+                for (uint32_t kb = 0; kb < p.num_kb; ++kb) {
+                    if (!mbar_wait_cluster(&full[stage], phase, abort_flag, p.err)) {
+                        ok = false;
+                        break;
+                    }
+                    tc_fence_after();
+                    const uint32_t a_addr = a0 + stage * kABytes, b_addr = b0 + kb * kHalfB;
+#pragma unroll
+                    for (uint32_t s = 0; s < 4; ++s) {
+                        const uint64_t ad = kmaj | (uint64_t)(((a_addr + s * 32u) >> 4) & 0x3fffu);
+                        const uint64_t bd = kmaj | (uint64_t)(((b_addr + s * 32u) >> 4) & 0x3fffu);
+                        tc_mma_pair(d_tmem, ad, bd, idesc, (kb | s) != 0u);
+                    }
+                    tc_commit_pair_mc(&empty[stage], 0x3);
+                    if (++stage == stages) {
+                        stage = 0;
+                        phase ^= 1u;
+                    }
+                }
+                if (!ok) break;
+                tc_commit_pair_mc(&tfull[acc], 0x3);
+                if (++acc == 2) {
+                    acc = 0;
+                    acc_phase ^= 1u;
+                }
+            }
+            tc_commit_pair(drain);
+            mbar_drain(drain, 0, 100000000ull);
+        }
+    } else if (warp > kMmaWarp) {
+        // ---------------------------------------------------- epilogue
+        // As in the streaming kernel, on this CTA's 128 rows of each 256-row
+        // tile; the accumulator is released on the leader's barrier.  The
+        // arrive only orders TMEM reads before the next MMAs, which the
+        // tcgen05 fences do, so it is relaxed: a release at cluster scope
+        // would first wait for this thread's global stores.
+        const uint32_t e = warp - 5u, qd = warp & 3u, half = e >> 2;
+        const uint32_t col0 = half * (uint32_t)(BN / 2);
+        const uint32_t stg = smem_u32(staging) + e * kWarpStaging;
+        const int mode = epi_mode(p);
+        if (lane == 0) tma_prefetch_map(&tmap_y);
+        const uint32_t lead_tempty0 = map_to_rank(&tempty[0], 0);
+        uint32_t acc = 0, acc_phase = 0;
+        for (uint32_t tile = pair_id; tile < num_tiles; tile += num_pairs) {
+            bool ok = true;
+            if (lane == 0) ok = mbar_wait_cluster(&tfull[acc], acc_phase, abort_flag, p.err);
+            ok = __shfl_sync(0xffffffffu, ok ? 1 : 0, 0) != 0;
+            if (!ok) break;
+            tc_fence_after();
+            const uint32_t te = lead_tempty0 + acc * 8u;
+            epilogue_rows<BN>(p, &tmap_y, tmem_base + ((qd * 32u) << 16) + acc * BN + col0,
+                              tile * 256u + rank * 128u + qd * 32u, col0, stg, mode, lane, [&] {
+                                  tc_fence_before();
+                                  __syncwarp();
+                                  if (lane == 0) mbar_arrive_remote_relaxed(te);
+                              });
+            if (++acc == 2) {
+                acc = 0;
+                acc_phase ^= 1u;
+            }
+        }
+        if (lane == 0) bulk_wait_all();
+    }
+
+    tc_fence_before();
+    __syncthreads();
+    cluster_sync();
+    if (warp == kMmaWarp) {
+        tc_fence_after();
+        asm volatile("tcgen05.dealloc.cta_group::2.sync.aligned.b32 %0, %1;" ::"r"(tmem_base),
+                     "r"(kTmemCols)
                      : "memory");
     }
 }
@@ -457,6 +697,40 @@ static int launch_bn(const Params& p, const CUtensorMap& mx, const CUtensorMap& 
     const uint32_t tiles = p.m_blocks * p.n_blocks;
     const uint32_t grid = tiles < (uint32_t)max_ctas ? tiles : (uint32_t)max_ctas;
     conv_kernel<BN, kTma><<<grid, kThreads, C::kSmemBytes, stream>>>(p, mx, mw, my);
+    cudaError_t e = cudaGetLastError();
+    if (e != cudaSuccess) {
+        char buf[200];
+        snprintf(buf, sizeof buf, "foil_conv2d_nhwc: launch failed: %s", cudaGetErrorString(e));
+        foil_set_error(FOIL_ERR_CUDA, buf);
+        return FOIL_ERR_CUDA;
+    }
+    foil_count_launch();
+    return FOIL_OK;
+}
+
+// Shared memory of the pair kernel: resident weights, `stages` A stages,
+// epilogue staging, barriers (+ 1 KiB alignment slack).
+static uint32_t pair_smem_bytes(const Params& p, int bn, uint32_t stages) {
+    return p.num_kb * (uint32_t)(bn / 2) * 128u + stages * 16384u + kEpiWarps * (uint32_t)(bn / 64) * 2048u +
+           1024u + 256u;
+}
+
+template <int BN>
+static int launch_pair(const Params& p, uint32_t stages, const CUtensorMap& mx, const CUtensorMap& mw,
+                       const CUtensorMap& my, cudaStream_t stream, int max_ctas, int smem_optin) {
+    static std::once_flag once;
+    static cudaError_t attr = cudaSuccess;
+    std::call_once(once, [smem_optin] {
+        attr = cudaFuncSetAttribute(conv_pair_kernel<BN>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                    smem_optin);
+    });
+    if (attr != cudaSuccess) {
+        foil_set_error(FOIL_ERR_CUDA, "foil_conv2d_nhwc: cudaFuncSetAttribute failed");
+        return FOIL_ERR_CUDA;
+    }
+    const uint32_t max_pairs = (uint32_t)max_ctas / 2;
+    const uint32_t pairs = p.m_blocks < max_pairs ? p.m_blocks : max_pairs;
+    conv_pair_kernel<BN><<<2 * pairs, kThreads, pair_smem_bytes(p, BN, stages), stream>>>(p, mx, mw, my, stages);
     cudaError_t e = cudaGetLastError();
     if (e != cudaSuccess) {
         char buf[200];
@@ -504,14 +778,16 @@ static const Encoders& encoders() {
 // The tensor-copy producer serves Cin a multiple of 64 (one 128-byte channel
 // run per k-block) with a traversal stride the copy engine supports (<= 8)
 // and byte strides below 2^40; other shapes use the gather producer.
-// FOIL_CONV_PRODUCER=gather selects the gather producer for every shape
-// (A/B comparisons of the two producers).
+// FOIL_CONV_PRODUCER=gather selects the gather producer for every shape, and
+// FOIL_CONV_PRODUCER=single the tensor-copy producer in the single-CTA
+// kernel (A/B comparisons of the variants, which agree bit for bit).
+static const char* producer_override() {
+    static const char* v = getenv("FOIL_CONV_PRODUCER");
+    return v ? v : "";
+}
+
 static bool use_tensor_copies(const Params& p) {
-    static const bool force_gather = [] {
-        const char* v = getenv("FOIL_CONV_PRODUCER");
-        return v && strcmp(v, "gather") == 0;
-    }();
-    return !force_gather && p.Cin % 64 == 0 && p.stride <= 8 &&
+    return strcmp(producer_override(), "gather") != 0 && p.Cin % 64 == 0 && p.stride <= 8 &&
            (uint64_t)p.H * p.W * p.Cin * 2 < (1ull << 40);
 }
 
@@ -529,7 +805,9 @@ static bool encode_output_map(const Params& p, CUtensorMap* my) {
                    CU_TENSOR_MAP_L2_PROMOTION_NONE, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
 }
 
-static bool encode_maps(const Params& p, int bn, CUtensorMap* mx, CUtensorMap* mw) {
+// A (im2col of x) and weights as a K x Cout matrix read in boxes of 64
+// channels x `w_rows` output channels (BN, or BN/2 per CTA of a pair).
+static bool encode_maps(const Params& p, uint32_t w_rows, CUtensorMap* mx, CUtensorMap* mw) {
     const Encoders& e = encoders();
     if (!e.im2col || !e.tiled) return false;
     // Dims and byte strides innermost first: C, W, H, N.
@@ -548,7 +826,7 @@ static bool encode_maps(const Params& p, int bn, CUtensorMap* mx, CUtensorMap* m
     // Weights as a K x Cout matrix (K = KH * KW * Cin contiguous per row).
     const cuuint64_t wdim[2] = {(cuuint64_t)p.KH * p.KW * p.Cin, p.Cout};
     const cuuint64_t wstr[1] = {(cuuint64_t)p.KH * p.KW * p.Cin * 2};
-    const cuuint32_t box[2] = {64, (cuuint32_t)bn};
+    const cuuint32_t box[2] = {64, w_rows};
     const cuuint32_t one[2] = {1, 1};
     return e.tiled(mw, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, const_cast<uint16_t*>(p.w), wdim, wstr, box,
                    one, CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
@@ -589,11 +867,36 @@ int launch(const uint16_t* x, const uint16_t* w, const uint16_t* bias, uint16_t*
     memset(&mx, 0, sizeof mx);
     memset(&mw, 0, sizeof mw);
     const bool tc = use_tensor_copies(p);
-    if (!encode_output_map(p, &my) || (tc && !encode_maps(p, bn, &mx, &mw))) {
+    if (!encode_output_map(p, &my)) {
         foil_set_error(FOIL_ERR_CUDA, "foil_conv2d_nhwc: tensor-map encoding failed");
         return FOIL_ERR_CUDA;
     }
     if (!tc) return launch_tiles<false>(p, bn, mx, mw, my, stream, max_ctas);
+    // Weight-stationary pair kernel: one column block, more than one 128-row
+    // block, and at least 4 A stages beside the resident weights.
+    int dev = 0, optin = 0;
+    if (cudaGetDevice(&dev) != cudaSuccess ||
+        cudaDeviceGetAttribute(&optin, cudaDevAttrMaxSharedMemoryPerBlockOptin, dev) != cudaSuccess) {
+        foil_set_error(FOIL_ERR_CUDA, "foil_conv2d_nhwc: device query failed");
+        return FOIL_ERR_CUDA;
+    }
+    uint32_t stages = 0;
+    while (stages < (uint32_t)kPairMaxStages && pair_smem_bytes(p, bn, stages + 1) <= (uint32_t)optin) ++stages;
+    const bool pair = p.n_blocks == 1 && p.M > 128 && stages >= 4 && max_ctas >= 2 &&
+                      strcmp(producer_override(), "single") != 0;
+    if (!encode_maps(p, pair ? (uint32_t)bn / 2 : (uint32_t)bn, &mx, &mw)) {
+        foil_set_error(FOIL_ERR_CUDA, "foil_conv2d_nhwc: tensor-map encoding failed");
+        return FOIL_ERR_CUDA;
+    }
+    if (pair) {
+        Params q = p;
+        q.m_blocks = (p.M + 255) / 256;
+        switch (bn) {
+            case 64: return launch_pair<64>(q, stages, mx, mw, my, stream, max_ctas, optin);
+            case 128: return launch_pair<128>(q, stages, mx, mw, my, stream, max_ctas, optin);
+            default: return launch_pair<256>(q, stages, mx, mw, my, stream, max_ctas, optin);
+        }
+    }
     return launch_tiles<true>(p, bn, mx, mw, my, stream, max_ctas);
 }
 

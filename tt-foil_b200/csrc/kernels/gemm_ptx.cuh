@@ -173,6 +173,29 @@ __device__ __forceinline__ void tma_load_im2col_4d(uint32_t dst, const void* map
         : "memory");
 }
 
+// Pair (cta_group::2) forms, no multicast: the destination is this CTA's
+// shared memory and completion is signalled on the mbarrier at shared::cluster
+// address `bar_cluster`, which may be the pair leader's.
+__device__ __forceinline__ void tma_load_2d_pair(uint32_t dst, const void* map, int32_t x, int32_t y,
+                                                 uint32_t bar_cluster) {
+    asm volatile(
+        "cp.async.bulk.tensor.2d.cta_group::2.shared::cluster.global.mbarrier::complete_tx::bytes"
+        " [%0], [%1, {%2, %3}], [%4];" ::"r"(dst),
+        "l"(reinterpret_cast<uint64_t>(map)), "r"(x), "r"(y), "r"(bar_cluster)
+        : "memory");
+}
+
+__device__ __forceinline__ void tma_load_im2col_4d_pair(uint32_t dst, const void* map, int32_t c,
+                                                        int32_t w, int32_t h, int32_t n, uint16_t off_w,
+                                                        uint16_t off_h, uint32_t bar_cluster) {
+    asm volatile(
+        "cp.async.bulk.tensor.4d.im2col.cta_group::2.shared::cluster.global.mbarrier::complete_tx::bytes"
+        " [%0], [%1, {%2, %3, %4, %5}], [%6], {%7, %8};" ::"r"(dst),
+        "l"(reinterpret_cast<uint64_t>(map)), "r"(c), "r"(w), "r"(h), "r"(n), "r"(bar_cluster),
+        "h"(off_w), "h"(off_h)
+        : "memory");
+}
+
 // 2-D tiled store from shared memory (bulk group of this thread); elements of
 // the box outside the tensor are not written.  Coordinates must be >= 0.
 __device__ __forceinline__ void tma_store_2d(const void* map, int32_t x, int32_t y, uint32_t src) {
