@@ -124,10 +124,6 @@ def test_conv_shapes(env, N, H, W, Cin, Cout, k, stride, pad, bias, relu):
     (2, 12, 10, 64, 64, 3, 5, 1, 1),    # non-square kernel: W and H bounding boxes differ
     (1, 20, 17, 64, 128, 3, 3, 3, 1),   # stride 3
     (1, 9, 31, 192, 64, 1, 3, 2, 0),    # 1 x 3, three channel blocks
-    # 2-SM weight-stationary kernel (Cin % 64 == 0, Cout <= 256, M > 128):
-    (3, 10, 10, 64, 192, 3, 3, 1, 1),   # M = 300: the second pair's odd CTA has no valid row
-    (2, 14, 14, 256, 64, 3, 3, 1, 1),   # K = 2304: 144 KiB of resident weights, 4 A stages
-    (1, 23, 29, 128, 128, 3, 3, 2, 1),  # M = 180, stride 2, odd sizes
 ])
 def test_conv_rectangular_and_strided(env, N, H, W, Cin, Cout, kh, kw, stride, pad):
     x = oracle.rand_bf16((N, H, W, Cin), 11 + W)
@@ -138,16 +134,28 @@ def test_conv_rectangular_and_strided(env, N, H, W, Cin, Cout, kh, kw, stride, p
     check(got, exp, x, w)
 
 
-@pytest.mark.parametrize("variant", ["gather", "single"])
-def test_kernel_variants_agree_bitwise(env, tmp_path, variant):
-    """Cin a multiple of 64 and Cout <= 256 runs the 2-SM weight-stationary
-    kernel with tensor copies; FOIL_CONV_PRODUCER=single runs the same shape
-    on the single-CTA kernel with tensor copies, =gather with the cp.async
-    gather producer.  All feed identical operand tiles in the same K order, so
-    the outputs are bit-identical (config-2 shape and a batch-2 stride-2
-    shape)."""
-    cases = [((1, 56, 56, 64), (64, 3, 3, 64), 1, 1), ((2, 30, 30, 128), (256, 3, 3, 128), 2, 1)]
-    script = tmp_path / "gather_run.py"
+VARIANTS = {
+    "gather": {"FOIL_CONV_PRODUCER": "gather"},
+    "single": {"FOIL_CONV_PRODUCER": "single"},
+    "pair": {"FOIL_CONV_PRODUCER": "pair"},
+}
+
+VARIANT_CASES = [  # x shape, w shape, stride, pad
+    ((1, 56, 56, 64), (64, 3, 3, 64), 1, 1),       # config-2 shape
+    ((2, 30, 30, 128), (256, 3, 3, 128), 2, 1),    # BN 256, two channel blocks
+    ((3, 10, 10, 64), (192, 3, 3, 64), 1, 1),      # M = 300: the second pair's odd CTA has no valid row
+    ((2, 14, 14, 256), (64, 3, 3, 256), 1, 1),     # K = 2304: 144 KiB of resident weights
+    ((1, 23, 29, 128), (128, 3, 3, 128), 2, 1),    # M = 180, odd sizes
+    ((4, 16, 16, 64), (64, 5, 5, 64), 1, 2),       # 5x5
+]
+
+
+@pytest.fixture(scope="module")
+def variant_inputs(env, tmp_path_factory):
+    """Seeded inputs of VARIANT_CASES, their default-path outputs (checked
+    against the oracle) and the script that reruns a case in a subprocess."""
+    d = tmp_path_factory.mktemp("variants")
+    script = d / "run_case.py"
     script.write_text(
         "import sys, numpy as np, torch\n"
         f"sys.path.insert(0, {PKG!r})\n"
@@ -160,19 +168,34 @@ def test_kernel_variants_agree_bitwise(env, tmp_path, variant):
         "ttfoil.conv2d_nhwc(x, w, b, y, N, H, W, Cin, Cout, KH, KW, s, p, relu=True)\n"
         "torch.cuda.synchronize(); assert ttfoil.device_error() == 0\n"
         "np.save(sys.argv[2], y.cpu().numpy())\n")
-    for i, (xs, ws, stride, pad) in enumerate(cases):
+    cases = []
+    for i, (xs, ws, stride, pad) in enumerate(VARIANT_CASES):
         x = oracle.rand_bf16(xs, 40 + i)
         w = oracle.randn_bf16(ws, 50 + i, np.sqrt(2.0 / (ws[1] * ws[2] * ws[3])))
         b = oracle.rand_bf16((ws[0],), 60 + i, -0.1, 0.1)
         got = run_conv(env, x, w, b, stride, pad, relu=True)
-        inp, out = tmp_path / f"in{i}.npz", tmp_path / f"out{i}.npy"
+        check(got, oracle.conv_nhwc(x, w, b, stride, pad, relu=True, threads=8), x, w)
+        inp = d / f"in{i}.npz"
         np.savez(inp, x=x, w=w, b=b, s=stride, p=pad)
-        env_vars = dict(os.environ, FOIL_CONV_PRODUCER=variant)
+        cases.append((inp, got))
+    return script, cases
+
+
+@pytest.mark.parametrize("variant", sorted(VARIANTS))
+def test_kernel_variants_agree_bitwise(variant_inputs, tmp_path, variant):
+    """Every kernel variant (gather producer, single-CTA tensor copies, 2-SM
+    weight-stationary pair) feeds identical operand tiles in the same K order,
+    so each reproduces the default path's output bit for bit on every case;
+    the default outputs are themselves checked against the oracle."""
+    script, cases = variant_inputs
+    env_vars = dict(os.environ, **VARIANTS[variant])
+    for i, (inp, got) in enumerate(cases):
+        out = tmp_path / f"out{i}.npy"
         r = subprocess.run([sys.executable, str(script), str(inp), str(out)], env=env_vars,
                            capture_output=True, text=True, timeout=300)
         assert r.returncode == 0, r.stderr[-2000:]
         ref = np.load(out).view(np.uint16).reshape(got.shape)
-        assert np.array_equal(got, ref), int(np.sum(got != ref))
+        assert np.array_equal(got, ref), (i, int(np.sum(got != ref)))
 
 
 def test_conv_rejects_bad_shapes(env):

@@ -35,16 +35,16 @@
 // K loops (9 k-blocks for 3x3x64, 2 for 1x1x128), so the epilogue matters:
 // 8 epilogue warps (two per TMEM lane quadrant, each half the columns) read 32
 // columns per TMEM load, release the accumulator as soon as their last load
-// has landed, and write through shared memory with coalesced stores (see
-// epilogue_rows).
+// has landed, and stage their rows for 2-D tensor stores (see epilogue_rows).
 //
-// Throughput limits measured on B200 that shaped this file: the tensor-copy
-// engine of an SM issues about one row request (<= 128 bytes) per 3 cycles
-// for tiled copies (~81 GB/s per SM with 128-byte rows, independent of how
-// many SMs run or how many copies are in flight) and one per ~4.3 cycles for
-// im2col copies (~56 GB/s per SM).  Weights are therefore kept resident where
-// they fit (conv_pair_kernel), so that only A crosses per k-block.  Every
-// wait is bounded (see gemm_ptx.cuh).
+// Throughput limit measured on B200 that shaped this file: the tensor-copy
+// engine of an SM completes about one tiled copy per ~200 ns and one im2col
+// copy per ~295 ns, nearly independent of the box size up to 128-256 rows
+// and of how many copies are in flight or how many SMs issue them.  So copy
+// INSTRUCTIONS are the budget: a 128-row im2col of 16 KiB moves ~56 GB/s per
+// SM, a 256-row one twice that.  Hence the weight-stationary pair kernel
+// (no weight copies per k-block, 256-row im2col copies) and epilogue stores
+// of whole 128-row boxes.  Every wait is bounded (see gemm_ptx.cuh).
 #include <cuda.h>
 #include <cudaTypedefs.h>
 
@@ -69,6 +69,7 @@ constexpr int kProdWarps = 4;
 constexpr int kMmaWarp = 4;
 constexpr int kEpiWarps = 8;  // two per TMEM lane quadrant, each half of the columns
 constexpr int kThreads = (5 + kEpiWarps) * 32;
+constexpr int kBarrierBytes = 512;  // mbarriers and flags after the staging area
 
 struct Params {
     const uint16_t* x;
@@ -90,13 +91,12 @@ struct Cfg {
     static constexpr int kABytes = 128 * 128;               // 128 rows x 64 ch x 2 B (max kc)
     static constexpr int kBBytes = BN * 128;                // BN rows x 64 ch x 2 B
     static constexpr int kStageBytes = kABytes + kBBytes;
-    // Epilogue staging: per warp BN/64 boxes of 32 rows x 32 columns.
-    static constexpr int kWarpStaging = (BN / 64) * 2048;
-    static constexpr int kStagingBytes = kEpiWarps * kWarpStaging;
+    // Epilogue staging: 8 warps x 32 rows x BN/2 columns (see Epi).
+    static constexpr int kStagingBytes = 256 * BN;
     static constexpr int kLimit = 220 * 1024;
-    static constexpr int kFit = (kLimit - kStagingBytes - 1280) / kStageBytes;
+    static constexpr int kFit = (kLimit - kStagingBytes - 1024 - kBarrierBytes) / kStageBytes;
     static constexpr int kStages = kFit > 8 ? 8 : kFit;
-    static constexpr int kSmemBytes = kStages * kStageBytes + kStagingBytes + 1024 + 256;
+    static constexpr int kSmemBytes = kStages * kStageBytes + kStagingBytes + 1024 + kBarrierBytes;
     static constexpr int kTmemCols = 2 * BN;                // power of two for BN in {64,128,256}
 };
 
@@ -127,76 +127,106 @@ __device__ __forceinline__ int epi_mode(const Params& p) {
     return p.relu ? 2 : (p.bias != nullptr ? 1 : 0);
 }
 
-// One epilogue warp's share of an accumulator tile: 32 rows (its TMEM lane
-// quadrant; t_row addresses lane 0 of the quadrant at the first column) x
-// BN/2 columns from output channel co0, output rows m0 .. m0 + 31.  The
-// columns are read 32 at a time (lane = row), the load of chunk ci + 1 in
-// flight while chunk ci is converted.  Each chunk is staged in its own box
-// (32 rows x 64 bytes, SWIZZLE_64B: 16-byte piece k of row r at k ^ ((r >> 1)
-// & 3), conflict-free for row-per-lane writes) and stored at once by lane 0
-// with a 2-D tensor store into y viewed as an M x Cout matrix (the copy
-// engine clips rows >= M and columns >= Cout), one bulk group per chunk.  Box
-// j is rewritten one tile later, after waiting until at most kChunks - 1
-// newer groups still read shared memory, i.e. box j's previous store has.
-// (Stores through the load/store units, staged the same way and read back as
-// 8 rows x 64 bytes per instruction, measured 24% slower on the 1x1
-// convolution.)  `release` runs after the last TMEM load.
+// Bias words (bf16 pairs) of output channels co .. co + 31, or zeros.
+__device__ __forceinline__ void load_bias32(const Params& p, uint32_t co, bool want, uint32_t (&bw)[16]) {
+    if (want && co < p.Cout) {
+        const uint4* bp = reinterpret_cast<const uint4*>(p.bias + co);
+#pragma unroll
+        for (int i = 0; i < 4; ++i) {
+            const uint4 bv = __ldg(bp + i);
+            bw[4 * i] = bv.x; bw[4 * i + 1] = bv.y; bw[4 * i + 2] = bv.z; bw[4 * i + 3] = bv.w;
+        }
+    } else {
+#pragma unroll
+        for (int i = 0; i < 16; ++i) bw[i] = 0u;
+    }
+}
+
+// Epilogue geometry.  Epilogue warp e covers TMEM lane quadrant e % 4 (32
+// rows) and column half e / 4 (BN/2 columns); it stages its 32 x BN/2 share
+// in boxes of 32 rows x kCols columns (128-byte rows with SWIZZLE_128B for
+// BN >= 128, else 64-byte rows with SWIZZLE_64B) and stores each box with one
+// 2-D tensor store.  (Boxes of 128 rows shared by the four warps of a column
+// half, synchronised through mbarriers, cut the store instructions by 4 but
+// measured 6-37% slower: the warps then wait on each other and on the
+// previous store of the shared box.)
+template <int BN>
+struct Epi {
+    static constexpr int kChunks = BN / 64;              // 32-column chunks per warp
+    static constexpr int kCols = BN >= 128 ? 64 : 32;    // columns per box
+    static constexpr int kCPB = kCols / 32;              // chunks per box
+    static constexpr int kBoxes = kChunks / kCPB;        // boxes per warp
+    static constexpr uint32_t kRowBytes = kCols * 2;
+    static constexpr uint32_t kBoxBytes = 32 * kRowBytes;
+    static constexpr uint32_t kWarpBytes = kBoxes * kBoxBytes;  // 32 rows x BN/2 columns
+};
+
+// One epilogue warp's share of an accumulator tile: 32 rows (TMEM lane
+// quadrant; t_row addresses lane 0 of the quadrant at the warp's first
+// column) x BN/2 columns from output channel co0, output rows m0 .. m0 + 31.
+// The columns are read 32 at a time (lane = row); the TMEM load and the bias
+// load of chunk ci + 1 are in flight while chunk ci is converted.  Chunk ci
+// goes to box ci / kCPB at its swizzled position (16-byte piece k of row r at
+// k ^ (r & 7), or k ^ ((r >> 1) & 3) for 64-byte rows: conflict-free for
+// row-per-lane writes), and each full box is stored by lane 0 (the copy
+// engine clips rows >= M and columns >= Cout), one bulk group per box.  Box
+// b is rewritten one tile later, after waiting until at most kBoxes - 1 newer
+// groups still read shared memory, i.e. box b's previous store has.
+// `release` runs after the last TMEM load.
 template <int BN, class Release>
 __device__ __forceinline__ void epilogue_rows(const Params& p, const CUtensorMap* tmap_y, uint32_t t_row,
-                                              uint32_t m0, uint32_t co0, uint32_t stg, int mode,
-                                              uint32_t lane, Release release) {
-    constexpr int kChunks = BN / 64;
-    constexpr uint32_t kBoxBytes = 32 * 32 * 2;
-    const uint32_t row_off = lane * 64u, sw = (lane >> 1) & 3u;
-    const bool has_bias = p.bias != nullptr;
-    // TMEM loads run one chunk ahead of the conversion: chunk ci + 1 is in
-    // flight while chunk ci is converted and stored.
-    uint32_t v[2][32];
+                                              uint32_t m0, uint32_t co0, uint32_t stg, int mode, uint32_t lane,
+                                              Release release) {
+    using E = Epi<BN>;
+    const uint32_t row_off = lane * E::kRowBytes;
+    const uint32_t sw = E::kCols == 64 ? (lane & 7u) : ((lane >> 1) & 3u);
+    const bool want_bias = mode != 0 && p.bias != nullptr;
+    uint32_t v[2][32], bw[2][16];
+    load_bias32(p, co0, want_bias, bw[0]);
     tmem_ld32(t_row, v[0]);
 #pragma unroll
-    for (int ci = 0; ci < kChunks; ++ci) {
-        const uint32_t co = co0 + 32u * ci;
-        uint32_t bw[16];
-        if (mode != 0 && has_bias && co < p.Cout) {
-            const uint4* bp = reinterpret_cast<const uint4*>(p.bias + co);
-#pragma unroll
-            for (int i = 0; i < 4; ++i) {
-                const uint4 bv = __ldg(bp + i);
-                bw[4 * i] = bv.x; bw[4 * i + 1] = bv.y; bw[4 * i + 2] = bv.z; bw[4 * i + 3] = bv.w;
-            }
-        } else {
-#pragma unroll
-            for (int i = 0; i < 16; ++i) bw[i] = 0u;
-        }
+    for (int ci = 0; ci < E::kChunks; ++ci) {
         tmem_ld_wait();  // chunk ci has landed (no other load is in flight)
-        if (ci + 1 < kChunks) tmem_ld32(t_row + 32u * (ci + 1), v[(ci + 1) & 1]);
-        if (ci + 1 == kChunks) release();
+        if (ci + 1 < E::kChunks) {
+            tmem_ld32(t_row + 32u * (ci + 1), v[(ci + 1) & 1]);
+            load_bias32(p, co0 + 32u * (ci + 1), want_bias, bw[(ci + 1) & 1]);
+        }
+        if (ci + 1 == E::kChunks) release();
         const uint32_t* c = v[ci & 1];
+        const uint32_t* b = bw[ci & 1];
         uint32_t o[16];
         if (mode == 0) {
 #pragma unroll
             for (int i = 0; i < 16; ++i) o[i] = epi_pair(c[2 * i], c[2 * i + 1], 0u, 0);
         } else if (mode == 1) {
 #pragma unroll
-            for (int i = 0; i < 16; ++i) o[i] = epi_pair(c[2 * i], c[2 * i + 1], bw[i], 1);
+            for (int i = 0; i < 16; ++i) o[i] = epi_pair(c[2 * i], c[2 * i + 1], b[i], 1);
         } else {
 #pragma unroll
-            for (int i = 0; i < 16; ++i) o[i] = epi_pair(c[2 * i], c[2 * i + 1], bw[i], 2);
+            for (int i = 0; i < 16; ++i) o[i] = epi_pair(c[2 * i], c[2 * i + 1], b[i], 2);
         }
-        const uint32_t box = stg + ci * kBoxBytes;
-        if (lane == 0) bulk_wait_read_n<kChunks - 1>();
-        __syncwarp();
+        const int bx = ci / E::kCPB, part = ci % E::kCPB;
+        const uint32_t box = stg + bx * E::kBoxBytes;
+        if (part == 0) {
+            if (lane == 0) bulk_wait_read_n<E::kBoxes - 1>();
+            __syncwarp();
+        }
 #pragma unroll
-        for (int i = 0; i < 4; ++i)
-            asm volatile("st.shared.v4.b32 [%0], {%1, %2, %3, %4};" ::"r"(box + row_off + (((uint32_t)i ^ sw) << 4)),
+        for (int i = 0; i < 4; ++i) {
+            const uint32_t k = (uint32_t)(part * 4 + i);
+            asm volatile("st.shared.v4.b32 [%0], {%1, %2, %3, %4};" ::"r"(box + row_off + ((k ^ sw) << 4)),
                          "r"(o[4 * i]), "r"(o[4 * i + 1]), "r"(o[4 * i + 2]), "r"(o[4 * i + 3])
                          : "memory");
-        // Generic-proxy writes above, async-proxy (tensor store) reads below.
-        asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
-        __syncwarp();
-        if (lane == 0) {
-            if (m0 < p.M && co < p.Cout) tma_store_2d(tmap_y, (int32_t)co, (int32_t)m0, box);
-            bulk_commit();
+        }
+        if (part == E::kCPB - 1) {
+            // Generic-proxy writes above, async-proxy (tensor store) reads below.
+            asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+            __syncwarp();
+            if (lane == 0) {
+                const uint32_t xc = co0 + (uint32_t)(bx * E::kCols);
+                if (m0 < p.M && xc < p.Cout) tma_store_2d(tmap_y, (int32_t)xc, (int32_t)m0, box);
+                bulk_commit();
+            }
         }
     }
 }
@@ -426,7 +456,7 @@ __global__ void __launch_bounds__(kThreads, 1)
         // columns [half * BN/2, (half + 1) * BN/2).
         const uint32_t e = warp - 5u, qd = warp & 3u, half = e >> 2;
         const uint32_t col0 = half * (uint32_t)(BN / 2);
-        const uint32_t stg = smem_u32(staging) + e * (uint32_t)C::kWarpStaging;
+        const uint32_t stg = smem_u32(staging) + e * Epi<BN>::kWarpBytes;
         const int mode = epi_mode(p);
         if (lane == 0) tma_prefetch_map(&tmap_y);
         uint32_t acc = 0, acc_phase = 0;
@@ -438,8 +468,8 @@ __global__ void __launch_bounds__(kThreads, 1)
             if (!ok) break;
             tc_fence_after();
             uint64_t* te = &tempty[acc];
-            epilogue_rows<BN>(p, &tmap_y, tmem_base + ((qd * 32u) << 16) + acc * BN + col0,
-                              mb * 128u + qd * 32u, nb * BN + col0, stg, mode, lane, [&] {
+            epilogue_rows<BN>(p, &tmap_y, tmem_base + ((qd * 32u) << 16) + acc * BN + col0, mb * 128u + qd * 32u,
+                              nb * BN + col0, stg, mode, lane, [&] {
                                   tc_fence_before();
                                   __syncwarp();
                                   if (lane == 0) mbar_arrive(te);
@@ -465,33 +495,42 @@ __global__ void __launch_bounds__(kThreads, 1)
 
 // ------------------------------------------------------------------------
 // Weight-stationary 2-SM variant (tensor copies, Cout <= 256).  A CTA pair
-// (cluster of 2) computes 256-row tiles with tcgen05.mma.cta_group::2
-// (M = 256, N = BN): each CTA stages its own 128 output pixels of A per
-// k-block, and keeps its half of the weights (BN/2 output channels x all of
-// K) resident in shared memory for the whole kernel, loaded once.  Per
-// k-block only 16 KiB of A crosses L2 -> SM, against 16 KiB + BN x 128 B in
-// the streaming kernel above, whose feed (not the tensor pipe) bounds the
-// 3x3 stride-2 convolution.  Both CTAs' tensor copies complete on the
-// leader's barriers (cta_group::2 form); the leader issues the MMAs and
-// multicasts its commits to both CTAs; each CTA drains its own TMEM rows.
+// (cluster of 2) computes tiles of 256 kSub rows with tcgen05.mma.cta_group::2
+// (M = 256, N = BN): each CTA loads 128 kSub consecutive output pixels of A
+// per k-block with ONE im2col copy (kSub = 2 for BN <= 128, 1 for BN = 256,
+// bounded by TMEM: 2 buffers x kSub x BN columns <= 512), and keeps its half
+// of the weights (BN/2 output channels x all of K) resident in shared memory
+// for the whole kernel, loaded once.  Sub-tile s of a stage (rows 128 s ..
+// 128 s + 127 of both CTAs) is one M = 256 MMA group into accumulator s.
+// Per k-block and CTA the copy engine thus runs one ~295 ns instruction for
+// 128 kSub rows, against one im2col plus one weight copy per 128 rows in the
+// streaming kernel above.  Both CTAs' copies complete on the leader's
+// barriers (cta_group::2 form); the leader issues the MMAs and multicasts
+// its commits to both CTAs; each CTA drains its own TMEM rows.
 constexpr int kPairMaxStages = 8;
+
+template <int BN>
+struct PairCfg {
+    static constexpr int kSub = BN <= 128 ? 2 : 1;
+    static constexpr uint32_t kHalfB = (BN / 2) * 128;        // this CTA's weight rows of one k-block
+    static constexpr uint32_t kABytes = kSub * 128u * 128u;    // A rows of one stage
+    static constexpr uint32_t kTmemCols = 2u * kSub * BN;
+};
 
 template <int BN>
 __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
     conv_pair_kernel(const Params p, const __grid_constant__ CUtensorMap tmap_x,
                      const __grid_constant__ CUtensorMap tmap_w, const __grid_constant__ CUtensorMap tmap_y,
                      uint32_t stages) {
-    constexpr uint32_t kHalfB = (BN / 2) * 128;  // this CTA's weight rows of one k-block
-    constexpr uint32_t kABytes = 128 * 128;
-    constexpr uint32_t kWarpStaging = (BN / 64) * 2048;
-    constexpr uint32_t kTmemCols = 2 * BN;
+    using PC = PairCfg<BN>;
+    constexpr int kSub = PC::kSub;
     extern __shared__ uint8_t smem_raw[];
     uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) &
                                                ~uintptr_t(1023));
     uint8_t* b_res = smem;
-    uint8_t* a_st = b_res + p.num_kb * kHalfB;
-    uint8_t* staging = a_st + stages * kABytes;
-    uint64_t* full = reinterpret_cast<uint64_t*>(staging + kEpiWarps * kWarpStaging);
+    uint8_t* a_st = b_res + p.num_kb * PC::kHalfB;
+    uint8_t* staging = a_st + stages * PC::kABytes;
+    uint64_t* full = reinterpret_cast<uint64_t*>(staging + 256u * BN);
     uint64_t* empty = full + kPairMaxStages;
     uint64_t* tfull = empty + kPairMaxStages;
     uint64_t* tempty = tfull + 2;
@@ -511,7 +550,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
         }
         for (int b = 0; b < 2; ++b) {
             mbar_init(&tfull[b], 1);
-            mbar_init(&tempty[b], 2 * kEpiWarps);
+            mbar_init(&tempty[b], 2 * kEpiWarps * kSub);
         }
         mbar_init(bfull, 1);
         mbar_init(drain, 1);
@@ -522,7 +561,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
     if (warp == kMmaWarp) {
         asm volatile("tcgen05.alloc.cta_group::2.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(
                          smem_u32(tmem_slot)),
-                     "r"(kTmemCols)
+                     "r"(PC::kTmemCols)
                      : "memory");
         asm volatile("tcgen05.relinquish_alloc_permit.cta_group::2.sync.aligned;" ::: "memory");
     }
@@ -531,7 +570,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
     cluster_sync();
     tc_fence_after();
     const uint32_t tmem_base = *tmem_slot;
-    const uint32_t num_tiles = p.m_blocks;  // 256-row blocks
+    const uint32_t num_tiles = p.m_blocks;  // tiles of 256 kSub rows
 
     if (warp == 0) {
         if (lane == 0) {
@@ -541,12 +580,12 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
             const uint32_t lead_full0 = map_to_rank(&full[0], 0);
             // Resident weights: rows [rank * BN/2, (rank + 1) * BN/2) of the
             // K x Cout weight matrix, one box per k-block.
-            if (leader) mbar_expect_tx(bfull, 2u * p.num_kb * kHalfB);
+            if (leader) mbar_expect_tx(bfull, 2u * p.num_kb * PC::kHalfB);
             {
                 const uint32_t lead_bfull = map_to_rank(bfull, 0);
                 uint32_t kh = 0, kw = 0, cb = 0;
                 for (uint32_t kb = 0; kb < p.num_kb; ++kb) {
-                    tma_load_2d_pair(smem_u32(b_res) + kb * kHalfB, &tmap_w,
+                    tma_load_2d_pair(smem_u32(b_res) + kb * PC::kHalfB, &tmap_w,
                                      (int32_t)((kh * p.KW + kw) * p.Cin + cb * 64u), (int32_t)(rank * (BN / 2)),
                                      lead_bfull);
                     if (++cb == p.cblocks) {
@@ -564,7 +603,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
             for (uint32_t tile = pair_id; ok && tile < num_tiles; tile += num_pairs) {
                 // Base pixel (tap (0, 0)) of this CTA's first output pixel; past
                 // the last image it lies outside the tensor and reads zeros.
-                const uint32_t m0 = tile * 256u + rank * 128u, n = m0 / hw, rem = m0 - n * hw;
+                const uint32_t m0 = (tile * 2u + rank) * (128u * kSub), n = m0 / hw, rem = m0 - n * hw;
                 const uint32_t ho = rem / p.Wo, wo = rem - ho * p.Wo;
                 const int32_t w0 = (int32_t)(wo * p.stride) - (int32_t)p.pad;
                 const int32_t h0 = (int32_t)(ho * p.stride) - (int32_t)p.pad;
@@ -574,8 +613,8 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
                         ok = false;
                         break;
                     }
-                    if (leader) mbar_expect_tx(&full[stage], 2u * kABytes);
-                    tma_load_im2col_4d_pair(smem_u32(a_st + stage * kABytes), &tmap_x, (int32_t)(cb * 64u), w0,
+                    if (leader) mbar_expect_tx(&full[stage], 2u * PC::kABytes);
+                    tma_load_im2col_4d_pair(smem_u32(a_st + stage * PC::kABytes), &tmap_x, (int32_t)(cb * 64u), w0,
                                             h0, (int32_t)n, (uint16_t)kw, (uint16_t)kh, lead_full0 + stage * 8u);
                     if (++stage == stages) {
                         stage = 0;
@@ -604,19 +643,23 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
             for (uint32_t tile = pair_id; ok && tile < num_tiles; tile += num_pairs) {
                 if (!mbar_wait_cluster(&tempty[acc], acc_phase ^ 1u, abort_flag, p.err)) break;
                 tc_fence_after();
-                const uint32_t d_tmem = tmem_base + acc * BN;
+                const uint32_t d_tmem = tmem_base + acc * (uint32_t)(kSub * BN);
                 for (uint32_t kb = 0; kb < p.num_kb; ++kb) {
                     if (!mbar_wait_cluster(&full[stage], phase, abort_flag, p.err)) {
                         ok = false;
                         break;
                     }
                     tc_fence_after();
-                    const uint32_t a_addr = a0 + stage * kABytes, b_addr = b0 + kb * kHalfB;
+                    const uint32_t a_addr = a0 + stage * PC::kABytes, b_addr = b0 + kb * PC::kHalfB;
 #pragma unroll
-                    for (uint32_t s = 0; s < 4; ++s) {
-                        const uint64_t ad = kmaj | (uint64_t)(((a_addr + s * 32u) >> 4) & 0x3fffu);
-                        const uint64_t bd = kmaj | (uint64_t)(((b_addr + s * 32u) >> 4) & 0x3fffu);
-                        tc_mma_pair(d_tmem, ad, bd, idesc, (kb | s) != 0u);
+                    for (int sub = 0; sub < kSub; ++sub) {
+#pragma unroll
+                        for (uint32_t s = 0; s < 4; ++s) {
+                            const uint64_t ad =
+                                kmaj | (uint64_t)(((a_addr + sub * 16384u + s * 32u) >> 4) & 0x3fffu);
+                            const uint64_t bd = kmaj | (uint64_t)(((b_addr + s * 32u) >> 4) & 0x3fffu);
+                            tc_mma_pair(d_tmem + sub * BN, ad, bd, idesc, (kb | s) != 0u);
+                        }
                     }
                     tc_commit_pair_mc(&empty[stage], 0x3);
                     if (++stage == stages) {
@@ -636,17 +679,16 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
         }
     } else if (warp > kMmaWarp) {
         // ---------------------------------------------------- epilogue
-        // As in the streaming kernel, on this CTA's 128 rows of each 256-row
-        // tile; the accumulator is released on the leader's barrier.  The
-        // arrive only orders TMEM reads before the next MMAs, which the
-        // tcgen05 fences do, so it is relaxed: a release at cluster scope
-        // would first wait for this thread's global stores.
+        // As in the streaming kernel, on this CTA's 128 kSub rows of each
+        // tile (sub-tile s from accumulator s); the accumulators are released
+        // on the leader's barrier.  That arrive only orders TMEM reads before
+        // the next MMAs, which the tcgen05 fences do, so it is relaxed.
         const uint32_t e = warp - 5u, qd = warp & 3u, half = e >> 2;
         const uint32_t col0 = half * (uint32_t)(BN / 2);
-        const uint32_t stg = smem_u32(staging) + e * kWarpStaging;
+        const uint32_t stg = smem_u32(staging) + e * Epi<BN>::kWarpBytes;
         const int mode = epi_mode(p);
-        if (lane == 0) tma_prefetch_map(&tmap_y);
         const uint32_t lead_tempty0 = map_to_rank(&tempty[0], 0);
+        if (lane == 0) tma_prefetch_map(&tmap_y);
         uint32_t acc = 0, acc_phase = 0;
         for (uint32_t tile = pair_id; tile < num_tiles; tile += num_pairs) {
             bool ok = true;
@@ -655,12 +697,17 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
             if (!ok) break;
             tc_fence_after();
             const uint32_t te = lead_tempty0 + acc * 8u;
-            epilogue_rows<BN>(p, &tmap_y, tmem_base + ((qd * 32u) << 16) + acc * BN + col0,
-                              tile * 256u + rank * 128u + qd * 32u, col0, stg, mode, lane, [&] {
-                                  tc_fence_before();
-                                  __syncwarp();
-                                  if (lane == 0) mbar_arrive_remote_relaxed(te);
-                              });
+#pragma unroll 1
+            for (int sub = 0; sub < kSub; ++sub) {
+                const uint32_t m0 = (tile * 2u + rank) * (128u * kSub) + 128u * sub + qd * 32u;
+                epilogue_rows<BN>(p, &tmap_y,
+                                  tmem_base + ((qd * 32u) << 16) + acc * (uint32_t)(kSub * BN) + sub * BN + col0, m0,
+                                  col0, stg, mode, lane, [&] {
+                                      tc_fence_before();
+                                      __syncwarp();
+                                      if (lane == 0) mbar_arrive_remote_relaxed(te);
+                                  });
+            }
             if (++acc == 2) {
                 acc = 0;
                 acc_phase ^= 1u;
@@ -675,7 +722,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
     if (warp == kMmaWarp) {
         tc_fence_after();
         asm volatile("tcgen05.dealloc.cta_group::2.sync.aligned.b32 %0, %1;" ::"r"(tmem_base),
-                     "r"(kTmemCols)
+                     "r"(PC::kTmemCols)
                      : "memory");
     }
 }
@@ -711,8 +758,9 @@ static int launch_bn(const Params& p, const CUtensorMap& mx, const CUtensorMap& 
 // Shared memory of the pair kernel: resident weights, `stages` A stages,
 // epilogue staging, barriers (+ 1 KiB alignment slack).
 static uint32_t pair_smem_bytes(const Params& p, int bn, uint32_t stages) {
-    return p.num_kb * (uint32_t)(bn / 2) * 128u + stages * 16384u + kEpiWarps * (uint32_t)(bn / 64) * 2048u +
-           1024u + 256u;
+    const uint32_t sub = bn <= 128 ? 2u : 1u;
+    return p.num_kb * (uint32_t)(bn / 2) * 128u + stages * sub * 16384u + 256u * (uint32_t)bn + 1024u +
+           (uint32_t)kBarrierBytes;
 }
 
 template <int BN>
@@ -778,9 +826,10 @@ static const Encoders& encoders() {
 // The tensor-copy producer serves Cin a multiple of 64 (one 128-byte channel
 // run per k-block) with a traversal stride the copy engine supports (<= 8)
 // and byte strides below 2^40; other shapes use the gather producer.
-// FOIL_CONV_PRODUCER=gather selects the gather producer for every shape, and
-// FOIL_CONV_PRODUCER=single the tensor-copy producer in the single-CTA
-// kernel (A/B comparisons of the variants, which agree bit for bit).
+// FOIL_CONV_PRODUCER=gather selects the gather producer for every shape,
+// =single the tensor-copy producer in the single-CTA kernel, and =pair the
+// pair kernel wherever it can run (A/B comparisons of the variants, which
+// agree bit for bit).
 static const char* producer_override() {
     static const char* v = getenv("FOIL_CONV_PRODUCER");
     return v ? v : "";
@@ -791,23 +840,25 @@ static bool use_tensor_copies(const Params& p) {
            (uint64_t)p.H * p.W * p.Cin * 2 < (1ull << 40);
 }
 
-// Output y as an M x Cout matrix, stored in boxes of 32 rows x 32 columns
-// from the epilogue's swizzled staging.
-static bool encode_output_map(const Params& p, CUtensorMap* my) {
+// Output y as an M x Cout matrix, stored in boxes of 32 rows x 64 columns
+// (SWIZZLE_128B) for BN >= 128, else 32 columns (SWIZZLE_64B), matching the
+// epilogue's staging.
+static bool encode_output_map(const Params& p, int bn, CUtensorMap* my) {
     const Encoders& e = encoders();
     if (!e.tiled) return false;
+    const bool wide = bn >= 128;
     const cuuint64_t ydim[2] = {p.Cout, p.M};
     const cuuint64_t ystr[1] = {(cuuint64_t)p.Cout * 2};
-    const cuuint32_t box[2] = {32, 32};
+    const cuuint32_t box[2] = {wide ? 64u : 32u, 32};
     const cuuint32_t one[2] = {1, 1};
     return e.tiled(my, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, p.y, ydim, ystr, box, one,
-                   CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_64B,
+                   CU_TENSOR_MAP_INTERLEAVE_NONE, wide ? CU_TENSOR_MAP_SWIZZLE_128B : CU_TENSOR_MAP_SWIZZLE_64B,
                    CU_TENSOR_MAP_L2_PROMOTION_NONE, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
 }
 
 // A (im2col of x) and weights as a K x Cout matrix read in boxes of 64
 // channels x `w_rows` output channels (BN, or BN/2 per CTA of a pair).
-static bool encode_maps(const Params& p, uint32_t w_rows, CUtensorMap* mx, CUtensorMap* mw) {
+static bool encode_maps(const Params& p, uint32_t w_rows, uint32_t pixels, CUtensorMap* mx, CUtensorMap* mw) {
     const Encoders& e = encoders();
     if (!e.im2col || !e.tiled) return false;
     // Dims and byte strides innermost first: C, W, H, N.
@@ -820,7 +871,7 @@ static bool encode_maps(const Params& p, uint32_t w_rows, CUtensorMap* mx, CUten
     const int upper[2] = {(int)p.pad - (int)(p.KW - 1), (int)p.pad - (int)(p.KH - 1)};
     const cuuint32_t trav[4] = {1, p.stride, p.stride, 1};
     if (e.im2col(mx, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 4, const_cast<uint16_t*>(p.x), xdim, xstr, lower,
-                 upper, 64, 128, trav, CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
+                 upper, 64, pixels, trav, CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
                  CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) != CUDA_SUCCESS)
         return false;
     // Weights as a K x Cout matrix (K = KH * KW * Cin contiguous per row).
@@ -867,7 +918,7 @@ int launch(const uint16_t* x, const uint16_t* w, const uint16_t* bias, uint16_t*
     memset(&mx, 0, sizeof mx);
     memset(&mw, 0, sizeof mw);
     const bool tc = use_tensor_copies(p);
-    if (!encode_output_map(p, &my)) {
+    if (!encode_output_map(p, bn, &my)) {
         foil_set_error(FOIL_ERR_CUDA, "foil_conv2d_nhwc: tensor-map encoding failed");
         return FOIL_ERR_CUDA;
     }
@@ -882,15 +933,25 @@ int launch(const uint16_t* x, const uint16_t* w, const uint16_t* bias, uint16_t*
     }
     uint32_t stages = 0;
     while (stages < (uint32_t)kPairMaxStages && pair_smem_bytes(p, bn, stages + 1) <= (uint32_t)optin) ++stages;
-    const bool pair = p.n_blocks == 1 && p.M > 128 && stages >= 4 && max_ctas >= 2 &&
-                      strcmp(producer_override(), "single") != 0;
-    if (!encode_maps(p, pair ? (uint32_t)bn / 2 : (uint32_t)bn, &mx, &mw)) {
+    // The pair kernel pays ~1 us more start-up (cluster launch, resident
+    // weights); it needs one column block and at least 3 A stages beside the
+    // resident weights.
+    const bool pair_ok = p.n_blocks == 1 && p.M > 128 && stages >= 3 && max_ctas >= 2;
+    // Measured: the pair kernel wins on the 3x3 stride-2 batch-32 convolution
+    // (9 k-blocks; 23.5 against 31.5 us) and loses on the 1x1 one (2
+    // k-blocks; 18.8 against 16.8 us), where weights are a small share of the
+    // operand copies and the start-up is not amortised.
+    const bool pair = pair_ok && strcmp(producer_override(), "single") != 0 &&
+                      (strcmp(producer_override(), "pair") == 0 ||
+                       (p.num_kb >= 4 && p.m_blocks >= (uint32_t)max_ctas));
+    const uint32_t sub = bn <= 128 ? 2u : 1u;
+    if (!encode_maps(p, pair ? (uint32_t)bn / 2 : (uint32_t)bn, pair ? 128u * sub : 128u, &mx, &mw)) {
         foil_set_error(FOIL_ERR_CUDA, "foil_conv2d_nhwc: tensor-map encoding failed");
         return FOIL_ERR_CUDA;
     }
     if (pair) {
         Params q = p;
-        q.m_blocks = (p.M + 255) / 256;
+        q.m_blocks = (p.M + 256u * sub - 1u) / (256u * sub);
         switch (bn) {
             case 64: return launch_pair<64>(q, stages, mx, mw, my, stream, max_ctas, optin);
             case 128: return launch_pair<128>(q, stages, mx, mw, my, stream, max_ctas, optin);
