@@ -17,6 +17,20 @@ roofline   GEMM FLOPs per launch / mean launch time against the measured bf16
            peak (MEASURED_PEAKS.json).
 cpu_baseline  the oracle (the reference golden's loop nest, oracle/golden.cpp)
            on a bounded sample of output rows, all host threads, rank 0, N=1.
+secondary  the other parts of the metric, each on every rank with CUDA events
+           (max over ranks; values summed over ranks):
+           conv   3x3 s1 56^2x64->64 (N=1) and the batch-32 pair 3x3 s2
+                  112^2x64->128 + 1x1 56^2x128->256, bias+relu, batch sharded
+                  over ranks; TFLOP/s and algorithmic HBM GB/s against the
+                  measured HBM peak (both convolutions are HBM-bound: the
+                  working set is below L2, so L2 is flushed before each timed
+                  launch: a 256 MiB buffer written, then another read);
+           gemm   4096^3 and 16384^3 per rank, 65536x8192x8192 M-sharded;
+           eltwise tilize / untilize 16384^2, add_tiles / bias_add / relu on
+                  2^28 elements, tile_copy of 1 GiB: GB/s of algorithmic
+                  traffic against the measured HBM peak;
+           cpu    the oracle restatements of the conv and elementwise goldens
+                  on bounded samples (rank 0, N=1).
 
 --impl reference times the reference's CPU golden implementation of the same
 workload (the oracle port; see the cpu_baseline note) and prints its line.
@@ -50,6 +64,7 @@ def parse():
     ap.add_argument("--e2e-steps", type=int, default=20)
     ap.add_argument("--cpu-seconds", type=float, default=12.0)
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--no-secondary", action="store_true")
     return ap.parse_args()
 
 
@@ -305,9 +320,13 @@ def run_ours(args, dist):
 
     e2e = run_e2e(args, dist, flops)
 
+    secondary = None if args.no_secondary else run_secondary(dist, pk)
+
     cpu = None
     if dist.rank == 0 and dist.world == 1 and not args.no_cpu_baseline:
         cpu = cpu_gemm_baseline(args.cpu_seconds, host_threads())
+        if secondary is not None:
+            secondary["cpu"] = cpu_secondary_baseline(host_threads())
 
     if dist.rank == 0:
         line = {"metric": METRIC, "value": value, "unit": "TFLOP/s", "n_gpus": dist.world,
@@ -321,10 +340,153 @@ def run_ours(args, dist):
                            "parallelism": f"M-shard x{dist.world}",
                            "l2": "operands 384 MiB per GPU > 126 MB L2, no flush"},
                 "roofline": roofline, "cpu_baseline": cpu, "e2e": e2e, "clocks": clk,
-                "gpu_launches": launches, "parity_spot_check": check}
+                "gpu_launches": launches, "parity_spot_check": check, "secondary": secondary}
         if allgather:
             line["allgather"] = allgather
         print(json.dumps(line), flush=True)
+
+
+def _timed(torch, fn, iters, flush=None, warmup=3):
+    """Mean device time (ms) of fn over `iters` launches on the current
+    stream.  With `flush` (two 256 MiB buffers), before each launch and
+    outside the timed interval one buffer is rewritten and the other read, so
+    that no operand starts in L2 and the rewrite's dirty lines have been
+    written back before the timed launch."""
+    for _ in range(warmup):
+        fn()
+    torch.cuda.synchronize()
+    evs = []
+    for _ in range(iters):
+        if flush is not None:
+            flush[0].add_(1)
+            flush[1].sum()
+        e0 = torch.cuda.Event(enable_timing=True)
+        e1 = torch.cuda.Event(enable_timing=True)
+        e0.record()
+        fn()
+        e1.record()
+        evs.append((e0, e1))
+    torch.cuda.synchronize()
+    return statistics.mean(a.elapsed_time(b) for a, b in evs)
+
+
+def run_secondary(dist, pk):
+    """Conv, GEMM-sweep and memory-bound numbers of the metric (see the module
+    docstring).  Every rank runs the same launches; times are max over ranks."""
+    import torch
+    import ttfoil
+
+    dev = torch.device("cuda", dist.local)
+    g = torch.Generator(device=dev).manual_seed(777 + dist.rank)
+    hbm = pk["hbm_gbs"]
+
+    def rnd(n, scale=1.0):
+        return ((torch.rand(n, device=dev, generator=g) * 2 - 1) * scale).to(torch.bfloat16)
+
+    flush = (torch.zeros(256 << 18, dtype=torch.int32, device=dev),   # 2 x 256 MiB > L2
+             torch.ones(256 << 18, dtype=torch.int32, device=dev))
+    out = {}
+
+    # ---- conv (configs: 3x3 s1 N=1, and the batch-32 pair sharded by batch)
+    def conv_case(N, H, Cin, Cout, k, stride, pad, x=None):
+        Ho = (H + 2 * pad - k) // stride + 1
+        x = rnd(N * H * H * Cin) if x is None else x
+        w = rnd(Cout * k * k * Cin, (2.0 / (k * k * Cin)) ** 0.5)
+        b = rnd(Cout, 0.1)
+        y = torch.empty(N * Ho * Ho * Cout, dtype=torch.bfloat16, device=dev)
+        fn = lambda: ttfoil.conv2d_nhwc(x, w, b, y, N, H, H, Cin, Cout, k, k, stride, pad, relu=True)
+        ms = dist.max(_timed(torch, fn, 20, flush))
+        flops = 2.0 * N * Ho * Ho * Cout * k * k * Cin
+        nbytes = 2.0 * (N * H * H * Cin + Cout * k * k * Cin + Cout + N * Ho * Ho * Cout)
+        gbs = dist.world * nbytes / (ms / 1e3) / 1e9
+        return y, {"us": ms * 1e3, "TFLOPs": dist.world * flops / (ms / 1e3) / 1e12,
+                   "hbm_GBps": gbs, "hbm_frac": gbs / (dist.world * hbm), "bound": "hbm",
+                   "algorithmic_bytes_per_rank": nbytes, "flops_per_rank": flops}
+
+    _, c2 = conv_case(1, 56, 64, 64, 3, 1, 1)
+    nb = max(1, 32 // dist.world)
+    y1, c3a = conv_case(nb, 112, 64, 128, 3, 2, 1)
+    _, c3b = conv_case(nb, 56, 128, 256, 1, 1, 0, x=y1)
+    pair_us = c3a["us"] + c3b["us"]
+    pair_flops = dist.world * (c3a["flops_per_rank"] + c3b["flops_per_rank"])
+    out["conv"] = {"conv3x3_s1_56x56x64_n1": c2,
+                   "conv3x3_s2_112x112x64to128": dict(c3a, batch_per_rank=nb),
+                   "conv1x1_56x56x128to256": dict(c3b, batch_per_rank=nb),
+                   "pair_TFLOPs": pair_flops / (pair_us / 1e6) / 1e12,
+                   "pair_us": pair_us, "global_batch": nb * dist.world,
+                   "l2": "flushed before each timed launch (256 MiB written, another 256 MiB read)"}
+
+    # ---- GEMM sweep (config 4): square per rank, tall M-sharded
+    sweep = {}
+    for name, (M, K, N) in {"4096^3": (4096, 4096, 4096), "16384^3": (16384, 16384, 16384),
+                            "65536x8192x8192": (65536 // dist.world, 8192, 8192)}.items():
+        a, b = rnd(M * K), rnd(K * N)
+        c = torch.empty(M * N, dtype=torch.bfloat16, device=dev)
+        fn = lambda: ttfoil.matmul_tiles(a, b, c, M // 32, K // 32, N // 32)
+        small = 2 * (M * K + K * N + M * N) < (128 << 20)
+        ms = dist.max(_timed(torch, fn, 10 if M * N * K > 2 ** 40 else 30, flush if small else None))
+        t = dist.world * 2.0 * M * N * K / (ms / 1e3) / 1e12
+        sweep[name] = {"M_per_rank": M, "N": N, "K": K, "ms": ms, "TFLOPs": t,
+                       "frac_of_peak": t / (dist.world * pk["bf16_tflops"])}
+        del a, b, c
+    out["gemm_sweep"] = sweep
+
+    # ---- memory-bound sweep (config 5)
+    elt = {}
+    R = C = 16384
+    x, y = rnd(R * C), torch.empty(R * C, dtype=torch.bfloat16, device=dev)
+    for name, fn in (("tilize_16384^2", lambda: ttfoil.tilize(x, y, R, C)),
+                     ("untilize_16384^2", lambda: ttfoil.untilize(x, y, R, C))):
+        ms = dist.max(_timed(torch, fn, 10))
+        elt[name] = 4.0 * R * C / (ms / 1e3) / 1e9
+    band = rnd(32 * C)
+    ms = dist.max(_timed(torch, lambda: ttfoil.bias_add_tiles(x, band, y, R, C), 10))
+    elt["bias_add_2^28"] = (4.0 * R * C + 64.0 * C) / (ms / 1e3) / 1e9
+    n = 1 << 28
+    z = rnd(n)
+    ms = dist.max(_timed(torch, lambda: ttfoil.add_tiles(x, z, y, n), 10))
+    elt["add_tiles_2^28"] = 6.0 * n / (ms / 1e3) / 1e9
+    ms = dist.max(_timed(torch, lambda: ttfoil.relu_tiles(x, y, n), 10))
+    elt["relu_2^28"] = 4.0 * n / (ms / 1e3) / 1e9
+    del x, y, z, band
+    nbytes = 1 << 30
+    src = torch.empty(nbytes // 2, dtype=torch.int16, device=dev).random_(generator=g)
+    dst = torch.empty_like(src)
+    ms = dist.max(_timed(torch, lambda: ttfoil.tile_copy(src, dst, nbytes), 10))
+    elt["tile_copy_1GiB"] = 2.0 * nbytes / (ms / 1e3) / 1e9
+    del src, dst
+    out["eltwise_GBps_per_gpu"] = elt
+    out["eltwise_frac_of_hbm"] = {k: v / hbm for k, v in elt.items()}
+    assert ttfoil.device_error() == 0
+    return out
+
+
+def cpu_secondary_baseline(threads):
+    """Oracle restatements of the conv and elementwise goldens on bounded
+    samples: one image of the 3x3 s2 conv, a 4096^2 tilize, 2^24-element add."""
+    from oracle import oracle
+    res = {"cores": threads, "kind": "port"}
+    x = oracle.rand_bf16((1, 112, 112, 64), 3)
+    w = oracle.randn_bf16((128, 3, 3, 64), 31, (2.0 / 576) ** 0.5)
+    b = oracle.rand_bf16((128,), 32, -0.1, 0.1)
+    t0 = time.perf_counter()
+    oracle.conv_nhwc(x, w, b, 2, 1, relu=True, threads=threads)
+    el = time.perf_counter() - t0
+    res["conv3x3_s2_TFLOPs"] = 2.0 * 56 * 56 * 128 * 576 / el / 1e12
+    res["conv_sample"] = f"1 image of 112^2x64->128 3x3 s2, {el:.2f} s"
+    m = oracle.rand_bf16((4096, 4096), 5)
+    t0 = time.perf_counter()
+    oracle.tilize(m)
+    el = time.perf_counter() - t0
+    res["tilize_GBps"] = 4.0 * 4096 * 4096 / el / 1e9
+    a = oracle.rand_bf16((1 << 24,), 6)
+    c = oracle.rand_bf16((1 << 24,), 7)
+    t0 = time.perf_counter()
+    oracle.add(a, c)
+    el = time.perf_counter() - t0
+    res["add_GBps"] = 6.0 * (1 << 24) / el / 1e9
+    res["eltwise_sample"] = "4096^2 tilize, 2^24-element add_tiles (single-threaded golden loops)"
+    return res
 
 
 def bits(t):

@@ -24,30 +24,52 @@ sys.path.insert(0, os.path.dirname(HERE))
 import ttfoil  # noqa: E402
 
 
+_FLUSH = None
+
+
 def _time(torch, fn, iters, warmup=3):
+    """Mean ms per launch: back to back, or with --flush L2 flushed before
+    each launch (256 MiB written, another 256 MiB read, outside the timing)."""
     for _ in range(warmup):
         fn()
     torch.cuda.synchronize()
-    e0 = torch.cuda.Event(enable_timing=True)
-    e1 = torch.cuda.Event(enable_timing=True)
-    e0.record()
+    if _FLUSH is None:
+        e0 = torch.cuda.Event(enable_timing=True)
+        e1 = torch.cuda.Event(enable_timing=True)
+        e0.record()
+        for _ in range(iters):
+            fn()
+        e1.record()
+        torch.cuda.synchronize()
+        return e0.elapsed_time(e1) / iters
+    evs = []
     for _ in range(iters):
+        _FLUSH[0].add_(1)
+        _FLUSH[1].sum()
+        e0 = torch.cuda.Event(enable_timing=True)
+        e1 = torch.cuda.Event(enable_timing=True)
+        e0.record()
         fn()
-    e1.record()
+        e1.record()
+        evs.append((e0, e1))
     torch.cuda.synchronize()
-    return e0.elapsed_time(e1) / iters
+    return sum(a.elapsed_time(b) for a, b in evs) / iters
 
 
 def run(kind, args):
     import torch
+    global _FLUSH
     torch.cuda.set_device(0)
     dev = torch.device("cuda", 0)
+    if args.flush:
+        _FLUSH = (torch.zeros(1 << 26, dtype=torch.int32, device=dev),
+                  torch.ones(1 << 26, dtype=torch.int32, device=dev))
     g = torch.Generator(device=dev).manual_seed(0)
 
     def rnd(n):
         return (torch.rand(n, device=dev, generator=g) * 2 - 1).to(torch.bfloat16)
 
-    res = {"kernel": kind}
+    res = {"kernel": kind, "l2": "flushed" if args.flush else "back-to-back"}
     if kind == "gemm":
         M, N, K = args.m, args.n, args.k
         a, b = rnd(M * K), rnd(K * N)
@@ -121,6 +143,7 @@ def main():
     ap.add_argument("--iters", type=int, default=20)
     ap.add_argument("--bias", action="store_true")
     ap.add_argument("--relu", action="store_true")
+    ap.add_argument("--flush", action="store_true", help="flush L2 before each timed launch")
     ap.add_argument("--batch", type=int, default=1)
     ap.add_argument("--hw", type=int, default=56)
     ap.add_argument("--cin", type=int, default=64)
