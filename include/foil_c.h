@@ -298,6 +298,38 @@ FOIL_API int foil_matmul_tiles_noalloc_dev(const uint16_t* a, const uint16_t* b,
  * Synchronizes `stream`. */
 FOIL_API int foil_device_error_dev(void* stream, uint32_t* out_error);
 
+/* Tiled GEMM on host buffers, pipelined: C (Mt x Nt tiles) = A (Mt x Kt) .
+ * B (Kt x Nt), tile streams in host memory, optional bias (Nt * 32 values,
+ * one per output column, NULL for none) and relu as in
+ * foil_matmul_tiles_dev, on CUDA device `device`.  B is copied first, then A
+ * in chunks of `chunk_rows` tile rows (0 = about 8 chunks, at least 8 rows):
+ * the copy of chunk i + 1 and the read-back of chunk i - 1 overlap the GEMM
+ * of chunk i, and host-to-device and device-to-host copies run at the same
+ * time.  Blocking: returns when C is in host memory.  Replaces the
+ * reference's blocking sequence write_buffer(A), write_buffer(B), execute,
+ * read_buffer(C) (include/tt_foil/runtime.hpp:91, :132, :94;
+ * tests/test_matmul_dram.cpp:163-208).  Host buffers should be page-locked
+ * for the copies to overlap; pageable buffers work but serialize.  Device
+ * buffers are cached per device and grow as needed (one call at a time per
+ * device; foil_host_pipeline_release frees them). */
+FOIL_API int foil_matmul_tiles_host(int32_t device, const uint16_t* a, const uint16_t* b, uint16_t* c,
+                                    uint32_t Mt, uint32_t Kt, uint32_t Nt, const uint16_t* bias,
+                                    int32_t relu, uint32_t chunk_rows);
+
+/* NHWC convolution on host buffers, pipelined over chunks of `chunk_images`
+ * images (0 = about 8 chunks) as foil_matmul_tiles_host; arguments as
+ * foil_conv2d_nhwc_dev.  Replaces the reference conv tests' write_buffer /
+ * execute / read_buffer sequence around the host im2col
+ * (tests/test_conv_3x3.cpp:236-279). */
+FOIL_API int foil_conv2d_nhwc_host(int32_t device, const uint16_t* x, const uint16_t* w,
+                                   const uint16_t* bias, uint16_t* y, uint32_t N, uint32_t H,
+                                   uint32_t W, uint32_t Cin, uint32_t Cout, uint32_t KH, uint32_t KW,
+                                   uint32_t stride, uint32_t pad, int32_t relu,
+                                   uint32_t chunk_images);
+
+/* Free the device buffers cached by the host pipelines on `device`. */
+FOIL_API int foil_host_pipeline_release(int32_t device);
+
 #ifdef __cplusplus
 }  /* extern "C" */
 #endif

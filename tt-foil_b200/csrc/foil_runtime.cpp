@@ -18,6 +18,7 @@
 #include <cuda_runtime.h>
 #include <cudaTypedefs.h>
 
+#include <algorithm>
 #include <atomic>
 #include <chrono>
 #include <cstring>
@@ -692,6 +693,174 @@ extern "C" int foil_conv2d_nhwc_dev(const uint16_t* x, const uint16_t* w, const 
         uint32_t* err = error_word_for_current_device();
         throw_status(foil::conv::launch(x, w, bias, y, N, H, W, Cin, Cout, KH, KW, stride, pad, relu, err,
                                         (cudaStream_t)stream, sm_count_current()));
+    });
+}
+
+// ------------------------------------------------ host-buffer pipelines ---
+// One set of streams, events and grow-only device buffers per device: h2d
+// (inputs), comp (kernels) and d2h (outputs), so that the copy of chunk i + 1
+// and the read-back of chunk i - 1 overlap the kernel of chunk i, and H2D and
+// D2H run at the same time on the full-duplex link.
+namespace {
+struct HostPipe {
+    std::mutex mu;
+    cudaStream_t h2d = nullptr, comp = nullptr, d2h = nullptr;
+    std::vector<cudaEvent_t> ev;
+    void* buf[4] = {};
+    size_t cap[4] = {};
+};
+HostPipe g_pipes[64];
+
+HostPipe& pipe_for(int32_t device) {
+    if (device < 0 || device >= 64) throw FoilError(FOIL_ERR_INVALID, "tt-foil: device ordinal out of range");
+    int count = 0;
+    cuda_check(cudaGetDeviceCount(&count), "cudaGetDeviceCount");
+    if (device >= count) throw FoilError(FOIL_ERR_INVALID, "tt-foil: no such CUDA device");
+    cuda_check(cudaSetDevice(device), "cudaSetDevice");
+    return g_pipes[device];
+}
+
+void pipe_init(HostPipe& hp) {
+    if (hp.h2d) return;
+    cuda_check(cudaStreamCreateWithFlags(&hp.h2d, cudaStreamNonBlocking), "cudaStreamCreate");
+    cuda_check(cudaStreamCreateWithFlags(&hp.comp, cudaStreamNonBlocking), "cudaStreamCreate");
+    cuda_check(cudaStreamCreateWithFlags(&hp.d2h, cudaStreamNonBlocking), "cudaStreamCreate");
+}
+
+void* pipe_buffer(HostPipe& hp, int slot, size_t bytes) {
+    if (hp.cap[slot] < bytes) {
+        if (hp.buf[slot]) cuda_check(cudaFree(hp.buf[slot]), "cudaFree");
+        hp.buf[slot] = nullptr;
+        hp.cap[slot] = 0;
+        if (cudaMalloc(&hp.buf[slot], bytes) != cudaSuccess) {
+            cudaGetLastError();
+            throw FoilError(FOIL_ERR_OOM, "tt-foil: out of device memory for the host pipeline");
+        }
+        hp.cap[slot] = bytes;
+    }
+    return hp.buf[slot];
+}
+
+cudaEvent_t pipe_event(HostPipe& hp, size_t i) {
+    while (hp.ev.size() <= i) {
+        cudaEvent_t e;
+        cuda_check(cudaEventCreateWithFlags(&e, cudaEventDisableTiming), "cudaEventCreate");
+        hp.ev.push_back(e);
+    }
+    return hp.ev[i];
+}
+
+// Waits for the pipeline's last read-back, then reads and clears the device
+// error word (bounded waits that expired in any chunk's kernel).
+void pipe_finish(HostPipe& hp, const char* what) {
+    cuda_check(cudaStreamSynchronize(hp.d2h), "cudaStreamSynchronize");
+    cuda_check(cudaStreamSynchronize(hp.comp), "cudaStreamSynchronize");
+    uint32_t* err = error_word_for_current_device();
+    uint32_t word = 0;
+    cuda_check(cudaMemcpy(&word, err, 4, cudaMemcpyDeviceToHost), "read error word");
+    if (word) {
+        cuda_check(cudaMemset(err, 0, 4), "clear error word");
+        throw FoilError(FOIL_ERR_DEVICE, std::string(what) + ": a bounded device wait expired");
+    }
+}
+}  // namespace
+
+extern "C" int foil_matmul_tiles_host(int32_t device, const uint16_t* a, const uint16_t* b, uint16_t* c,
+                                      uint32_t Mt, uint32_t Kt, uint32_t Nt, const uint16_t* bias, int32_t relu,
+                                      uint32_t chunk_rows) {
+    return guarded([&] {
+        if (Mt == 0 || Kt == 0 || Nt == 0) return;
+        if (Mt > 65535 || Kt > 65535 || Nt > 65535)
+            throw FoilError(FOIL_ERR_INVALID, "foil_matmul_tiles_host: tile counts must be <= 65535");
+        if (!a || !b || !c) throw FoilError(FOIL_ERR_INVALID, "foil_matmul_tiles_host: null pointer");
+        HostPipe& hp = pipe_for(device);
+        std::lock_guard<std::mutex> lk(hp.mu);
+        pipe_init(hp);
+        const size_t tile = 1024;  // elements per 32 x 32 tile
+        uint16_t* dA = static_cast<uint16_t*>(pipe_buffer(hp, 0, (size_t)Mt * Kt * tile * 2));
+        uint16_t* dB = static_cast<uint16_t*>(pipe_buffer(hp, 1, (size_t)Kt * Nt * tile * 2));
+        uint16_t* dC = static_cast<uint16_t*>(pipe_buffer(hp, 2, (size_t)Mt * Nt * tile * 2));
+        uint16_t* dBias = bias ? static_cast<uint16_t*>(pipe_buffer(hp, 3, (size_t)Nt * 32 * 2)) : nullptr;
+        uint32_t* err = error_word_for_current_device();
+        const int sms = sm_count_current();
+        // Chunks of 8 tile rows (one 2-SM row block) or more, about 8 chunks.
+        uint32_t chunk = chunk_rows ? chunk_rows : std::max<uint32_t>(8u, (Mt / 8u + 7u) / 8u * 8u);
+        cuda_check(cudaMemcpyAsync(dB, b, (size_t)Kt * Nt * tile * 2, cudaMemcpyHostToDevice, hp.h2d), "copy B");
+        if (bias) cuda_check(cudaMemcpyAsync(dBias, bias, (size_t)Nt * 64, cudaMemcpyHostToDevice, hp.h2d), "copy bias");
+        size_t e = 0;
+        for (uint32_t r0 = 0; r0 < Mt; r0 += chunk) {
+            const uint32_t rows = std::min(chunk, Mt - r0);
+            const size_t ao = (size_t)r0 * Kt * tile, co = (size_t)r0 * Nt * tile;
+            cuda_check(cudaMemcpyAsync(dA + ao, a + ao, (size_t)rows * Kt * tile * 2, cudaMemcpyHostToDevice,
+                                       hp.h2d), "copy A chunk");
+            cudaEvent_t in = pipe_event(hp, e++), done = pipe_event(hp, e++);
+            cuda_check(cudaEventRecord(in, hp.h2d), "cudaEventRecord");
+            cuda_check(cudaStreamWaitEvent(hp.comp, in, 0), "cudaStreamWaitEvent");
+            throw_status(foil::gemm::launch(dA + ao, dB, dC + co, rows, Kt, Nt, dBias, relu, err, hp.comp, sms));
+            cuda_check(cudaEventRecord(done, hp.comp), "cudaEventRecord");
+            cuda_check(cudaStreamWaitEvent(hp.d2h, done, 0), "cudaStreamWaitEvent");
+            cuda_check(cudaMemcpyAsync(c + co, dC + co, (size_t)rows * Nt * tile * 2, cudaMemcpyDeviceToHost,
+                                       hp.d2h), "copy C chunk");
+        }
+        pipe_finish(hp, "foil_matmul_tiles_host");
+    });
+}
+
+extern "C" int foil_conv2d_nhwc_host(int32_t device, const uint16_t* x, const uint16_t* w, const uint16_t* bias,
+                                     uint16_t* y, uint32_t N, uint32_t H, uint32_t W, uint32_t Cin, uint32_t Cout,
+                                     uint32_t KH, uint32_t KW, uint32_t stride, uint32_t pad, int32_t relu,
+                                     uint32_t chunk_images) {
+    return guarded([&] {
+        if (N == 0 || Cout == 0) return;
+        if (!x || !w || !y) throw FoilError(FOIL_ERR_INVALID, "foil_conv2d_nhwc_host: null pointer");
+        if (H == 0 || W == 0 || KH == 0 || KW == 0 || stride == 0 || H + 2 * pad < KH || W + 2 * pad < KW)
+            throw FoilError(FOIL_ERR_INVALID, "foil_conv2d_nhwc_host: unsupported kernel / stride / padding");
+        HostPipe& hp = pipe_for(device);
+        std::lock_guard<std::mutex> lk(hp.mu);
+        pipe_init(hp);
+        const uint64_t Ho = (H + 2 * pad - KH) / stride + 1, Wo = (W + 2 * pad - KW) / stride + 1;
+        const size_t x_img = (size_t)H * W * Cin, y_img = (size_t)Ho * Wo * Cout;
+        uint16_t* dX = static_cast<uint16_t*>(pipe_buffer(hp, 0, (size_t)N * x_img * 2));
+        uint16_t* dW = static_cast<uint16_t*>(pipe_buffer(hp, 1, (size_t)Cout * KH * KW * Cin * 2));
+        uint16_t* dY = static_cast<uint16_t*>(pipe_buffer(hp, 2, (size_t)N * y_img * 2));
+        uint16_t* dBias = bias ? static_cast<uint16_t*>(pipe_buffer(hp, 3, (size_t)Cout * 2)) : nullptr;
+        uint32_t chunk = chunk_images ? chunk_images : std::max<uint32_t>(1u, (N + 7u) / 8u);
+        cuda_check(cudaMemcpyAsync(dW, w, (size_t)Cout * KH * KW * Cin * 2, cudaMemcpyHostToDevice, hp.h2d),
+                   "copy weights");
+        if (bias) cuda_check(cudaMemcpyAsync(dBias, bias, (size_t)Cout * 2, cudaMemcpyHostToDevice, hp.h2d), "copy bias");
+        size_t e = 0;
+        for (uint32_t n0 = 0; n0 < N; n0 += chunk) {
+            const uint32_t imgs = std::min(chunk, N - n0);
+            cuda_check(cudaMemcpyAsync(dX + n0 * x_img, x + n0 * x_img, imgs * x_img * 2, cudaMemcpyHostToDevice,
+                                       hp.h2d), "copy x chunk");
+            cudaEvent_t in = pipe_event(hp, e++), done = pipe_event(hp, e++);
+            cuda_check(cudaEventRecord(in, hp.h2d), "cudaEventRecord");
+            cuda_check(cudaStreamWaitEvent(hp.comp, in, 0), "cudaStreamWaitEvent");
+            throw_status(foil_conv2d_nhwc_dev(dX + n0 * x_img, dW, dBias, dY + n0 * y_img, imgs, H, W, Cin, Cout, KH,
+                                              KW, stride, pad, relu, hp.comp));
+            cuda_check(cudaEventRecord(done, hp.comp), "cudaEventRecord");
+            cuda_check(cudaStreamWaitEvent(hp.d2h, done, 0), "cudaStreamWaitEvent");
+            cuda_check(cudaMemcpyAsync(y + n0 * y_img, dY + n0 * y_img, imgs * y_img * 2, cudaMemcpyDeviceToHost,
+                                       hp.d2h), "copy y chunk");
+        }
+        pipe_finish(hp, "foil_conv2d_nhwc_host");
+    });
+}
+
+extern "C" int foil_host_pipeline_release(int32_t device) {
+    return guarded([&] {
+        HostPipe& hp = pipe_for(device);
+        std::lock_guard<std::mutex> lk(hp.mu);
+        if (hp.h2d) {
+            cuda_check(cudaStreamSynchronize(hp.d2h), "cudaStreamSynchronize");
+            cuda_check(cudaStreamSynchronize(hp.comp), "cudaStreamSynchronize");
+            cuda_check(cudaStreamSynchronize(hp.h2d), "cudaStreamSynchronize");
+        }
+        for (int i = 0; i < 4; ++i) {
+            if (hp.buf[i]) cuda_check(cudaFree(hp.buf[i]), "cudaFree");
+            hp.buf[i] = nullptr;
+            hp.cap[i] = 0;
+        }
     });
 }
 

@@ -99,6 +99,12 @@ SIGNATURES = {
                                                      ctypes.c_uint32, ctypes.c_uint32, _U16P,
                                                      ctypes.c_int32, _P,
                                                      ctypes.POINTER(ctypes.c_uint32)]),
+    "foil_matmul_tiles_host": (ctypes.c_int, [ctypes.c_int32, _U16P, _U16P, _U16P, ctypes.c_uint32,
+                                              ctypes.c_uint32, ctypes.c_uint32, _U16P, ctypes.c_int32,
+                                              ctypes.c_uint32]),
+    "foil_conv2d_nhwc_host": (ctypes.c_int, [ctypes.c_int32, _U16P, _U16P, _U16P, _U16P] +
+                              [ctypes.c_uint32] * 9 + [ctypes.c_int32, ctypes.c_uint32]),
+    "foil_host_pipeline_release": (ctypes.c_int, [ctypes.c_int32]),
 }
 
 _lib = None
@@ -183,6 +189,37 @@ def conv2d_nhwc(x, w, bias, y, N, H, W, Cin, Cout, KH, KW, stride, pad, relu=Fal
     """y (N,Ho,Wo,Cout) = relu?(conv(x (N,H,W,Cin), w (Cout,KH,KW,Cin)) + bias)."""
     check(lib().foil_conv2d_nhwc_dev(_ptr(x), _ptr(w), _ptr(bias), _ptr(y), N, H, W, Cin, Cout, KH,
                                      KW, stride, pad, 1 if relu else 0, _stream(stream)))
+
+
+def matmul_tiles_host(device, a, b, c, Mt, Kt, Nt, bias=None, relu=False, chunk_rows=0):
+    """Pipelined C = A . B (+bias, relu) on host tile streams (pinned CPU
+    tensors, numpy arrays or host addresses): copies, GEMM chunks and
+    read-back overlap; returns when C is in host memory."""
+    check(lib().foil_matmul_tiles_host(device, _hptr(a), _hptr(b), _hptr(c), Mt, Kt, Nt, _hptr(bias),
+                                       1 if relu else 0, chunk_rows))
+
+
+def conv2d_nhwc_host(device, x, w, bias, y, N, H, W, Cin, Cout, KH, KW, stride, pad, relu=False,
+                     chunk_images=0):
+    """Pipelined NHWC convolution on host buffers (see matmul_tiles_host)."""
+    check(lib().foil_conv2d_nhwc_host(device, _hptr(x), _hptr(w), _hptr(bias), _hptr(y), N, H, W, Cin,
+                                      Cout, KH, KW, stride, pad, 1 if relu else 0, chunk_images))
+
+
+def host_pipeline_release(device):
+    check(lib().foil_host_pipeline_release(device))
+
+
+def _hptr(t):
+    """Host address of a CPU torch tensor, a numpy array or an int (None -> NULL)."""
+    if t is None:
+        return None
+    if isinstance(t, int):
+        return t
+    if hasattr(t, "ctypes"):
+        return t.ctypes.data
+    assert not t.is_cuda, "host pipeline entry points take host memory"
+    return t.data_ptr()
 
 
 def device_error(stream=None):
