@@ -1,7 +1,10 @@
 """Multi-rank host logic on CPU (gloo, world size 2 and 3): the M-shard of the
 tiled GEMM and the batch shard of the NHWC conv, reassembled with an
-all-gather, equal the unsharded result.  The GPU path (bench.py under
-torchrun) uses the same split_rows / contiguous-shard layout with NCCL.
+all-gather, equal the unsharded result; the row shard of a 'same'
+convolution with its halo exchange (shard.conv2d_nhwc_h_sharded, the oracle
+as the local convolution) gives every rank exactly its rows of the unsharded
+output.  The GPU path (bench.py under torchrun) uses the same split_rows /
+contiguous-shard layout with NCCL.
 """
 import os
 import socket
@@ -72,7 +75,26 @@ def worker(rank, world, port, q):
             ys.append(parts[r].numpy().view(np.uint16)[:(s1 - s0) * per])
         y_all = np.concatenate(ys).reshape(4, 3, 3, 16)
         ok_conv = np.array_equal(y_all, oracle.conv_nhwc(x, w, bias, 2, 1, relu=True))
-        q.put((rank, bool(ok_gemm), bool(ok_conv)))
+
+        # row shard with halos: 2 images of 11 rows (uneven split), 3x3 and 5x5.
+        ok_rows = True
+        for K, pad in ((3, 1), (5, 2)):
+            H, W, Cin, Cout = 11, 7, 16, 16
+            xi = oracle.rand_bf16((2, H, W, Cin), 10 + K)
+            wk = oracle.randn_bf16((Cout, K, K, Cin), 11 + K, 0.1)
+            bk = oracle.rand_bf16((Cout,), 12 + K, -0.1, 0.1)
+            h0, h1 = shard.split_rows(H, world, rank)
+
+            def oracle_conv(ext, w_, b_, N_, H_, W_, Cin_, Cout_, K_, pad_, relu_):
+                y = oracle.conv_nhwc(ext.numpy().view(np.uint16), w_, b_, 1, pad_, relu=relu_)
+                return torch.from_numpy(y.view(np.int16))
+
+            xs = torch.from_numpy(np.ascontiguousarray(xi[:, h0:h1]).view(np.int16))
+            ys = shard.conv2d_nhwc_h_sharded(xs, wk, bk, 2, h1 - h0, W, Cin, Cout, K, pad, relu=True,
+                                            conv=oracle_conv)
+            full = oracle.conv_nhwc(xi, wk, bk, 1, pad, relu=True)
+            ok_rows &= np.array_equal(ys.numpy().view(np.uint16), full[:, h0:h1])
+        q.put((rank, bool(ok_gemm), bool(ok_conv and ok_rows)))
     finally:
         dist.destroy_process_group()
 

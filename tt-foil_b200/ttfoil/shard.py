@@ -7,7 +7,12 @@ same split is done in tile rows: a tile row of a tile-layout matrix is one
 contiguous run of Nt*2 KiB, so each rank's C shard is a contiguous slice and
 concatenating the shards in rank order (an all-gather) rebuilds the global
 tile-layout C exactly.  Convolutions shard the batch: NHWC images are
-contiguous, so no halo is exchanged.
+contiguous, so no halo is exchanged.  A convolution of few large images can
+instead shard the image rows (conv2d_nhwc_h_sharded), as the reference splits
+one image's rows over two cores with a one-row halo each
+(tests/test_conv_3x3_2core.cpp:6-16, 114-133): neighbouring ranks exchange
+their border rows with point-to-point sends (NCCL between GPUs) into local
+memory before the local convolution.
 """
 
 
@@ -30,3 +35,61 @@ def gather_tiles(shards):
     on the device)."""
     import numpy as np
     return np.concatenate([s.reshape(-1) for s in shards])
+
+
+def _device_conv(ext, w, bias, N, H, W, Cin, Cout, K, pad, relu):
+    """Implicit-GEMM conv of the extended shard on its CUDA device."""
+    import torch
+    from . import conv2d_nhwc
+    y = torch.empty(N * H * W * Cout, dtype=ext.dtype, device=ext.device)
+    conv2d_nhwc(ext, w, bias, y, N, H, W, Cin, Cout, K, K, 1, pad, relu=relu)
+    return y.view(N, H, W, Cout)
+
+
+def conv2d_nhwc_h_sharded(x, w, bias, N, H_local, W, Cin, Cout, K, pad, relu=False, conv=None):
+    """Stride-1 'same' convolution (K = 2 pad + 1) of N images whose rows are
+    split over the ranks of the default process group in rank order: `x`
+    holds this rank's H_local rows of every image, (N, H_local, W, Cin) bf16
+    bits (int16 or bfloat16 tensor).  Returns this rank's output rows,
+    (N, H_local, W, Cout).
+
+    The rank sends its first `pad` rows to rank - 1 and its last `pad` rows to
+    rank + 1 and receives theirs (torch.distributed batched point-to-point:
+    NCCL over NVLink between GPUs, gloo on CPU), places them above and below
+    its own rows, and runs the convolution on those H_local + 2 pad rows with
+    the ordinary zero padding; of the H_local + 2 pad output rows, rows
+    pad .. pad + H_local - 1 are exactly the global output rows of this shard
+    (the first and last rank receive nothing: their outer halo stays zero, the
+    image's own padding).  Halos move as 32-bit words (gloo has no 16-bit
+    point-to-point types).  `conv(ext, w, bias, N, H, W, Cin, Cout, K, pad,
+    relu)` defaults to the implicit-GEMM kernel on the tensors' CUDA device."""
+    import torch
+    import torch.distributed as dist
+    if K != 2 * pad + 1:
+        raise ValueError("conv2d_nhwc_h_sharded: only stride-1 'same' convolutions (K = 2 pad + 1)")
+    rank, world = dist.get_rank(), dist.get_world_size()
+    if world > 1 and H_local < pad:
+        raise ValueError("conv2d_nhwc_h_sharded: every shard needs at least `pad` rows")
+    xv = x.view(N, H_local, W, Cin)
+    p = pad
+    ext = torch.zeros((N, H_local + 2 * p, W, Cin), dtype=x.dtype, device=x.device)
+    ext[:, p:p + H_local] = xv
+    if p and world > 1:
+        top_send, bot_send = xv[:, :p].contiguous(), xv[:, H_local - p:].contiguous()
+        top_recv, bot_recv = torch.empty_like(top_send), torch.empty_like(bot_send)
+        w32 = lambda t: t.view(torch.int32)
+        ops = []
+        if rank > 0:
+            ops += [dist.P2POp(dist.isend, w32(top_send), rank - 1),
+                    dist.P2POp(dist.irecv, w32(top_recv), rank - 1)]
+        if rank < world - 1:
+            ops += [dist.P2POp(dist.isend, w32(bot_send), rank + 1),
+                    dist.P2POp(dist.irecv, w32(bot_recv), rank + 1)]
+        for req in dist.batch_isend_irecv(ops):
+            req.wait()
+        if rank > 0:
+            ext[:, :p] = top_recv
+        if rank < world - 1:
+            ext[:, p + H_local:] = bot_recv
+    y_ext = (conv or _device_conv)(ext, w, bias, N, H_local + 2 * p, W, Cin, Cout, K, p, relu)
+    return y_ext[:, p:p + H_local].contiguous()
