@@ -109,9 +109,14 @@ def test_validation_errors_without_gpu():
     assert L.foil_relu_tiles_dev(None, None, 12, None) == 1
     assert L.foil_bias_add_tiles_dev(None, None, None, 32, 48, None) == 1
     assert L.foil_matmul_tiles_dev(None, None, None, 70000, 1, 1, None, 0, None) == 1
+    assert L.foil_matmul_tiles_host(0, None, None, None, 1, 1, 1, None, 0, 0) == 1
+    assert b"null pointer" in L.foil_last_error()
+    assert L.foil_matmul_tiles_host(0, None, None, None, 70000, 1, 1, None, 0, 0) == 1
+    assert L.foil_conv2d_nhwc_host(0, None, None, None, None, 1, 4, 4, 16, 16, 3, 3, 1, 1, 0, 0) == 1
     # zero-sized work is a no-op
     assert L.foil_tile_copy_dev(None, None, 0, None) == 0
     assert L.foil_matmul_tiles_dev(None, None, None, 0, 4, 4, None, 0, None) == 0
+    assert L.foil_matmul_tiles_host(0, None, None, None, 0, 4, 4, None, 0, 0) == 0
 
 
 def test_host_logic_unit_binary(tmp_path):
