@@ -56,6 +56,7 @@ __device__ __forceinline__ uint32_t pack_bf16x2(uint32_t lo, uint32_t hi) {
 // Device-side error codes written to the error word.
 enum : uint32_t {
     kErrWaitTimeout = 1u,  // a bounded mbarrier wait gave up
+    kErrConfig = 4u,       // launch parameters inconsistent with the kernel instantiation (nothing ran)
     kErrBadShape = 2u,     // kernel saw a shape it cannot handle
 };
 

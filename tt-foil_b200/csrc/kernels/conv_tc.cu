@@ -83,6 +83,7 @@ struct Params {
     uint32_t num_kb;       // KH * KW * cblocks
     uint32_t m_blocks, n_blocks;
     int relu;
+    uint32_t box_cols;     // columns of the output tensor map's box (must equal Epi<BN>::kCols)
     uint32_t* err;
 };
 
@@ -248,6 +249,12 @@ __global__ void __launch_bounds__(kThreads, 1)
     uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(drain + 1);
     volatile uint32_t* abort_flag = tmem_slot + 1;
 
+    // The output map's box must be this instantiation's staging box; every
+    // thread takes the same early exit otherwise (nothing started yet).
+    if (p.box_cols != (uint32_t)Epi<BN>::kCols) {
+        if (threadIdx.x == 0 && blockIdx.x == 0) atomicOr(p.err, kErrConfig);
+        return;
+    }
     const uint32_t warp = threadIdx.x >> 5, lane = threadIdx.x & 31u;
     if (threadIdx.x == 0) {
         for (int s = 0; s < C::kStages; ++s) {
@@ -539,6 +546,10 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
     uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(drain + 1);
     volatile uint32_t* abort_flag = tmem_slot + 1;
 
+    if (p.box_cols != (uint32_t)Epi<BN>::kCols) {
+        if (threadIdx.x == 0 && blockIdx.x == 0) atomicOr(p.err, kErrConfig);
+        return;
+    }
     const uint32_t warp = threadIdx.x >> 5, lane = threadIdx.x & 31u;
     const uint32_t rank = cluster_ctarank();
     const bool leader = rank == 0;
@@ -840,13 +851,13 @@ static bool use_tensor_copies(const Params& p) {
            (uint64_t)p.H * p.W * p.Cin * 2 < (1ull << 40);
 }
 
-// Output y as an M x Cout matrix, stored in boxes of 32 rows x 64 columns
-// (SWIZZLE_128B) for BN >= 128, else 32 columns (SWIZZLE_64B), matching the
-// epilogue's staging.
-static bool encode_output_map(const Params& p, int bn, CUtensorMap* my) {
+// Output y as an M x Cout matrix, stored in boxes of 32 rows x p.box_cols
+// columns: 64 (SWIZZLE_128B) or 32 (SWIZZLE_64B), the epilogue's staging
+// boxes (Epi<BN>::kCols, which the kernels check against p.box_cols).
+static bool encode_output_map(const Params& p, CUtensorMap* my) {
     const Encoders& e = encoders();
     if (!e.tiled) return false;
-    const bool wide = bn >= 128;
+    const bool wide = p.box_cols == 64;
     const cuuint64_t ydim[2] = {p.Cout, p.M};
     const cuuint64_t ystr[1] = {(cuuint64_t)p.Cout * 2};
     const cuuint32_t box[2] = {wide ? 64u : 32u, 32};
@@ -918,7 +929,8 @@ int launch(const uint16_t* x, const uint16_t* w, const uint16_t* bias, uint16_t*
     memset(&mx, 0, sizeof mx);
     memset(&mw, 0, sizeof mw);
     const bool tc = use_tensor_copies(p);
-    if (!encode_output_map(p, bn, &my)) {
+    p.box_cols = bn >= 128 ? 64u : 32u;  // Epi<bn>::kCols
+    if (!encode_output_map(p, &my)) {
         foil_set_error(FOIL_ERR_CUDA, "foil_conv2d_nhwc: tensor-map encoding failed");
         return FOIL_ERR_CUDA;
     }
