@@ -352,18 +352,28 @@ def run_ours(args, dist):
 
 def _timed(torch, fn, iters, flush=None, warmup=3):
     """Mean device time (ms) of fn over `iters` launches on the current
-    stream.  With `flush` (two 256 MiB buffers), before each launch and
-    outside the timed interval one buffer is rewritten and the other read, so
+    stream: back to back between one pair of events, or with `flush` (two
+    256 MiB buffers) one event pair per launch, and before each launch,
+    outside the timed interval, one buffer rewritten and the other read, so
     that no operand starts in L2 and the rewrite's dirty lines have been
     written back before the timed launch."""
     for _ in range(warmup):
         fn()
     torch.cuda.synchronize()
+    if flush is None:
+        # Back-to-back launches between one pair of events (operands > L2).
+        e0 = torch.cuda.Event(enable_timing=True)
+        e1 = torch.cuda.Event(enable_timing=True)
+        e0.record()
+        for _ in range(iters):
+            fn()
+        e1.record()
+        torch.cuda.synchronize()
+        return e0.elapsed_time(e1) / iters
     evs = []
     for _ in range(iters):
-        if flush is not None:
-            flush[0].add_(1)
-            flush[1].sum()
+        flush[0].add_(1)
+        flush[1].sum()
         e0 = torch.cuda.Event(enable_timing=True)
         e1 = torch.cuda.Event(enable_timing=True)
         e0.record()
@@ -441,22 +451,22 @@ def run_secondary(dist, pk):
     x, y = rnd(R * C), torch.empty(R * C, dtype=torch.bfloat16, device=dev)
     for name, fn in (("tilize_16384^2", lambda: ttfoil.tilize(x, y, R, C)),
                      ("untilize_16384^2", lambda: ttfoil.untilize(x, y, R, C))):
-        ms = dist.max(_timed(torch, fn, 10))
+        ms = dist.max(_timed(torch, fn, 20))
         elt[name] = 4.0 * R * C / (ms / 1e3) / 1e9
     band = rnd(32 * C)
-    ms = dist.max(_timed(torch, lambda: ttfoil.bias_add_tiles(x, band, y, R, C), 10))
+    ms = dist.max(_timed(torch, lambda: ttfoil.bias_add_tiles(x, band, y, R, C), 20))
     elt["bias_add_2^28"] = (4.0 * R * C + 64.0 * C) / (ms / 1e3) / 1e9
     n = 1 << 28
     z = rnd(n)
-    ms = dist.max(_timed(torch, lambda: ttfoil.add_tiles(x, z, y, n), 10))
+    ms = dist.max(_timed(torch, lambda: ttfoil.add_tiles(x, z, y, n), 20))
     elt["add_tiles_2^28"] = 6.0 * n / (ms / 1e3) / 1e9
-    ms = dist.max(_timed(torch, lambda: ttfoil.relu_tiles(x, y, n), 10))
+    ms = dist.max(_timed(torch, lambda: ttfoil.relu_tiles(x, y, n), 20))
     elt["relu_2^28"] = 4.0 * n / (ms / 1e3) / 1e9
     del x, y, z, band
     nbytes = 1 << 30
     src = torch.empty(nbytes // 2, dtype=torch.int16, device=dev).random_(generator=g)
     dst = torch.empty_like(src)
-    ms = dist.max(_timed(torch, lambda: ttfoil.tile_copy(src, dst, nbytes), 10))
+    ms = dist.max(_timed(torch, lambda: ttfoil.tile_copy(src, dst, nbytes), 20))
     elt["tile_copy_1GiB"] = 2.0 * nbytes / (ms / 1e3) / 1e9
     del src, dst
     out["eltwise_GBps_per_gpu"] = elt
