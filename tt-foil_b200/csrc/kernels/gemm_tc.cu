@@ -352,7 +352,7 @@ gemm_tiles_kernel(const Params p) {
 // and whose B columns 0..127 / 128..255 likewise; each CTA's TMEM receives its
 // 128 rows x 256 columns.  Per k-block (K = 64) a CTA stages 16 KiB of A and
 // 16 KiB of B (a third less L2 traffic per FLOP than 128x256 on one SM), so
-// six stages fit in shared memory.
+// seven stages fit in shared memory.
 //
 // Synchronisation: each CTA's producers arrive on their own full[s] through
 // cp.async.mbarrier.arrive; in the odd CTA a relay lane waits for it, fences
@@ -361,7 +361,7 @@ gemm_tiles_kernel(const Params p) {
 // empty[s] / tfull[b]; both CTAs' epilogue warps arrive on the even CTA's
 // tempty[b] (8 arrivals).  A cluster barrier after set-up and before exit
 // keeps both CTAs alive while the other may touch their shared memory.
-constexpr int kPStages = 6;
+constexpr int kPStages = 7;
 constexpr int kPABytes = 128 * kBKT * 32 * 2;  // 16 KiB: 128 rows x K 64
 constexpr int kPBBytes = 128 * kBKT * 32 * 2;  // 16 KiB: 128 cols x K 64
 constexpr int kPStageBytes = kPABytes + kPBBytes;
