@@ -49,6 +49,7 @@
 // in-flight copies and MMAs are drained and TMEM is freed.
 #include <mutex>
 #include <cstdio>
+#include <cstdlib>
 #include <cstring>
 
 #include "common.cuh"
@@ -91,13 +92,13 @@ struct Params {
 };
 
 __device__ __forceinline__ void tile_coords(uint32_t tile, uint32_t m_blocks, uint32_t n_blocks,
-                                            uint32_t& mb, uint32_t& nb) {
-    const uint32_t band_tiles = m_blocks * kBandN;
+                                            uint32_t& mb, uint32_t& nb, uint32_t bandn = kBandN) {
+    const uint32_t band_tiles = m_blocks * bandn;
     const uint32_t band = tile / band_tiles;
     const uint32_t inner = tile - band * band_tiles;
-    const uint32_t width = min((uint32_t)kBandN, n_blocks - band * kBandN);
+    const uint32_t width = min(bandn, n_blocks - band * bandn);
     mb = inner / width;
-    nb = band * kBandN + (inner - mb * width);
+    nb = band * bandn + (inner - mb * width);
 }
 
 // out = bf16(acc) [+ bias -> bf16] [relu], the composition of the reference
@@ -587,6 +588,224 @@ static int check_launch(const char* what) {
     return FOIL_OK;
 }
 
+// ============================================= 2-SM kernel, 512 columns ===
+// The pair tile widened to 256 x 512: per K-step the even CTA issues two
+// tcgen05.mma.cta_group::2 of N = 256 (column halves h = 0, 1) on the same A
+// rows, into TMEM columns [256 h, 256 h + 256) of both CTAs.  Per k-block a
+// CTA stages 16 KiB of A and 32 KiB of B (its 128 columns of each half) for
+// twice the MMAs of the 256 x 256 tile: a quarter fewer L2 -> SM bytes per
+// FLOP, the operand feed's limit.  The 512 accumulator columns leave no room
+// for a second TMEM buffer, so the MMAs of a tile wait for the previous
+// tile's epilogue; eight epilogue warps (one per TMEM lane quadrant and
+// column half) keep that short, and the producers keep loading meanwhile.
+constexpr int kWStages = 4;
+constexpr int kWABytes = 128 * kBKT * 32 * 2;      // 16 KiB: 128 rows x K 64
+constexpr int kWBBytes = 2 * 128 * kBKT * 32 * 2;  // 32 KiB: 2 halves x 128 cols x K 64
+constexpr int kWStageBytes = kWABytes + kWBBytes;
+constexpr int kWFaces = 96;                        // 32 A + 64 B faces per CTA
+constexpr int kWEpiWarps = 8;
+constexpr int kWThreads = (5 + kWEpiWarps) * 32;
+constexpr int kWSmemBytes = kWStages * kWStageBytes + 1024 + 256;
+constexpr int kWBandN = 4;                         // 512-column blocks per raster band
+
+__global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kWThreads, 1)
+gemm_pair_wide_kernel(const Params p) {
+    extern __shared__ uint8_t smem_raw[];
+    uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) &
+                                               ~uintptr_t(1023));
+    uint64_t* full = reinterpret_cast<uint64_t*>(smem + kWStages * kWStageBytes);
+    uint64_t* empty = full + kWStages;
+    uint64_t* tfull = empty + kWStages;
+    uint64_t* tempty = tfull + 1;
+    uint64_t* drain = tempty + 1;
+    uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(drain + 1);
+    volatile uint32_t* abort_flag = tmem_slot + 1;
+
+    const uint32_t warp = threadIdx.x >> 5, lane = threadIdx.x & 31u;
+    const uint32_t rank = cluster_ctarank();
+    const bool leader = rank == 0;
+    const uint32_t pair_id = blockIdx.x >> 1, num_pairs = gridDim.x >> 1;
+
+    if (threadIdx.x == 0) {
+        for (int s = 0; s < kWStages; ++s) {
+            mbar_init(&full[s], kProdWarps * 32 + (leader ? 1 : 0));
+            mbar_init(&empty[s], 1);
+        }
+        mbar_init(tfull, 1);
+        mbar_init(tempty, 2 * kWEpiWarps);
+        mbar_init(drain, 1);
+        *abort_flag = 0u;
+        asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+        asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+    }
+    if (warp == kMmaWarp) {
+        asm volatile("tcgen05.alloc.cta_group::2.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(
+                         smem_u32(tmem_slot)),
+                     "r"(kTmemCols)
+                     : "memory");
+        asm volatile("tcgen05.relinquish_alloc_permit.cta_group::2.sync.aligned;" ::: "memory");
+    }
+    tc_fence_before();
+    __syncthreads();
+    cluster_sync();
+    tc_fence_after();
+    const uint32_t tmem_base = *tmem_slot;
+
+    const uint32_t num_tiles = p.m_blocks * p.n_blocks;  // 256-row x 512-column blocks
+    const uint32_t num_kb = (p.Kt + kBKT - 1) / kBKT;
+
+    if (warp < kProdWarps) {
+        // ---------------------------------------------------- producers
+        const uint32_t src_lane = lane * 16u;
+        const uint32_t dst_lane = (lane >> 1) * 32u + ((((lane & 1u) ^ ((lane >> 3) & 1u))) << 4);
+        const char* a_g = reinterpret_cast<const char*>(p.a);
+        const char* b_g = reinterpret_cast<const char*>(p.b);
+        uint32_t stage = 0, phase = 0;
+        for (uint32_t tile = pair_id; tile < num_tiles; tile += num_pairs) {
+            uint32_t mp, nb;
+            tile_coords(tile, p.m_blocks, p.n_blocks, mp, nb, kWBandN);
+            const uint32_t mt0 = (mp * 2u + rank) * 4u;  // this CTA's 4 tile rows
+            bool ok = true;
+            for (uint32_t kb = 0; kb < num_kb; ++kb) {
+                bool w = true;
+                if (lane == 0) w = mbar_wait_cluster(&empty[stage], phase ^ 1u, abort_flag, p.err);
+                if (__shfl_sync(0xffffffffu, w ? 1 : 0, 0) == 0) {
+                    ok = false;
+                    break;
+                }
+                const uint32_t a_s = smem_u32(smem + stage * kWStageBytes);
+                const uint32_t b_s = a_s + kWABytes;
+                const uint32_t kt0 = kb * kBKT;
+#pragma unroll
+                for (int i = 0; i < kWFaces / kProdWarps; ++i) {
+                    const uint32_t f = warp + kProdWarps * i;
+                    const char* src;
+                    uint32_t dst;
+                    bool valid;
+                    if (i < 32 / kProdWarps) {  // A face: (mt_l, ktl, fr, fc)
+                        const uint32_t mt_l = f >> 3, ktl = (f >> 2) & 1u, fr = (f >> 1) & 1u,
+                                       fc = f & 1u;
+                        const uint32_t mt = mt0 + mt_l, kt = kt0 + ktl;
+                        valid = mt < p.Mt && kt < p.Kt;
+                        src = a_g + (((uint64_t)mt * p.Kt + kt) * 1024u + (fr * 2u + fc) * 256u) * 2u;
+                        dst = a_s + (ktl * 2u + fc) * 4096u + (mt_l * 32u + fr * 16u) * 32u;
+                    } else {  // B face: (half, ktl, nt_l, fr, fc)
+                        const uint32_t g = f - 32u;
+                        const uint32_t h = g >> 5, ktl = (g >> 4) & 1u, nt_l = (g >> 2) & 3u,
+                                       fr = (g >> 1) & 1u, fc = g & 1u;
+                        const uint32_t kt = kt0 + ktl, nt = nb * 16u + h * 8u + rank * 4u + nt_l;
+                        valid = kt < p.Kt && nt < p.Nt;
+                        src = b_g + (((uint64_t)kt * p.Nt + nt) * 1024u + (fr * 2u + fc) * 256u) * 2u;
+                        dst = b_s + h * 16384u + fr * 8192u + ktl * 4096u + (nt_l * 2u + fc) * 512u;
+                    }
+                    cp_async16(dst + dst_lane, valid ? src + src_lane : a_g, valid ? 16u : 0u);
+                }
+                cp_async_arrive(&full[stage]);
+                if (++stage == kWStages) {
+                    stage = 0;
+                    phase ^= 1u;
+                }
+            }
+            if (!ok) break;
+        }
+        asm volatile("cp.async.wait_all;" ::: "memory");
+    } else if (warp == kMmaWarp) {
+        if (lane == 0 && !leader) {
+            // ---------------------------------- relay (odd CTA): full -> leader
+            const uint32_t remote_full0 = map_to_rank(&full[0], 0);
+            uint32_t stage = 0, phase = 0;
+            bool ok = true;
+            for (uint32_t tile = pair_id; ok && tile < num_tiles; tile += num_pairs) {
+                for (uint32_t kb = 0; kb < num_kb; ++kb) {
+                    if (!mbar_wait(&full[stage], phase, abort_flag, p.err)) {
+                        ok = false;
+                        break;
+                    }
+                    asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+                    mbar_arrive_remote_relaxed(remote_full0 + stage * 8u);
+                    if (++stage == kWStages) {
+                        stage = 0;
+                        phase ^= 1u;
+                    }
+                }
+            }
+        } else if (lane == 0) {
+            // ------------------------------------- MMA issuer (even CTA)
+            constexpr uint32_t idesc = make_idesc(256, 256);
+            constexpr uint64_t a_base = smem_desc_base(16, 256);   // K-major SW32
+            constexpr uint64_t b_base = smem_desc_base(512, 256);  // MN-major SW32
+            uint32_t stage = 0, phase = 0, t_phase = 0;
+            bool ok = true;
+            for (uint32_t tile = pair_id; ok && tile < num_tiles; tile += num_pairs) {
+                if (!mbar_wait_cluster(tempty, t_phase ^ 1u, abort_flag, p.err)) break;
+                tc_fence_after();
+                for (uint32_t kb = 0; kb < num_kb; ++kb) {
+                    if (!mbar_wait_cluster(&full[stage], phase, abort_flag, p.err)) {
+                        ok = false;
+                        break;
+                    }
+                    asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+                    tc_fence_after();
+                    const uint32_t a_addr = smem_u32(smem + stage * kWStageBytes);
+                    const uint32_t b_addr = a_addr + kWABytes;
+#pragma unroll
+                    for (uint32_t s = 0; s < 4; ++s) {
+                        const uint64_t ad = a_base | (uint64_t)(((a_addr + s * 4096u) >> 4) & 0x3fffu);
+                        const uint32_t b_off = (s & 1u) * 8192u + (s >> 1) * 4096u;
+#pragma unroll
+                        for (uint32_t h = 0; h < 2; ++h) {
+                            const uint64_t bd =
+                                b_base | (uint64_t)(((b_addr + h * 16384u + b_off) >> 4) & 0x3fffu);
+                            tc_mma_pair(tmem_base + h * 256u, ad, bd, idesc, (kb | s) != 0u);
+                        }
+                    }
+                    tc_commit_pair_mc(&empty[stage], 0x3);
+                    if (++stage == kWStages) {
+                        stage = 0;
+                        phase ^= 1u;
+                    }
+                }
+                if (!ok) break;
+                tc_commit_pair_mc(tfull, 0x3);
+                t_phase ^= 1u;
+            }
+            tc_commit_pair(drain);
+            mbar_drain(drain, 0, 100000000ull);
+        }
+    } else {
+        // ---------------------------------------------------- epilogue
+        // Warp e (0..7): TMEM lane quadrant warp % 4, column half e / 4.
+        const uint32_t e = warp - 5u, q = warp & 3u, h = e >> 2;
+        const uint32_t remote_tempty = map_to_rank(tempty, 0);
+        uint32_t t_phase = 0;
+        for (uint32_t tile = pair_id; tile < num_tiles; tile += num_pairs) {
+            uint32_t mp, nb;
+            tile_coords(tile, p.m_blocks, p.n_blocks, mp, nb, kWBandN);
+            bool ok = true;
+            if (lane == 0) ok = mbar_wait_cluster(tfull, t_phase, abort_flag, p.err);
+            ok = __shfl_sync(0xffffffffu, ok ? 1 : 0, 0) != 0;
+            if (!ok) break;
+            tc_fence_after();
+            store_tile_row(p, tmem_base + ((q * 32u) << 16) + h * 256u, (mp * 2u + rank) * 4u + q,
+                           nb * 16u + h * 8u, lane);
+            tc_fence_before();
+            __syncwarp();
+            if (lane == 0) mbar_arrive_remote(remote_tempty);
+            t_phase ^= 1u;
+        }
+    }
+
+    tc_fence_before();
+    __syncwarp();
+    cluster_sync();
+    if (warp == kMmaWarp) {
+        tc_fence_after();
+        asm volatile("tcgen05.dealloc.cta_group::2.sync.aligned.b32 %0, %1;" ::"r"(tmem_base),
+                     "r"(kTmemCols)
+                     : "memory");
+    }
+}
+
 int launch(const uint16_t* a, const uint16_t* b, uint16_t* c, uint32_t Mt, uint32_t Kt,
            uint32_t Nt, const uint16_t* bias, int relu, uint32_t* err, cudaStream_t stream,
            int max_ctas) {
@@ -624,6 +843,27 @@ int launch(const uint16_t* a, const uint16_t* b, uint16_t* c, uint32_t Mt, uint3
         return check_launch("foil_matmul_tiles");
     }
     p.m_blocks = (Mt + 7) / 8;  // 256-row blocks, one per CTA pair
+    // More than one 256-column block: the 512-column pair kernel (a quarter
+    // fewer L2 -> SM bytes per FLOP; 8192^3: 1.17 -> 1.46 PFLOP/s over 50
+    // launches, 1.07 -> 1.32 under the power cap over 400).
+    if (Nt > 8) {
+        static std::once_flag wide_once;
+        static cudaError_t wide_err = cudaSuccess;
+        std::call_once(wide_once, [] {
+            wide_err = cudaFuncSetAttribute(gemm_pair_wide_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                            kWSmemBytes);
+        });
+        if (wide_err != cudaSuccess) {
+            foil_set_error(FOIL_ERR_CUDA, "foil_matmul_tiles: cudaFuncSetAttribute failed");
+            return FOIL_ERR_CUDA;
+        }
+        p.n_blocks = (Nt + 15) / 16;  // 512-column blocks
+        const uint32_t wtiles = p.m_blocks * p.n_blocks;
+        const uint32_t wmax = (uint32_t)max_ctas / 2;
+        const uint32_t wpairs = wtiles < wmax ? wtiles : wmax;
+        gemm_pair_wide_kernel<<<wpairs * 2, kWThreads, kWSmemBytes, stream>>>(p);
+        return check_launch("foil_matmul_tiles (2-SM, 512 columns)");
+    }
     const uint32_t tiles = p.m_blocks * p.n_blocks;
     const uint32_t max_pairs = (uint32_t)max_ctas / 2;
     const uint32_t pairs = tiles < max_pairs ? tiles : max_pairs;
