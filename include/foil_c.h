@@ -225,7 +225,11 @@ FOIL_API int foil_tilize_dev(const uint16_t* row_major, uint16_t* tiles,
 FOIL_API int foil_untilize_dev(const uint16_t* tiles, uint16_t* row_major,
                       uint32_t rows, uint32_t cols, void* stream);
 
-/* Identity copy of `bytes` (multiple of 16, 16-byte aligned pointers).
+/* Element-wise stages below: pointers 16-byte aligned; the output may be the
+ * same buffer as an input (in place) but must not partially overlap one
+ * (FOIL_ERR_INVALID).  A stalled copy sets the device error word.
+ *
+ * Identity copy of `bytes` (multiple of 16).
  * Replaces examples/tile_copy/kernels/{reader,compute,writer}.cpp. */
 FOIL_API int foil_tile_copy_dev(const void* src, void* dst, uint64_t bytes,
                        void* stream);
@@ -243,7 +247,8 @@ FOIL_API int foil_relu_tiles_dev(const uint16_t* in, uint16_t* out, uint64_t n,
 /* Row-broadcast bias on a tile-layout matrix of rows x cols:
  * out[r][c] = bf16(f32(in[r][c]) + f32(bias[0][c])), where `bias_tiles` is a
  * tile-layout band of 1 x (cols/32) tiles whose row 0 holds the bias (the
- * reference's bias-tile convention, tests/test_bias_add.cpp:53-56).
+ * reference's bias-tile convention, tests/test_bias_add.cpp:53-56); the
+ * output must not overlap the bias band.
  * Replaces examples/bias_add/kernels/compute.cpp:19-42. */
 FOIL_API int foil_bias_add_tiles_dev(const uint16_t* in, const uint16_t* bias_tiles,
                             uint16_t* out, uint32_t rows, uint32_t cols,

@@ -108,6 +108,19 @@ def test_validation_errors_without_gpu():
     assert L.foil_add_tiles_dev(None, None, None, 7, None) == 1
     assert L.foil_relu_tiles_dev(None, None, 12, None) == 1
     assert L.foil_bias_add_tiles_dev(None, None, None, 32, 48, None) == 1
+    # element-wise stages: misaligned pointers, partial overlap of the output
+    # with an input, and an output over the bias band are rejected before
+    # anything is launched (the addresses are never dereferenced)
+    base = 1 << 40
+    assert L.foil_relu_tiles_dev(base + 8, base + 4096, 8, None) == 1
+    assert b"misaligned" in L.foil_last_error()
+    assert L.foil_relu_tiles_dev(base, base + 16, 64, None) == 1
+    assert b"partially overlaps" in L.foil_last_error()
+    assert L.foil_add_tiles_dev(base, base + 4096, base + 4096 - 16, 64, None) == 1
+    assert b"partially overlaps" in L.foil_last_error()
+    assert L.foil_tile_copy_dev(base + 16, base, 64, None) == 1
+    assert L.foil_bias_add_tiles_dev(base, base + (1 << 20) + 512, base + (1 << 20), 32, 64, None) == 1
+    assert b"bias band" in L.foil_last_error()
     assert L.foil_matmul_tiles_dev(None, None, None, 70000, 1, 1, None, 0, None) == 1
     assert L.foil_matmul_tiles_host(0, None, None, None, 1, 1, 1, None, 0, 0) == 1
     assert b"null pointer" in L.foil_last_error()

@@ -113,7 +113,90 @@ def test_add_bit_exact(torch_cuda, tf):
     assert np.array_equal(host(out), oracle.add(a, b))
 
 
-@pytest.mark.parametrize("rows,cols", [(32, 32), (64, 160), (256, 512)])
+def test_add_every_bf16_and_rounding_edges(torch_cuda, tf):
+    """Every bf16 bit pattern as the first operand (NaNs, infinities,
+    subnormals, signed zeros) against random second operands, plus pairs
+    whose exponents differ by 0..26 (where the golden's fp32 sum stops being
+    exact), both signs: bit-exact to the golden."""
+    torch = torch_cuda
+    rng = np.random.default_rng(11)
+    every = np.arange(1 << 16, dtype=np.uint32).astype(np.uint16)
+    a1 = np.tile(every, 16)
+    b1 = rng.integers(0, 1 << 16, a1.size, dtype=np.uint32).astype(np.uint16)
+    base = rng.integers(0, 1 << 16, 8192, dtype=np.uint32)
+    base = base[((base >> 7) & 0xff) > 30]                     # exponent room below
+    d = np.arange(27, dtype=np.uint32)
+    ea = (base[:, None] >> 7) & 0xff
+    eb = np.maximum(ea.astype(np.int64) - d[None, :], 0).astype(np.uint32)
+    mant = rng.integers(0, 128, eb.shape, dtype=np.uint32)
+    sign = rng.integers(0, 2, eb.shape, dtype=np.uint32) << 15
+    a2 = np.broadcast_to(base[:, None], eb.shape).ravel().astype(np.uint16)
+    b2 = (sign | (eb << 7) | mant).ravel().astype(np.uint16)
+    a = np.concatenate([a1, a2, b2])
+    b = np.concatenate([b1, b2, a2])
+    n = (a.size // 8) * 8
+    a, b = a[:n], b[:n]
+    out = empty(torch, n)
+    tf.add_tiles(dev(torch, a), dev(torch, b), out, n)
+    torch.cuda.synchronize()
+    assert tf.device_error() == 0
+    got, exp = host(out), oracle.add(a, b)
+    bad = np.nonzero(got != exp)[0]
+    assert bad.size == 0, f"{bad.size} mismatches; (a, b, got, golden): " + ", ".join(
+        f"({a[i]:04x}, {b[i]:04x}, {got[i]:04x}, {exp[i]:04x})" for i in bad[:24])
+
+
+@pytest.mark.parametrize("n", [8, 24, 1024 + 8, 4096 * 3 + 40, (1 << 20) + 8 * 1001])
+def test_eltwise_ragged_sizes(torch_cuda, tf, n):
+    """Sizes that leave a partial last chunk in the streaming pipeline (and
+    fewer chunks than CTAs): relu, add and copy stay bit-exact and write
+    nothing past n."""
+    torch = torch_cuda
+    a = oracle.rand_bf16(n, 21, -4, 4)
+    b = oracle.rand_bf16(n, 22, -4, 4)
+    guard = 64
+    out = torch.full((n + guard,), 0x1234, dtype=torch.int16, device="cuda")
+    tf.relu_tiles(dev(torch, a), out, n)
+    torch.cuda.synchronize()
+    h = host(out)
+    assert np.array_equal(h[:n], oracle.relu(a)) and np.all(h[n:] == 0x1234)
+    tf.add_tiles(dev(torch, a), dev(torch, b), out, n)
+    torch.cuda.synchronize()
+    h = host(out)
+    assert np.array_equal(h[:n], oracle.add(a, b)) and np.all(h[n:] == 0x1234)
+    tf.tile_copy(dev(torch, b), out, 2 * n)
+    torch.cuda.synchronize()
+    h = host(out)
+    assert np.array_equal(h[:n], b) and np.all(h[n:] == 0x1234)
+    assert tf.device_error() == 0
+
+
+def test_eltwise_in_place(torch_cuda, tf):
+    """out == input: relu and add in place, bias_add in place."""
+    torch = torch_cuda
+    n = (3 << 20) + 8 * 5
+    a = oracle.rand_bf16(n, 31)
+    b = oracle.rand_bf16(n, 32)
+    x = dev(torch, a)
+    tf.relu_tiles(x, x, n)
+    torch.cuda.synchronize()
+    assert np.array_equal(host(x), oracle.relu(a))
+    x = dev(torch, a)
+    tf.add_tiles(x, dev(torch, b), x, n)
+    torch.cuda.synchronize()
+    assert np.array_equal(host(x), oracle.add(a, b))
+    rows, cols = 96, 4096
+    m = oracle.rand_bf16((rows, cols), 33)
+    band = np.zeros((32, cols), dtype=np.uint16)
+    band[0] = oracle.rand_bf16(cols, 34, -0.5, 0.5)
+    x = dev(torch, oracle.tilize(m))
+    tf.bias_add_tiles(x, dev(torch, oracle.tilize(band)), x, rows, cols)
+    torch.cuda.synchronize()
+    assert np.array_equal(oracle.untilize(host(x), rows, cols), oracle.bias_add(m, band[0]))
+    assert tf.device_error() == 0
+
+
+@pytest.mark.parametrize("rows,cols", [(32, 32), (64, 160), (256, 512), (1056, 3 * 32 * 7)])
 def test_bias_add_bit_exact(torch_cuda, tf, rows, cols):
     torch = torch_cuda
     x = oracle.rand_bf16((rows, cols), 6)

@@ -101,6 +101,23 @@ def test_eltwise_semantics():
     assert np.array_equal(o, ref)
 
 
+def test_add_nan_results_of_the_x86_golden():
+    """NaN results of the golden's `f(a) + f(b)` as compiled for x86-64 (the
+    device kernels reproduce exactly these): one NaN operand comes out
+    quieted, of two the second wins, inf - inf is the default NaN.  Scalar
+    and vectorised loops agree (1 and 8 elements)."""
+    a = np.array([0x7f83, 0xff8a, 0x7f80, 0x7f80, 0x3f80, 0x7f83, 0x7fc0, 0xff80], dtype=np.uint16)
+    b = np.array([0x7f9f, 0xffe1, 0xff80, 0x7f80, 0x7f85, 0x3f80, 0xffc1, 0x7f80], dtype=np.uint16)
+    exp = [0x7fdf, 0xffe1, 0xffc0, 0x7f80, 0x7fc5, 0x7fc3, 0xffc1, 0xffc0]
+    assert list(oracle.add(a, b)) == exp
+    assert [int(oracle.add(a[i:i + 1], b[i:i + 1])[0]) for i in range(8)] == exp
+    x = np.full((1, 32), 0x3f80, dtype=np.uint16)
+    x[0, :2] = 0x7f83
+    bias = np.full(32, 0x3f80, dtype=np.uint16)
+    bias[0] = 0x7f9f
+    assert list(oracle.bias_add(x, bias)[0, :2]) == [0x7fdf, 0x7fc3]
+
+
 def test_conv_nhwc_epilogue_is_composition():
     x = oracle.rand_bf16((2, 6, 7, 16), 5)
     w = oracle.randn_bf16((8, 3, 3, 16), 6, 0.1)

@@ -34,6 +34,7 @@
 #include "host_logic.hpp"
 #include "kernels/gemm_tc.cuh"
 #include "kernels/conv_tc.cuh"
+#include "kernels/eltwise.cuh"
 
 namespace {
 
@@ -272,6 +273,36 @@ char* loc_ptr(foil_device* d, const foil::Loc& l, const char* what) {
 }
 
 bool aligned16(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15u) == 0; }
+
+// Element-wise stages (tile_copy / relu / add_tiles / bias_add) on the bulk
+// streaming pipeline.  `out` may equal an input (in place) but must not
+// partially overlap one: chunks are processed in no fixed order.  err: the
+// device error word (null: this device's scratch word).
+void launch_eltwise(const char* what, foil::stream::Op op, const void* a, const void* b, void* out,
+                    uint64_t bytes, const uint16_t* bias_tiles, uint32_t Nt, uint32_t* err,
+                    cudaStream_t stream) {
+    if (bytes == 0) return;
+    if (bytes % (op == foil::stream::kBias ? 2048 : 16))
+        throw FoilError(FOIL_ERR_INVALID, std::string(what) + ": size is not a whole number of vectors / tiles");
+    auto overlaps = [&](const void* in, uint64_t in_bytes) {
+        if (!in || in == out) return false;
+        const uintptr_t i0 = (uintptr_t)in, o0 = (uintptr_t)out;
+        return i0 < o0 + bytes && o0 < i0 + in_bytes;
+    };
+    if (!a || !out || !aligned16(a) || !aligned16(out) || (op == foil::stream::kAdd && (!b || !aligned16(b))) ||
+        (op == foil::stream::kBias && (!bias_tiles || !aligned16(bias_tiles))))
+        throw FoilError(FOIL_ERR_INVALID, std::string(what) + ": null or misaligned pointer");
+    if (overlaps(a, bytes) || (op == foil::stream::kAdd && overlaps(b, bytes)))
+        throw FoilError(FOIL_ERR_INVALID, std::string(what) + ": output partially overlaps an input");
+    if (op == foil::stream::kBias && (bias_tiles == out || overlaps(bias_tiles, (uint64_t)Nt * 2048)))
+        throw FoilError(FOIL_ERR_INVALID, std::string(what) + ": output overlaps the bias band");
+    if (!err) err = error_word_for_current_device();
+    const int e = foil::stream::launch(op, a, b, out, bytes, bias_tiles, Nt, err, stream);
+    if (e != 0)
+        throw FoilError(FOIL_ERR_CUDA, std::string(what) + ": CUDA launch failed: " +
+                                           cudaGetErrorString(static_cast<cudaError_t>(e)));
+    foil_count_launch();
+}
 
 // Wait for the device stream with a deadline; throws on timeout.
 void wait_stream(foil_device* d, std::chrono::steady_clock::time_point deadline,
@@ -545,18 +576,20 @@ void run_op(foil_device* d, ResolvedOp& r) {
     cudaStream_t s = d->stream;
     switch (r.op.kind) {
         case foil::OpKind::Copy:
-            throw_status(foil_tile_copy_dev(r.p0, r.po, r.op.in0.bytes, s));
+            launch_eltwise("tile_copy", foil::stream::kCopy, r.p0, nullptr, r.po, r.op.in0.bytes, nullptr, 0,
+                           d->err_word, s);
             break;
         case foil::OpKind::Relu:
-            throw_status(foil_relu_tiles_dev((const uint16_t*)r.p0, (uint16_t*)r.po, r.op.in0.bytes / 2, s));
+            launch_eltwise("relu", foil::stream::kRelu, r.p0, nullptr, r.po, r.op.in0.bytes, nullptr, 0,
+                           d->err_word, s);
             break;
         case foil::OpKind::Add:
-            throw_status(foil_add_tiles_dev((const uint16_t*)r.p0, (const uint16_t*)r.p1, (uint16_t*)r.po,
-                                            r.op.in0.bytes / 2, s));
+            launch_eltwise("add_tiles", foil::stream::kAdd, r.p0, r.p1, r.po, r.op.in0.bytes, nullptr, 0,
+                           d->err_word, s);
             break;
         case foil::OpKind::BiasAdd:
-            throw_status(foil_bias_add_tiles_dev((const uint16_t*)r.p0, (const uint16_t*)r.p1,
-                                                 (uint16_t*)r.po, 32, 32, s));
+            launch_eltwise("bias_add", foil::stream::kBias, r.p0, nullptr, r.po, 2048, (const uint16_t*)r.p1, 1,
+                           d->err_word, s);
             break;
         case foil::OpKind::Matmul:
             throw_status(foil::gemm::launch((const uint16_t*)r.p0, (const uint16_t*)r.p1, (uint16_t*)r.po,
@@ -693,6 +726,48 @@ extern "C" int foil_conv2d_nhwc_dev(const uint16_t* x, const uint16_t* w, const 
         uint32_t* err = error_word_for_current_device();
         throw_status(foil::conv::launch(x, w, bias, y, N, H, W, Cin, Cout, KH, KW, stride, pad, relu, err,
                                         (cudaStream_t)stream, sm_count_current()));
+    });
+}
+
+// ------------------------------------------------ element-wise entries ---
+extern "C" int foil_tile_copy_dev(const void* src, void* dst, uint64_t bytes, void* stream) {
+    return guarded([&] {
+        if (bytes % 16) throw FoilError(FOIL_ERR_INVALID, "foil_tile_copy_dev: bytes must be a multiple of 16");
+        if (bytes == 0) return;
+        launch_eltwise("foil_tile_copy_dev", foil::stream::kCopy, src, nullptr, dst, bytes, nullptr, 0,
+                       nullptr, (cudaStream_t)stream);
+    });
+}
+
+extern "C" int foil_add_tiles_dev(const uint16_t* a, const uint16_t* b, uint16_t* out, uint64_t n,
+                                  void* stream) {
+    return guarded([&] {
+        if (n % 8) throw FoilError(FOIL_ERR_INVALID, "foil_add_tiles_dev: n must be a multiple of 8");
+        if (n == 0) return;
+        if (n > (1ull << 62)) throw FoilError(FOIL_ERR_INVALID, "foil_add_tiles_dev: n too large");
+        launch_eltwise("foil_add_tiles_dev", foil::stream::kAdd, a, b, out, 2 * n, nullptr, 0,
+                       nullptr, (cudaStream_t)stream);
+    });
+}
+
+extern "C" int foil_relu_tiles_dev(const uint16_t* in, uint16_t* out, uint64_t n, void* stream) {
+    return guarded([&] {
+        if (n % 8) throw FoilError(FOIL_ERR_INVALID, "foil_relu_tiles_dev: n must be a multiple of 8");
+        if (n == 0) return;
+        if (n > (1ull << 62)) throw FoilError(FOIL_ERR_INVALID, "foil_relu_tiles_dev: n too large");
+        launch_eltwise("foil_relu_tiles_dev", foil::stream::kRelu, in, nullptr, out, 2 * n, nullptr, 0,
+                       nullptr, (cudaStream_t)stream);
+    });
+}
+
+extern "C" int foil_bias_add_tiles_dev(const uint16_t* in, const uint16_t* bias_tiles, uint16_t* out,
+                                       uint32_t rows, uint32_t cols, void* stream) {
+    return guarded([&] {
+        if (rows % 32 || cols % 32)
+            throw FoilError(FOIL_ERR_INVALID, "foil_bias_add_tiles_dev: rows and cols must be multiples of 32");
+        if (rows == 0 || cols == 0) return;
+        launch_eltwise("foil_bias_add_tiles_dev", foil::stream::kBias, in, nullptr, out,
+                       (uint64_t)rows * cols * 2, bias_tiles, cols / 32, nullptr, (cudaStream_t)stream);
     });
 }
 

@@ -22,19 +22,20 @@ __device__ __forceinline__ uint32_t f32_to_bf16_bits(float f) {
     return u >> 16;
 }
 
-// fp32 addition with the NaN results of the x86-64 host that computes the
-// reference golden (SSE addss): a NaN operand propagates quieted, the first
-// operand winning; an invalid sum (inf - inf) yields the default NaN
-// 0xffc00000.  The GPU's adder returns one canonical NaN instead, so without
-// this the narrowed bf16 of a NaN result would differ from the golden.
+// fp32 addition with the NaN results of the x86-64 build of the reference
+// golden (`f(a) + f(b)` compiled to SSE addss / addps): a NaN operand
+// propagates quieted, the SECOND operand winning when both are NaN; an
+// invalid sum (inf - inf) yields the default NaN 0xffc00000.  The GPU's adder
+// returns one canonical NaN instead, so without this the narrowed bf16 of a
+// NaN result would differ from the golden.
 __device__ __forceinline__ float host_add_f32(float a, float b) {
     const float sum = __fadd_rn(a, b);
     if (sum == sum) return sum;  // no NaN operand and no invalid operation
     const uint32_t ua = __float_as_uint(a), ub = __float_as_uint(b);
     const bool na = (ua & 0x7fffffffu) > 0x7f800000u;
     const bool nb = (ub & 0x7fffffffu) > 0x7f800000u;
-    if (na) return __uint_as_float(ua | 0x00400000u);
     if (nb) return __uint_as_float(ub | 0x00400000u);
+    if (na) return __uint_as_float(ua | 0x00400000u);
     return __uint_as_float(0xffc00000u);
 }
 

@@ -1,33 +1,93 @@
-// Element-wise kernels on bf16 streams: add_tiles, relu, bias_add.
+// Element-wise kernels: tile_copy, relu, add_tiles, bias_add, as one
+// streaming pipeline on bulk copies.
 //
-// Memory-bound: each thread moves 16-byte vectors (8 bf16) with streaming
-// cache hints, several vectors in flight, in a grid-stride loop sized to a
-// multiple of the SM count.  The arithmetic is the reference golden's:
-// widen to fp32, operate, narrow with the golden's round-to-nearest-even
-// integer formula (tests/tile_utils.hpp:33-47), so results are bit-exact.
-#include "common.cuh"
-#include "../../../include/foil_c.h"
+// An SM-issued 16-byte load/store stream tops out at about 0.9 of the HBM
+// copy rate on B200 (each SM keeps only so many LSU requests in flight); the
+// bulk copy engine moves whole 8-32 KiB chunks per instruction instead.  Each
+// CTA owns chunks blockIdx.x, blockIdx.x + gridDim.x, ... and cycles them
+// through BUFS shared-memory buffers:
+//
+//   producer thread:  bulk load chunk -> buffer b         (full[b], tx bytes)
+//   compute warps:    op in place in buffer b              (done[b], per warp)
+//   producer thread:  bulk store buffer b -> out, then reload b with the
+//                     chunk BUFS steps ahead once the store has read it.
+//
+// tile_copy has no compute stage (the store follows full[b] directly).  The
+// arithmetic is the golden's: bf16 widened to fp32, operated on, narrowed
+// with round-to-nearest-even and the x86 host's NaN results
+// (tests/tile_utils.hpp:33-47, tests/test_relu.cpp:54-59,
+// tests/test_add_tiles.cpp:60), bit-exact.  Every wait is bounded; a timeout
+// raises the CTA's abort flag and sets kErrWaitTimeout in the error word.
+#include "eltwise.cuh"
 
-extern "C" void foil_set_error(int status, const char* msg);
+#include "gemm_ptx.cuh"
 
 namespace foil {
+namespace stream {
 namespace {
 
-__device__ __forceinline__ uint32_t add2(uint32_t a, uint32_t b) {
+using gemm::bulk_commit;
+using gemm::bulk_store;
+using gemm::bulk_wait_all;
+using gemm::bulk_wait_read;
+using gemm::mbar_arrive;
+using gemm::mbar_drain;
+using gemm::mbar_expect_tx;
+using gemm::mbar_init;
+using gemm::mbar_wait;
+using gemm::smem_u32;
+
+// Pipeline shape of one instantiation: BUFS buffers of CHUNK bytes per input
+// stream, CTAS CTAs per SM, WARPS compute warps (none for tile_copy).
+template <int OP, int BUFS, uint32_t CHUNK, int CTAS, int WARPS>
+struct Cfg {
+    static constexpr int kStreams = OP == kAdd ? 2 : 1;
+    static constexpr int kWarps = OP == kCopy ? 0 : WARPS;
+    static constexpr int kThreads = 32 * (1 + kWarps);
+    static constexpr uint32_t kStage = BUFS * CHUNK;             // one stream
+    static constexpr uint32_t kBarOff = kStreams * kStage;
+    static constexpr uint32_t kSmem = kBarOff + 2 * BUFS * 8 + 16;
+    static_assert(CHUNK % 2048 == 0 && BUFS >= 2, "pipeline shape");
+    static_assert(OP != kBias || (32 * WARPS) % 128 == 0, "bias: whole tiles per compute pass");
+};
+
+__device__ __forceinline__ void bulk_load(uint32_t dst, const void* src, uint32_t bytes,
+                                          uint64_t* bar) {
+    asm volatile(
+        "cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];" ::"r"(dst),
+        "l"(src), "r"(bytes), "r"(smem_u32(bar))
+        : "memory");
+}
+
+__device__ __forceinline__ void fence_async_shared() {
+    asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+}
+
+__device__ __forceinline__ uint32_t add2_golden(uint32_t a, uint32_t b) {
     float lo = host_add_f32(bf16_bits_to_f32(a & 0xffffu), bf16_bits_to_f32(b & 0xffffu));
     float hi = host_add_f32(bf16_bits_to_f32(a >> 16), bf16_bits_to_f32(b >> 16));
     return pack_bf16x2(f32_to_bf16_bits(lo), f32_to_bf16_bits(hi));
 }
-
-// max(x, 0) as the golden computes it: `v < 0.0f ? 0.0f : v`
-// (tests/test_relu.cpp:54-59).  -0.0 and NaN pass through unchanged.
-__device__ __forceinline__ uint32_t relu1(uint32_t b) {
-    return bf16_bits_to_f32(b) < 0.0f ? 0u : b;
+// The golden rounds twice (exact sum -> fp32 -> bf16, round to nearest
+// even); a single bf16 rounding of the exact sum gives the same bits for
+// two bf16 operands: their exact sum needs more than 24 significant bits
+// only when the exponents differ by more than 16, and then the bits between
+// the bf16 rounding position and the smaller operand are all equal (zeros
+// or, for a difference, ones), so the fp32 rounding can neither create nor
+// cross a bf16 tie.  NaN results (NaN operand or inf - inf) take the golden
+// path for the host's NaN bits.
+__device__ __forceinline__ uint32_t add2(uint32_t a, uint32_t b) {
+    uint32_t r;
+    asm("add.rn.bf16x2 %0, %1, %2;" : "=r"(r) : "r"(a), "r"(b));
+    const uint32_t m = r & 0x7fff7fffu;
+    if ((m & 0xffffu) > 0x7f80u || (m >> 16) > 0x7f80u) return add2_golden(a, b);
+    return r;
 }
+// `v < 0.0f ? 0.0f : v` per element: -0.0 and NaN pass through unchanged.
+__device__ __forceinline__ uint32_t relu1(uint32_t b) { return bf16_bits_to_f32(b) < 0.0f ? 0u : b; }
 __device__ __forceinline__ uint32_t relu2(uint32_t w) {
     return relu1(w & 0xffffu) | (relu1(w >> 16) << 16);
 }
-
 __device__ __forceinline__ uint4 add_v(uint4 a, uint4 b) {
     return make_uint4(add2(a.x, b.x), add2(a.y, b.y), add2(a.z, b.z), add2(a.w, b.w));
 }
@@ -35,63 +95,124 @@ __device__ __forceinline__ uint4 relu_v(uint4 a) {
     return make_uint4(relu2(a.x), relu2(a.y), relu2(a.z), relu2(a.w));
 }
 
-__global__ void __launch_bounds__(256)
-add_kernel(const uint4* __restrict__ a, const uint4* __restrict__ b,
-           uint4* __restrict__ out, uint64_t n8) {
-    const uint64_t stride = (uint64_t)gridDim.x * blockDim.x;
-    uint64_t i = (uint64_t)blockIdx.x * blockDim.x + threadIdx.x;
-    for (; i + stride < n8; i += 2 * stride) {
-        uint4 a0 = __ldcs(a + i), b0 = __ldcs(b + i);
-        uint4 a1 = __ldcs(a + i + stride), b1 = __ldcs(b + i + stride);
-        __stcs(out + i, add_v(a0, b0));
-        __stcs(out + i + stride, add_v(a1, b1));
-    }
-    for (; i < n8; i += stride) __stcs(out + i, add_v(__ldcs(a + i), __ldcs(b + i)));
+template <uint32_t CHUNK>
+__device__ __forceinline__ uint32_t chunk_bytes(uint64_t chunk, uint64_t bytes) {
+    const uint64_t off = chunk * CHUNK;
+    return (uint32_t)(bytes - off < CHUNK ? bytes - off : CHUNK);
 }
 
-__global__ void __launch_bounds__(256)
-relu_kernel(const uint4* __restrict__ in, uint4* __restrict__ out, uint64_t n8) {
-    const uint64_t stride = (uint64_t)gridDim.x * blockDim.x;
-    uint64_t i = (uint64_t)blockIdx.x * blockDim.x + threadIdx.x;
-    for (; i + 3 * stride < n8; i += 4 * stride) {
-        uint4 x0 = __ldcs(in + i), x1 = __ldcs(in + i + stride);
-        uint4 x2 = __ldcs(in + i + 2 * stride), x3 = __ldcs(in + i + 3 * stride);
-        __stcs(out + i, relu_v(x0));
-        __stcs(out + i + stride, relu_v(x1));
-        __stcs(out + i + 2 * stride, relu_v(x2));
-        __stcs(out + i + 3 * stride, relu_v(x3));
+// One CTA: warp 0 lane 0 is the copy producer, warps 1.. compute in place.
+// bias: `a` is a tile-layout matrix with Nt tile columns; a 16-byte vector at
+// byte offset o lies in tile o / 2048 (tile column (o / 2048) % Nt) as chunk
+// c = (o % 2048) / 16 of the tile, face c / 32, face column (c / 32) & 1,
+// half-row c & 1.  Its bias is row 0 of that column's bias tile:
+// bias_tiles[nt * 1024 + ((c / 32) & 1) * 256 + (c & 1) * 8 + 0..7].
+template <int OP, int BUFS, uint32_t CHUNK, int CTAS, int WARPS>
+__global__ void __launch_bounds__(Cfg<OP, BUFS, CHUNK, CTAS, WARPS>::kThreads, CTAS)
+stream_kernel(const uint8_t* a, const uint8_t* b, uint8_t* out, uint64_t bytes,
+              const uint16_t* __restrict__ bias_tiles, uint32_t Nt, uint32_t* err) {
+    using C = Cfg<OP, BUFS, CHUNK, CTAS, WARPS>;
+    extern __shared__ __align__(128) uint8_t smem[];
+    uint64_t* full = reinterpret_cast<uint64_t*>(smem + C::kBarOff);
+    uint64_t* done = full + BUFS;
+    volatile uint32_t* abort_flag = reinterpret_cast<volatile uint32_t*>(done + BUFS);
+    const uint32_t base = smem_u32(smem);
+    const uint32_t warp = threadIdx.x >> 5, lane = threadIdx.x & 31u;
+
+    if (threadIdx.x == 0) {
+        for (int i = 0; i < BUFS; ++i) {
+            mbar_init(&full[i], 1);
+            mbar_init(&done[i], C::kWarps > 0 ? C::kWarps : 1);
+        }
+        *abort_flag = 0u;
+        asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
     }
-    for (; i < n8; i += stride) __stcs(out + i, relu_v(__ldcs(in + i)));
+    __syncthreads();
+
+    const uint64_t nchunks = (bytes + CHUNK - 1) / CHUNK;
+    const uint64_t first = blockIdx.x, step = gridDim.x;
+    if (first >= nchunks) return;
+    const uint64_t mine = (nchunks - 1 - first) / step + 1;  // chunks of this CTA
+
+    if (warp == 0) {
+        if (lane != 0) return;
+        auto load = [&](uint64_t k) {
+            const int bi = (int)(k % BUFS);
+            const uint64_t chunk = first + k * step;
+            const uint32_t n = chunk_bytes<CHUNK>(chunk, bytes);
+            mbar_expect_tx(&full[bi], n * C::kStreams);
+            bulk_load(base + bi * CHUNK, a + chunk * CHUNK, n, &full[bi]);
+            if (OP == kAdd) bulk_load(base + C::kStage + bi * CHUNK, b + chunk * CHUNK, n, &full[bi]);
+        };
+        const uint64_t pro = mine < (uint64_t)BUFS ? mine : (uint64_t)BUFS;
+        for (uint64_t k = 0; k < pro; ++k) load(k);
+        // Loads are issued for chunks [0, issued).
+        uint64_t issued = pro, k = 0;
+        bool ok = true;
+        for (; k < mine; ++k) {
+            const int bi = (int)(k % BUFS);
+            const uint32_t ph = (uint32_t)((k / BUFS) & 1u);
+            if (!mbar_wait(OP == kCopy ? &full[bi] : &done[bi], ph, abort_flag, err)) {
+                ok = false;
+                break;
+            }
+            const uint64_t chunk = first + k * step;
+            bulk_store(out + chunk * CHUNK, base + bi * CHUNK, chunk_bytes<CHUNK>(chunk, bytes));
+            bulk_commit();
+            if (issued < mine) {
+                bulk_wait_read();  // buffer bi has been read by its store
+                load(issued++);
+            }
+        }
+        if (!ok) {
+            // Loads issued for chunks k .. issued - 1 may still land in
+            // shared memory: wait (bounded) for each before the CTA's shared
+            // memory is released.
+            for (uint64_t j = k; j < issued; ++j)
+                mbar_drain(&full[j % BUFS], (uint32_t)((j / BUFS) & 1u), 100000000ull);
+        }
+        bulk_wait_all();
+        return;
+    }
+
+    // compute warps
+    const uint32_t t = threadIdx.x - 32u;
+    constexpr uint32_t kT = 32u * C::kWarps;
+    for (uint64_t k = 0; k < mine; ++k) {
+        const int bi = (int)(k % BUFS);
+        const uint32_t ph = (uint32_t)((k / BUFS) & 1u);
+        if (!mbar_wait(&full[bi], ph, abort_flag, err)) return;
+        const uint64_t chunk = first + k * step;
+        const uint32_t nv = chunk_bytes<CHUNK>(chunk, bytes) / 16u;
+        uint4* va = reinterpret_cast<uint4*>(smem + bi * CHUNK);
+        if (OP == kRelu) {
+#pragma unroll 4
+            for (uint32_t v = t; v < nv; v += kT) va[v] = relu_v(va[v]);
+        } else if (OP == kAdd) {
+            const uint4* vb = reinterpret_cast<const uint4*>(smem + C::kStage + bi * CHUNK);
+#pragma unroll 4
+            for (uint32_t v = t; v < nv; v += kT) va[v] = add_v(va[v], vb[v]);
+        } else if (OP == kBias) {
+            // A pass of kT vectors covers kT / 128 whole tiles: thread t
+            // handles chunk c = t % 128 of tile t / 128 of each pass.
+            constexpr uint32_t kPassTiles = kT / 128u;
+            uint32_t nt = (uint32_t)((chunk * (CHUNK / 2048u) + t / 128u) % Nt);
+            const uint16_t* bt = bias_tiles + ((t >> 5) & 1u) * 256u + (t & 1u) * 8u;
+#pragma unroll 4
+            for (uint32_t v = t; v < nv; v += kT) {
+                const uint4 bv = __ldg(reinterpret_cast<const uint4*>(bt + (uint64_t)nt * 1024u));
+                va[v] = add_v(va[v], bv);
+                nt += kPassTiles;
+                if (nt >= Nt) nt = kPassTiles < Nt ? nt - Nt : nt % Nt;
+            }
+        }
+        fence_async_shared();
+        __syncwarp();
+        if (lane == 0) mbar_arrive(&done[bi]);
+    }
 }
 
-// Bias add over a tile-layout matrix with Nt tile-columns, one warp per
-// 2 KiB tile.  Lane l handles the 16-byte chunks l, l+32, l+64, l+96 of the
-// tile: chunk c lies in face c/32 (face column (c/32) & 1) and covers columns
-// ((c/32) & 1) * 16 + (l & 1) * 8 + [0, 8) of the tile.  The bias for column n
-// is in row 0 of bias tile n/32, i.e. at (n/32) * 1024 + ((n%32)/16) * 256 + n%16,
-// so each lane loads its two bias vectors once per tile.
-__global__ void __launch_bounds__(256)
-bias_kernel(const uint4* __restrict__ in, const uint16_t* __restrict__ bias_tiles,
-            uint4* __restrict__ out, uint64_t num_tiles, uint32_t Nt) {
-    const uint32_t lane = threadIdx.x & 31u;
-    const uint64_t warps = (uint64_t)gridDim.x * (blockDim.x >> 5);
-    for (uint64_t t = (uint64_t)blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5); t < num_tiles;
-         t += warps) {
-        const uint32_t nt = (uint32_t)(t % Nt);
-        const uint16_t* bt = bias_tiles + (uint64_t)nt * 1024 + (lane & 1u) * 8u;
-        const uint4 b0 = __ldg(reinterpret_cast<const uint4*>(bt));        // face column 0
-        const uint4 b1 = __ldg(reinterpret_cast<const uint4*>(bt + 256));  // face column 1
-        const uint4* src = in + t * 128u + lane;
-        uint4* dst = out + t * 128u + lane;
-        uint4 x0 = __ldcs(src), x1 = __ldcs(src + 32), x2 = __ldcs(src + 64), x3 = __ldcs(src + 96);
-        __stcs(dst, add_v(x0, b0));
-        __stcs(dst + 32, add_v(x1, b1));
-        __stcs(dst + 64, add_v(x2, b0));
-        __stcs(dst + 96, add_v(x3, b1));
-    }
-}
-
-int grid_for(uint64_t work_items) {
+int sm_count() {
     static int sms = 0;
     if (sms == 0) {
         int dev = 0;
@@ -99,75 +220,42 @@ int grid_for(uint64_t work_items) {
         cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
         if (sms <= 0) sms = 148;
     }
-    uint64_t want = (work_items + 255) / 256;
-    uint64_t cap = (uint64_t)sms * 8;  // 8 x 256-thread CTAs per SM
-    return (int)(want < cap ? (want ? want : 1) : cap);
+    return sms;
 }
 
-int check(const char* what) {
-    cudaError_t e = cudaGetLastError();
-    if (e != cudaSuccess) {
-        char buf[256];
-        snprintf(buf, sizeof buf, "%s: CUDA launch failed: %s", what, cudaGetErrorString(e));
-        foil_set_error(FOIL_ERR_CUDA, buf);
-        return FOIL_ERR_CUDA;
+template <int OP, int BUFS, uint32_t CHUNK, int CTAS, int WARPS>
+int launch_op(const void* a, const void* b, void* out, uint64_t bytes, const uint16_t* bias_tiles,
+              uint32_t Nt, uint32_t* err, cudaStream_t stream) {
+    using C = Cfg<OP, BUFS, CHUNK, CTAS, WARPS>;
+    auto kern = stream_kernel<OP, BUFS, CHUNK, CTAS, WARPS>;
+    static bool attr_set = false;  // per instantiation, per process
+    if (!attr_set) {
+        cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)C::kSmem);
+        if (e != cudaSuccess) return (int)e;
+        attr_set = true;
     }
-    foil_count_launch();
-    return FOIL_OK;
+    const uint64_t nchunks = (bytes + CHUNK - 1) / CHUNK;
+    const uint64_t cap = (uint64_t)sm_count() * CTAS;
+    const unsigned grid = (unsigned)(nchunks < cap ? nchunks : cap);
+    kern<<<grid, C::kThreads, C::kSmem, stream>>>(static_cast<const uint8_t*>(a),
+                                                   static_cast<const uint8_t*>(b),
+                                                   static_cast<uint8_t*>(out), bytes, bias_tiles, Nt, err);
+    return (int)cudaGetLastError();
 }
-
-bool ok16(const void* p) { return p && ((uintptr_t)p & 15u) == 0; }
 
 }  // namespace
+
+int launch(Op op, const void* a, const void* b, void* out, uint64_t bytes, const uint16_t* bias_tiles,
+           uint32_t Nt, uint32_t* err, cudaStream_t stream) {
+    if (bytes == 0) return 0;
+    switch (op) {
+        case kCopy: return launch_op<kCopy, 4, 32768, 1, 0>(a, b, out, bytes, bias_tiles, Nt, err, stream);
+        case kRelu: return launch_op<kRelu, 6, 16384, 2, 4>(a, b, out, bytes, bias_tiles, Nt, err, stream);
+        case kAdd: return launch_op<kAdd, 4, 8192, 2, 12>(a, b, out, bytes, bias_tiles, Nt, err, stream);
+        case kBias: return launch_op<kBias, 6, 16384, 2, 12>(a, b, out, bytes, bias_tiles, Nt, err, stream);
+    }
+    return (int)cudaErrorInvalidValue;
+}
+
+}  // namespace stream
 }  // namespace foil
-
-extern "C" int foil_add_tiles_dev(const uint16_t* a, const uint16_t* b, uint16_t* out,
-                                  uint64_t n, void* stream) {
-    if (n % 8) {
-        foil_set_error(FOIL_ERR_INVALID, "foil_add_tiles_dev: n must be a multiple of 8");
-        return FOIL_ERR_INVALID;
-    }
-    if (n == 0) return FOIL_OK;
-    if (!foil::ok16(a) || !foil::ok16(b) || !foil::ok16(out)) {
-        foil_set_error(FOIL_ERR_INVALID, "foil_add_tiles_dev: null or misaligned pointer");
-        return FOIL_ERR_INVALID;
-    }
-    uint64_t n8 = n / 8;
-    foil::add_kernel<<<foil::grid_for(n8), 256, 0, (cudaStream_t)stream>>>(
-        (const uint4*)a, (const uint4*)b, (uint4*)out, n8);
-    return foil::check("foil_add_tiles_dev");
-}
-
-extern "C" int foil_relu_tiles_dev(const uint16_t* in, uint16_t* out, uint64_t n, void* stream) {
-    if (n % 8) {
-        foil_set_error(FOIL_ERR_INVALID, "foil_relu_tiles_dev: n must be a multiple of 8");
-        return FOIL_ERR_INVALID;
-    }
-    if (n == 0) return FOIL_OK;
-    if (!foil::ok16(in) || !foil::ok16(out)) {
-        foil_set_error(FOIL_ERR_INVALID, "foil_relu_tiles_dev: null or misaligned pointer");
-        return FOIL_ERR_INVALID;
-    }
-    uint64_t n8 = n / 8;
-    foil::relu_kernel<<<foil::grid_for(n8), 256, 0, (cudaStream_t)stream>>>(
-        (const uint4*)in, (uint4*)out, n8);
-    return foil::check("foil_relu_tiles_dev");
-}
-
-extern "C" int foil_bias_add_tiles_dev(const uint16_t* in, const uint16_t* bias_tiles,
-                                       uint16_t* out, uint32_t rows, uint32_t cols,
-                                       void* stream) {
-    if (rows % 32 || cols % 32) {
-        foil_set_error(FOIL_ERR_INVALID, "foil_bias_add_tiles_dev: rows and cols must be multiples of 32");
-        return FOIL_ERR_INVALID;
-    }
-    if (rows == 0 || cols == 0) return FOIL_OK;
-    if (!foil::ok16(in) || !foil::ok16(out) || !foil::ok16(bias_tiles)) {
-        foil_set_error(FOIL_ERR_INVALID, "foil_bias_add_tiles_dev: null or misaligned pointer");
-        return FOIL_ERR_INVALID;
-    }
-    const uint64_t tiles = (uint64_t)(rows / 32) * (cols / 32);
-    foil::bias_kernel<<<foil::grid_for(tiles * 32), 256, 0, (cudaStream_t)stream>>>(
-        (const uint4*)in, bias_tiles, (uint4*)out, tiles, cols / 32);
-    return foil::check("foil_bias_add_tiles_dev");
-}

@@ -1,4 +1,4 @@
-// Layout kernels: tilize, untilize, tile_copy.
+// Layout kernels: tilize, untilize.
 //
 // Tile layout (the tt-foil wire format, tests/tile_utils.hpp:4-12): a 32x32
 // bf16 tile is four 16x16 faces, each row-major; a face row is 16 values =
@@ -94,24 +94,6 @@ untilize_kernel(const uint4* __restrict__ in, uint4* __restrict__ out,
     }
 }
 
-// Identity copy, 4 x 16 bytes in flight per thread.
-__global__ void __launch_bounds__(256)
-copy_kernel(const uint4* __restrict__ src, uint4* __restrict__ dst, uint64_t n16) {
-    const uint64_t stride = (uint64_t)gridDim.x * blockDim.x;
-    uint64_t i = (uint64_t)blockIdx.x * blockDim.x + threadIdx.x;
-    for (; i + 3 * stride < n16; i += 4 * stride) {
-        uint4 a = __ldcs(src + i);
-        uint4 b = __ldcs(src + i + stride);
-        uint4 c = __ldcs(src + i + 2 * stride);
-        uint4 d = __ldcs(src + i + 3 * stride);
-        __stcs(dst + i, a);
-        __stcs(dst + i + stride, b);
-        __stcs(dst + i + 2 * stride, c);
-        __stcs(dst + i + 3 * stride, d);
-    }
-    for (; i < n16; i += stride) __stcs(dst + i, __ldcs(src + i));
-}
-
 int sm_count() {
     static int n = 0;
     if (n == 0) {
@@ -176,22 +158,4 @@ extern "C" int foil_untilize_dev(const uint16_t* tiles, uint16_t* row_major,
     foil::untilize_kernel<<<(unsigned)grid, foil::kLayoutThreads, 0, (cudaStream_t)stream>>>(
         (const uint4*)tiles, (uint4*)row_major, rows, cols);
     return check_launch("foil_untilize_dev");
-}
-
-extern "C" int foil_tile_copy_dev(const void* src, void* dst, uint64_t bytes, void* stream) {
-    if (bytes % 16) {
-        foil_set_error(FOIL_ERR_INVALID, "foil_tile_copy_dev: bytes must be a multiple of 16");
-        return FOIL_ERR_INVALID;
-    }
-    if (bytes == 0) return FOIL_OK;
-    if (!src || !dst || !aligned16(src) || !aligned16(dst)) {
-        foil_set_error(FOIL_ERR_INVALID, "foil_tile_copy_dev: null or misaligned pointer");
-        return FOIL_ERR_INVALID;
-    }
-    uint64_t n16 = bytes / 16;
-    uint64_t want = (n16 + 255) / 256;
-    uint64_t cap = (uint64_t)foil::sm_count() * 8;
-    unsigned grid = (unsigned)(want < cap ? want : cap);
-    foil::copy_kernel<<<grid, 256, 0, (cudaStream_t)stream>>>((const uint4*)src, (uint4*)dst, n16);
-    return check_launch("foil_tile_copy_dev");
 }
