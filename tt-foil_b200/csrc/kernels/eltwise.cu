@@ -27,6 +27,7 @@ namespace stream {
 namespace {
 
 using gemm::bulk_commit;
+using gemm::bulk_load;
 using gemm::bulk_store;
 using gemm::bulk_wait_all;
 using gemm::bulk_wait_read;
@@ -50,14 +51,6 @@ struct Cfg {
     static_assert(CHUNK % 2048 == 0 && BUFS >= 2, "pipeline shape");
     static_assert(OP != kBias || (32 * WARPS) % 128 == 0, "bias: whole tiles per compute pass");
 };
-
-__device__ __forceinline__ void bulk_load(uint32_t dst, const void* src, uint32_t bytes,
-                                          uint64_t* bar) {
-    asm volatile(
-        "cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];" ::"r"(dst),
-        "l"(src), "r"(bytes), "r"(smem_u32(bar))
-        : "memory");
-}
 
 __device__ __forceinline__ void fence_async_shared() {
     asm volatile("fence.proxy.async.shared::cta;" ::: "memory");

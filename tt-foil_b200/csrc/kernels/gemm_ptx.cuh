@@ -228,6 +228,15 @@ __device__ __forceinline__ void tmem_ld32(uint32_t taddr, uint32_t (&v)[32]) {
         : "r"(taddr));
 }
 
+// Bulk (non-tensor) global -> shared copy of `bytes` (multiple of 16, both
+// addresses 16-byte aligned), completing on `bar` (no multicast).
+__device__ __forceinline__ void bulk_load(uint32_t dst, const void* src, uint32_t bytes, uint64_t* bar) {
+    asm volatile(
+        "cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];" ::"r"(dst),
+        "l"(src), "r"(bytes), "r"(smem_u32(bar))
+        : "memory");
+}
+
 // Bulk (non-tensor) shared -> global copy of `bytes` (multiple of 16, both
 // addresses 16-byte aligned), tracked by this thread's bulk groups.
 __device__ __forceinline__ void bulk_store(void* gdst, uint32_t ssrc, uint32_t bytes) {
