@@ -266,6 +266,33 @@ FOIL_API int foil_matmul_tiles_dev(const uint16_t* a, const uint16_t* b, uint16_
                           uint32_t Mt, uint32_t Kt, uint32_t Nt,
                           const uint16_t* bias, int32_t relu, void* stream);
 
+/* foil_matmul_tiles_dev whose kernel is also its own all-gather: every
+ * output tile is stored to `c` and to each of peer_c[0 .. npeers) (at most
+ * 7), other GPUs' buffers opened with foil_peer_open and offset like `c`.
+ * With the rows of C split over the GPUs of a node (each rank computing its
+ * tile rows into its slice of a full-size C), one launch per rank leaves the
+ * whole C on every GPU once all ranks' launches are complete (order a
+ * collective, e.g. a one-element all-reduce, after the launch before reading
+ * the peers' rows).  Replaces the per-core row split of
+ * tests/test_matmul_2core.cpp:43-63 (tests/test_matmul_4x2.cpp:164-180
+ * stitches the shards on the host) followed by a separate gather. */
+FOIL_API int foil_matmul_tiles_gather_dev(const uint16_t* a, const uint16_t* b, uint16_t* c,
+                          uint16_t* const* peer_c, uint32_t npeers,
+                          uint32_t Mt, uint32_t Kt, uint32_t Nt,
+                          const uint16_t* bias, int32_t relu, void* stream);
+
+/* Device buffers shared between the processes of a node (CUDA IPC).
+ * foil_peer_alloc allocates `bytes` on CUDA device `device` and writes its
+ * 64-byte export handle; another process passes the handle to
+ * foil_peer_open to get a pointer to the same memory usable from its own
+ * device (peer access over NVLink), and releases it with foil_peer_close.
+ * The owner frees with foil_peer_free after every opener has closed it. */
+#define FOIL_PEER_HANDLE_BYTES 64
+FOIL_API int foil_peer_alloc(int32_t device, uint64_t bytes, void** ptr, uint8_t* handle);
+FOIL_API int foil_peer_open(int32_t device, const uint8_t* handle, void** ptr);
+FOIL_API int foil_peer_close(int32_t device, void* ptr);
+FOIL_API int foil_peer_free(int32_t device, void* ptr);
+
 /* NHWC convolution as an implicit GEMM on tcgen05 tensor cores, with fused
  * bias and relu: y (N, Ho, Wo, Cout) = relu?(bf16(bf16(conv(x, w)) + bias)),
  * x (N, H, W, Cin), w (Cout, KH, KW, Cin), bias (Cout) or NULL, fp32

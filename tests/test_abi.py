@@ -122,6 +122,15 @@ def test_validation_errors_without_gpu():
     assert L.foil_bias_add_tiles_dev(base, base + (1 << 20) + 512, base + (1 << 20), 32, 64, None) == 1
     assert b"bias band" in L.foil_last_error()
     assert L.foil_matmul_tiles_dev(None, None, None, 70000, 1, 1, None, 0, None) == 1
+    # GEMM with its own all-gather: peer-list checks precede any CUDA call
+    peers = (ctypes.c_void_p * 8)(*([base] * 8))
+    assert L.foil_matmul_tiles_gather_dev(None, None, None, peers, 8, 1, 1, 1, None, 0, None) == 1
+    assert b"at most 7" in L.foil_last_error()
+    assert L.foil_matmul_tiles_gather_dev(None, None, None, None, 2, 1, 1, 1, None, 0, None) == 1
+    peers[1] = base + 8
+    assert L.foil_matmul_tiles_gather_dev(None, None, None, peers, 2, 1, 1, 1, None, 0, None) == 1
+    assert b"peer buffer" in L.foil_last_error()
+    assert L.foil_peer_alloc(0, 0, None, None) == 1
     assert L.foil_matmul_tiles_host(0, None, None, None, 1, 1, 1, None, 0, 0) == 1
     assert b"null pointer" in L.foil_last_error()
     assert L.foil_matmul_tiles_host(0, None, None, None, 70000, 1, 1, None, 0, 0) == 1

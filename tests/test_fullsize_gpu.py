@@ -69,6 +69,37 @@ def test_gemm_full_size_sampled_rows(env, M, N, K):
     del a, b, c
 
 
+def band_rows(t, r0, nrows, cols):
+    """Rows [r0, r0 + nrows) (r0, nrows multiples of 32) of a tile-layout
+    matrix with `cols` columns, from a CUDA tensor, row-major."""
+    ct = cols // 32
+    lo, hi = (r0 // 32) * ct * 1024, ((r0 + nrows) // 32) * ct * 1024
+    return oracle.untilize(bits(t[lo:hi]), nrows, cols)
+
+
+def test_gemm_8192_full_block_rows(env):
+    """8192^3: every element of the first and the last 128 x N block row
+    (the half pair-tiles of the first and last 2-SM row blocks, all 32
+    column tiles of each) against the oracle's sequential fp32 dot
+    products."""
+    torch, tf = env
+    M = N = K = 8192
+    a = rnd_dev(torch, M * K, 11)
+    b = rnd_dev(torch, K * N, 12)
+    c = torch.empty(M * N, dtype=torch.int16, device="cuda")
+    tf.matmul_tiles(a, b, c, M // 32, K // 32, N // 32)
+    torch.cuda.synchronize()
+    assert tf.device_error() == 0
+    b_rm = oracle.untilize(bits(b), K, N)
+    for r0 in (0, M - 128):
+        exp = oracle.matmul(band_rows(a, r0, 128, K), b_rm, threads=16)
+        got = band_rows(c, r0, 128, N)
+        assert oracle.normalized_error(got, exp, K, 1.0, 1.0) <= 1e-2, r0
+        bad, wa, wr = oracle.compare(got, exp)
+        assert bad == 0, (r0, bad, wa, wr)
+    del a, b, c
+
+
 def test_gemm_linearity_full_width(env):
     """C(B1 + B2) == C(B1) + C(B2) exactly for small-integer operands at
     16384 x 8192 x 8192: every product and partial sum is an exact fp32

@@ -248,6 +248,29 @@ def test_gemm_shapes_and_tails(torch_cuda, tf, Mt, Kt, Nt):
     check_gemm(got, oracle.matmul(a, b, threads=8), a, b, Kt * 32)
 
 
+@pytest.mark.parametrize("Mt,Kt,Nt", [(3, 4, 5), (20, 6, 9), (17, 5, 24)])
+def test_gemm_output_only_16_byte_aligned(torch_cuda, tf, Mt, Kt, Nt):
+    """C at a 16-byte (not 32-byte) aligned address, as the 16-byte L1 bump
+    allocator can hand out: the epilogue's 128-bit store path gives the same
+    bits as the 256-bit path (each of the three kernels)."""
+    torch = torch_cuda
+    a = oracle.rand_bf16((Mt * 32, Kt * 32), 70 + Mt)
+    b = oracle.rand_bf16((Kt * 32, Nt * 32), 71 + Nt)
+    ad, bd = dev(torch, oracle.tilize(a)), dev(torch, oracle.tilize(b))
+    n = Mt * Nt * 1024
+    c32 = empty(torch, n)
+    buf = torch.full((n + 16,), 0x1234, dtype=torch.int16, device="cuda")
+    c16 = buf[8:8 + n]                       # +16 bytes
+    assert c16.data_ptr() % 32 == 16
+    tf.matmul_tiles(ad, bd, c32, Mt, Kt, Nt)
+    tf.matmul_tiles(ad, bd, c16, Mt, Kt, Nt)
+    torch.cuda.synchronize()
+    assert tf.device_error() == 0
+    assert torch.equal(c32, c16)
+    assert torch.all(buf[:8] == 0x1234) and torch.all(buf[8 + n:] == 0x1234)
+    check_gemm(oracle.untilize(host(c16), Mt * 32, Nt * 32), oracle.matmul(a, b, threads=8), a, b, Kt * 32)
+
+
 def test_gemm_fused_bias_relu(torch_cuda, tf):
     Mt, Kt, Nt = 6, 9, 10
     a = oracle.rand_bf16((Mt * 32, Kt * 32), 21)

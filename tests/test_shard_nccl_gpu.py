@@ -1,7 +1,13 @@
-"""Row-sharded 'same' convolution across 2 GPUs (NCCL point-to-point halo
-exchange, then the implicit-GEMM kernel on each GPU): every rank's output
-rows equal the oracle's rows of the unsharded convolution.  Needs 2 GPUs;
-skipped otherwise."""
+"""Two-GPU paths (skipped with fewer GPUs):
+
+* row-sharded 'same' convolution (NCCL point-to-point halo exchange, then the
+  implicit-GEMM kernel on each GPU): every rank's output rows equal the
+  oracle's rows of the unsharded convolution;
+* the row-sharded GEMM whose kernel is its own all-gather (every output tile
+  stored to both GPUs' copies of C over NVLink): after the fence, both
+  copies equal the per-rank results of the plain GEMM concatenated (bit for
+  bit, same kernel), and the oracle on sampled rows.
+"""
 import datetime
 import os
 import socket
@@ -49,6 +55,83 @@ def worker(rank, world, port, q):
         q.put((rank, bool(ok)))
     finally:
         dist.destroy_process_group()
+
+
+def gather_worker(rank, world, port, q):
+    import sys
+    repo = os.path.dirname(os.path.dirname(os.path.abspath(__file__)))
+    sys.path[:0] = [repo, os.path.join(repo, "tt-foil_b200")]
+    os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port), NCCL_NVLS_ENABLE="0")
+    import torch
+    import torch.distributed as dist
+    from oracle import oracle
+    import ttfoil
+    from ttfoil import shard
+    torch.cuda.set_device(rank)
+    dist.init_process_group("nccl", rank=rank, world_size=world, timeout=datetime.timedelta(seconds=60),
+                            device_id=torch.device("cuda", rank))
+    ok = []
+    try:
+        # Mt odd -> uneven row split; Nt 8 (same kernel as the plain GEMM) and
+        # 24 (the plain GEMM takes the 512-column kernel there).
+        for (Mt, Kt, Nt) in ((25, 16, 8), (19, 12, 24)):
+            a_all = oracle.rand_bf16(Mt * Kt * 1024, 40 + Nt)
+            b = oracle.rand_bf16(Kt * Nt * 1024, 41 + Nt)
+            dev = lambda arr: torch.from_numpy(np.ascontiguousarray(arr).view(np.int16)).cuda()
+            g = shard.GatheredTiles(Mt, Nt)
+            m0, m1 = g.rows
+            a_r = dev(a_all[m0 * Kt * 1024:m1 * Kt * 1024])
+            b_d = dev(b)
+            g.tensor().fill_(0x7fff)
+            torch.cuda.synchronize()
+            dist.barrier()          # no rank's GEMM may land before every fill
+            g.matmul(a_r, b_d, Kt)
+            g.fence()
+            torch.cuda.synchronize()
+            full = g.tensor().cpu().numpy().view(np.uint16).copy()
+            # the plain GEMM of this rank's rows, gathered on the host
+            c_r = torch.empty((m1 - m0) * Nt * 1024, dtype=torch.int16, device="cuda")
+            ttfoil.matmul_tiles(a_r, b_d, c_r, m1 - m0, Kt, Nt)
+            torch.cuda.synchronize()
+            parts = [None] * world
+            dist.all_gather_object(parts, c_r.cpu().numpy().view(np.uint16))
+            ref = np.concatenate(parts)
+            if Nt <= 8:
+                ok.append(bool(np.array_equal(full, ref)))
+            a_rm = oracle.untilize(a_all, Mt * 32, Kt * 32)
+            b_rm = oracle.untilize(b, Kt * 32, Nt * 32)
+            got = oracle.untilize(full, Mt * 32, Nt * 32)
+            rows = [0, 31, 32 * m1 - 1, 32 * Mt - 1]
+            exp = oracle.matmul(a_rm[rows], b_rm)
+            ok.append(oracle.compare(got[rows], exp)[0] == 0)
+            ok.append(ttfoil.device_error() == 0)
+            g.close()
+        q.put((rank, all(ok), ok))
+    finally:
+        dist.destroy_process_group()
+
+
+def run_two(target):
+    import torch
+    if torch.cuda.device_count() < 2:
+        pytest.skip("needs 2 GPUs")
+    import torch.multiprocessing as mp
+    ctx = mp.get_context("spawn")
+    q = ctx.Queue()
+    port = free_port()
+    procs = [ctx.Process(target=target, args=(r, 2, port, q)) for r in range(2)]
+    for p in procs:
+        p.start()
+    res = [q.get(timeout=240) for _ in range(2)]
+    for p in procs:
+        p.join(timeout=120)
+        assert p.exitcode == 0
+    return res
+
+
+def test_gemm_is_its_own_allgather_two_gpus():
+    res = run_two(gather_worker)
+    assert all(r[1] for r in res), res
 
 
 def test_row_sharded_conv_two_gpus():

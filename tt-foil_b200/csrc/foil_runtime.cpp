@@ -706,6 +706,79 @@ extern "C" int foil_matmul_tiles_dev(const uint16_t* a, const uint16_t* b, uint1
     });
 }
 
+// ---------------------------------- GEMM with its own all-gather (NVLink) ---
+extern "C" int foil_matmul_tiles_gather_dev(const uint16_t* a, const uint16_t* b, uint16_t* c,
+                                            uint16_t* const* peer_c, uint32_t npeers, uint32_t Mt,
+                                            uint32_t Kt, uint32_t Nt, const uint16_t* bias, int32_t relu,
+                                            void* stream) {
+    return guarded([&] {
+        if (npeers > foil::gemm::kMaxPeers)
+            throw FoilError(FOIL_ERR_INVALID, "foil_matmul_tiles_gather_dev: at most 7 peer copies");
+        if (npeers && !peer_c)
+            throw FoilError(FOIL_ERR_INVALID, "foil_matmul_tiles_gather_dev: null peer list");
+        for (uint32_t i = 0; i < npeers; ++i)
+            if (!peer_c[i] || !aligned16(peer_c[i]))
+                throw FoilError(FOIL_ERR_INVALID, "foil_matmul_tiles_gather_dev: null or misaligned peer buffer");
+        if (Mt == 0 || Kt == 0 || Nt == 0) return;
+        if (Mt > 65535 || Kt > 65535 || Nt > 65535)
+            throw FoilError(FOIL_ERR_INVALID, "foil_matmul_tiles_gather_dev: tile counts must be <= 65535");
+        if (!a || !b || !c || !aligned16(a) || !aligned16(b) || !aligned16(c) || (bias && !aligned16(bias)))
+            throw FoilError(FOIL_ERR_INVALID, "foil_matmul_tiles_gather_dev: null or misaligned pointer");
+        uint32_t* err = error_word_for_current_device();
+        throw_status(foil::gemm::launch(a, b, c, Mt, Kt, Nt, bias, relu, err, (cudaStream_t)stream,
+                                        sm_count_current(), peer_c, npeers));
+    });
+}
+
+// Inter-process device buffers: allocated here, exported as a 64-byte handle,
+// opened by the other processes of the node as peer-mapped pointers.
+static_assert(sizeof(cudaIpcMemHandle_t) == FOIL_PEER_HANDLE_BYTES, "IPC handle size");
+
+extern "C" int foil_peer_alloc(int32_t device, uint64_t bytes, void** ptr, uint8_t* handle) {
+    return guarded([&] {
+        if (!ptr || !handle || bytes == 0) throw FoilError(FOIL_ERR_INVALID, "foil_peer_alloc: bad arguments");
+        cuda_check(cudaSetDevice(device), "cudaSetDevice");
+        void* p = nullptr;
+        cuda_check(cudaMalloc(&p, bytes), "cudaMalloc(peer buffer)");
+        cudaIpcMemHandle_t h;
+        const cudaError_t e = cudaIpcGetMemHandle(&h, p);
+        if (e != cudaSuccess) {
+            cudaFree(p);
+            cuda_check(e, "cudaIpcGetMemHandle");
+        }
+        std::memcpy(handle, &h, sizeof h);
+        *ptr = p;
+    });
+}
+
+extern "C" int foil_peer_open(int32_t device, const uint8_t* handle, void** ptr) {
+    return guarded([&] {
+        if (!ptr || !handle) throw FoilError(FOIL_ERR_INVALID, "foil_peer_open: bad arguments");
+        cuda_check(cudaSetDevice(device), "cudaSetDevice");
+        cudaIpcMemHandle_t h;
+        std::memcpy(&h, handle, sizeof h);
+        void* p = nullptr;
+        cuda_check(cudaIpcOpenMemHandle(&p, h, cudaIpcMemLazyEnablePeerAccess), "cudaIpcOpenMemHandle");
+        *ptr = p;
+    });
+}
+
+extern "C" int foil_peer_close(int32_t device, void* ptr) {
+    return guarded([&] {
+        if (!ptr) return;
+        cuda_check(cudaSetDevice(device), "cudaSetDevice");
+        cuda_check(cudaIpcCloseMemHandle(ptr), "cudaIpcCloseMemHandle");
+    });
+}
+
+extern "C" int foil_peer_free(int32_t device, void* ptr) {
+    return guarded([&] {
+        if (!ptr) return;
+        cuda_check(cudaSetDevice(device), "cudaSetDevice");
+        cuda_check(cudaFree(ptr), "cudaFree(peer buffer)");
+    });
+}
+
 extern "C" int foil_conv2d_nhwc_dev(const uint16_t* x, const uint16_t* w, const uint16_t* bias,
                                     uint16_t* y, uint32_t N, uint32_t H, uint32_t W, uint32_t Cin,
                                     uint32_t Cout, uint32_t KH, uint32_t KW, uint32_t stride,

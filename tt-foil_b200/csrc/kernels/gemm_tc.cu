@@ -89,6 +89,11 @@ struct Params {
     uint32_t m_blocks, n_blocks;
     int relu;
     uint32_t* err;
+    // Other GPUs' copies of C (peer-mapped, same layout as c): every output
+    // tile is also stored there, so the kernel is its own all-gather.
+    uint16_t* peer_c[kMaxPeers];
+    uint32_t npeers;
+    uint32_t wide_stores;  // c and every peer_c 32-byte aligned: 256-bit stores
 };
 
 __device__ __forceinline__ void tile_coords(uint32_t tile, uint32_t m_blocks, uint32_t n_blocks,
@@ -151,13 +156,41 @@ __device__ __forceinline__ void store_tile_row(const Params& p, uint32_t t_row, 
                 o[8 + i] = pack_bf16x2(epi1(v1[2 * i], bl1, has_bias, relu),
                                        epi1(v1[2 * i + 1], bh1, has_bias, relu));
             }
-            uint16_t* tile_base = p.c + ((uint64_t)mt * p.Nt + nt) * 1024u;
-            uint4* d0 = reinterpret_cast<uint4*>(tile_base + (fr * 2u + 0u) * 256u + r0 * 16u);
-            uint4* d1 = reinterpret_cast<uint4*>(tile_base + (fr * 2u + 1u) * 256u + r0 * 16u);
-            d0[0] = make_uint4(o[0], o[1], o[2], o[3]);
-            d0[1] = make_uint4(o[4], o[5], o[6], o[7]);
-            d1[0] = make_uint4(o[8], o[9], o[10], o[11]);
-            d1[1] = make_uint4(o[12], o[13], o[14], o[15]);
+            // Row r0 of face (fr, 0) at t0 and of face (fr, 1) at t0 + 256
+            // (elements): 32 contiguous bytes each, one 256-bit store, so a
+            // half-warp writes a whole 512-byte face per instruction (full
+            // lines, also over NVLink for the peer copies).
+            // (Buffers only 16-byte aligned take two 128-bit stores per row.)
+            const uint64_t t0 = ((uint64_t)mt * p.Nt + nt) * 1024u + fr * 512u + r0 * 16u;
+            if (p.wide_stores) {
+                st_global_v8(p.c + t0, o);
+                st_global_v8(p.c + t0 + 256u, o + 8);
+#pragma unroll
+                for (uint32_t d = 0; d < kMaxPeers; ++d) {
+                    if (d < p.npeers) {
+                        st_global_v8(p.peer_c[d] + t0, o);
+                        st_global_v8(p.peer_c[d] + t0 + 256u, o + 8);
+                    }
+                }
+            } else {
+                uint4* d0 = reinterpret_cast<uint4*>(p.c + t0);
+                uint4* d1 = reinterpret_cast<uint4*>(p.c + t0 + 256u);
+                d0[0] = make_uint4(o[0], o[1], o[2], o[3]);
+                d0[1] = make_uint4(o[4], o[5], o[6], o[7]);
+                d1[0] = make_uint4(o[8], o[9], o[10], o[11]);
+                d1[1] = make_uint4(o[12], o[13], o[14], o[15]);
+#pragma unroll
+                for (uint32_t d = 0; d < kMaxPeers; ++d) {
+                    if (d < p.npeers) {
+                        uint4* e0 = reinterpret_cast<uint4*>(p.peer_c[d] + t0);
+                        uint4* e1 = reinterpret_cast<uint4*>(p.peer_c[d] + t0 + 256u);
+                        e0[0] = make_uint4(o[0], o[1], o[2], o[3]);
+                        e0[1] = make_uint4(o[4], o[5], o[6], o[7]);
+                        e1[0] = make_uint4(o[8], o[9], o[10], o[11]);
+                        e1[1] = make_uint4(o[12], o[13], o[14], o[15]);
+                    }
+                }
+            }
         }
     }
 }
@@ -333,6 +366,9 @@ gemm_tiles_kernel(const Params p) {
                 acc_phase ^= 1u;
             }
         }
+        // Peer copies of C: make this thread's remote stores visible
+        // system-wide before the kernel's completion is observed.
+        if (p.npeers) __threadfence_system();
     }
 
     tc_fence_before();
@@ -562,6 +598,9 @@ gemm_pair_kernel(const Params p) {
                 acc_phase ^= 1u;
             }
         }
+        // Peer copies of C: make this thread's remote stores visible
+        // system-wide before the kernel's completion is observed.
+        if (p.npeers) __threadfence_system();
     }
 
     tc_fence_before();
@@ -793,6 +832,7 @@ gemm_pair_wide_kernel(const Params p) {
             if (lane == 0) mbar_arrive_remote(remote_tempty);
             t_phase ^= 1u;
         }
+        if (p.npeers) __threadfence_system();
     }
 
     tc_fence_before();
@@ -808,7 +848,7 @@ gemm_pair_wide_kernel(const Params p) {
 
 int launch(const uint16_t* a, const uint16_t* b, uint16_t* c, uint32_t Mt, uint32_t Kt,
            uint32_t Nt, const uint16_t* bias, int relu, uint32_t* err, cudaStream_t stream,
-           int max_ctas) {
+           int max_ctas, uint16_t* const* peer_c, uint32_t npeers) {
     static std::once_flag attr_once;
     static cudaError_t attr_err = cudaSuccess;
     std::call_once(attr_once, [] {
@@ -834,6 +874,11 @@ int launch(const uint16_t* a, const uint16_t* b, uint16_t* c, uint32_t Mt, uint3
     p.n_blocks = (Nt + 7) / 8;
     p.relu = relu;
     p.err = err;
+    p.npeers = peer_c ? npeers : 0u;
+    for (uint32_t d = 0; d < kMaxPeers; ++d) p.peer_c[d] = d < p.npeers ? peer_c[d] : nullptr;
+    bool al32 = ((uintptr_t)c & 31u) == 0;
+    for (uint32_t d = 0; d < p.npeers; ++d) al32 = al32 && ((uintptr_t)p.peer_c[d] & 31u) == 0;
+    p.wide_stores = al32 ? 1u : 0u;
     if (Mt <= 4 || max_ctas < 2) {
         // One 128-row block: the single-SM kernel avoids an idle partner CTA.
         p.m_blocks = (Mt + 3) / 4;
@@ -845,8 +890,11 @@ int launch(const uint16_t* a, const uint16_t* b, uint16_t* c, uint32_t Mt, uint3
     p.m_blocks = (Mt + 7) / 8;  // 256-row blocks, one per CTA pair
     // More than one 256-column block: the 512-column pair kernel (a quarter
     // fewer L2 -> SM bytes per FLOP; 8192^3: 1.17 -> 1.46 PFLOP/s over 50
-    // launches, 1.07 -> 1.32 under the power cap over 400).
-    if (Nt > 8) {
+    // launches, 1.07 -> 1.32 under the power cap over 400).  With peer
+    // copies of C the 256-column kernel runs instead: its two TMEM
+    // accumulators let the epilogue's NVLink stores of one tile overlap the
+    // MMAs of the next, where the 512-column tile fills TMEM and would wait.
+    if (Nt > 8 && p.npeers == 0) {
         static std::once_flag wide_once;
         static cudaError_t wide_err = cudaSuccess;
         std::call_once(wide_once, [] {

@@ -105,6 +105,14 @@ SIGNATURES = {
     "foil_conv2d_nhwc_host": (ctypes.c_int, [ctypes.c_int32, _U16P, _U16P, _U16P, _U16P] +
                               [ctypes.c_uint32] * 9 + [ctypes.c_int32, ctypes.c_uint32]),
     "foil_host_pipeline_release": (ctypes.c_int, [ctypes.c_int32]),
+    "foil_matmul_tiles_gather_dev": (ctypes.c_int, [_U16P, _U16P, _U16P, ctypes.POINTER(_P), ctypes.c_uint32,
+                                                    ctypes.c_uint32, ctypes.c_uint32, ctypes.c_uint32, _U16P,
+                                                    ctypes.c_int32, _P]),
+    "foil_peer_alloc": (ctypes.c_int, [ctypes.c_int32, ctypes.c_uint64, ctypes.POINTER(_P),
+                                       ctypes.POINTER(ctypes.c_uint8)]),
+    "foil_peer_open": (ctypes.c_int, [ctypes.c_int32, ctypes.POINTER(ctypes.c_uint8), ctypes.POINTER(_P)]),
+    "foil_peer_close": (ctypes.c_int, [ctypes.c_int32, _P]),
+    "foil_peer_free": (ctypes.c_int, [ctypes.c_int32, _P]),
 }
 
 _lib = None
@@ -183,6 +191,46 @@ def bias_add_tiles(x, bias_tiles, out, rows, cols, stream=None):
 def matmul_tiles(a, b, c, Mt, Kt, Nt, bias=None, relu=False, stream=None):
     check(lib().foil_matmul_tiles_dev(_ptr(a), _ptr(b), _ptr(c), Mt, Kt, Nt, _ptr(bias),
                                       1 if relu else 0, _stream(stream)))
+
+
+def matmul_tiles_gather(a, b, c, peer_c, Mt, Kt, Nt, bias=None, relu=False, stream=None):
+    """matmul_tiles that also stores every output tile to the peer buffers
+    `peer_c` (device addresses as ints, other GPUs' memory opened with
+    peer_open, offset like c): C = A . B lands in c and in every peer copy."""
+    arr = (_P * max(1, len(peer_c)))(*[int(x) for x in peer_c])
+    check(lib().foil_matmul_tiles_gather_dev(_ptr(a), _ptr(b), _ptr(c), arr, len(peer_c), Mt, Kt, Nt,
+                                             _ptr(bias), 1 if relu else 0, _stream(stream)))
+
+
+PEER_HANDLE_BYTES = 64
+
+
+def peer_alloc(device, nbytes):
+    """Device buffer on CUDA device `device` shareable with the node's other
+    processes: returns (device address, 64-byte export handle)."""
+    ptr = _P()
+    h = (ctypes.c_uint8 * PEER_HANDLE_BYTES)()
+    check(lib().foil_peer_alloc(device, nbytes, ctypes.byref(ptr), h))
+    return int(ptr.value), bytes(h)
+
+
+def peer_open(device, handle):
+    """Open another process's peer_alloc buffer on CUDA device `device`;
+    returns its device address there."""
+    if len(handle) != PEER_HANDLE_BYTES:
+        raise FoilError(1, "peer_open: handle must be 64 bytes")
+    ptr = _P()
+    h = (ctypes.c_uint8 * PEER_HANDLE_BYTES).from_buffer_copy(handle)
+    check(lib().foil_peer_open(device, h, ctypes.byref(ptr)))
+    return int(ptr.value)
+
+
+def peer_close(device, ptr):
+    check(lib().foil_peer_close(device, ptr))
+
+
+def peer_free(device, ptr):
+    check(lib().foil_peer_free(device, ptr))
 
 
 def conv2d_nhwc(x, w, bias, y, N, H, W, Cin, Cout, KH, KW, stride, pad, relu=False, stream=None):

@@ -93,3 +93,82 @@ def conv2d_nhwc_h_sharded(x, w, bias, N, H_local, W, Cin, Cout, K, pad, relu=Fal
             ext[:, p + H_local:] = bot_recv
     y_ext = (conv or _device_conv)(ext, w, bias, N, H_local + 2 * p, W, Cin, Cout, K, p, relu)
     return y_ext[:, p:p + H_local].contiguous()
+
+
+class _DeviceArray:
+    """Minimal __cuda_array_interface__ exporter (int16 elements) so that a
+    raw device address can be viewed as a torch tensor."""
+
+    def __init__(self, ptr, n):
+        self.__cuda_array_interface__ = {"shape": (n,), "typestr": "<i2", "data": (ptr, False),
+                                         "version": 3, "strides": None}
+
+
+class GatheredTiles:
+    """A tile-layout matrix of Mt x Nt tiles held in full on every rank of the
+    default process group (one process per GPU of a node).
+
+    Rank r owns the tile rows split_rows(Mt, world, r) (the reference's
+    per-core row split, tests/test_matmul_2core.cpp:43-63).  `matmul` runs
+    this rank's rows as ONE kernel launch whose epilogue stores every output
+    tile both into this GPU's copy and, over NVLink, into every other rank's
+    copy (foil_matmul_tiles_gather_dev), so the GEMM is its own all-gather:
+    no separate collective moves C.  `fence` (a one-element all-reduce on the
+    current stream) orders every rank's launch before later reads; after it,
+    `tensor()` is the whole C on every rank.
+
+    The copies are plain device buffers shared through CUDA IPC handles
+    (foil_peer_alloc / foil_peer_open), exchanged once here."""
+
+    def __init__(self, Mt, Nt, device=None):
+        import torch
+        import torch.distributed as dist
+        from . import peer_alloc, peer_open
+        self.rank, self.world = dist.get_rank(), dist.get_world_size()
+        self.device = torch.cuda.current_device() if device is None else int(device)
+        self.Mt, self.Nt = Mt, Nt
+        self.nbytes = Mt * Nt * 2048
+        self.rows = split_rows(Mt, self.world, self.rank)
+        self.ptr, handle = peer_alloc(self.device, self.nbytes)
+        handles = [None] * self.world
+        dist.all_gather_object(handles, handle)
+        self.bases = [self.ptr if r == self.rank else peer_open(self.device, h) for r, h in enumerate(handles)]
+        self._one = torch.zeros(1, dtype=torch.int32, device=torch.device("cuda", self.device))
+        self._closed = False
+
+    def tensor(self):
+        """This rank's copy of C as an int16 CUDA tensor (bf16 bits, tile layout)."""
+        import torch
+        return torch.as_tensor(_DeviceArray(self.ptr, self.nbytes // 2), device=torch.device("cuda", self.device))
+
+    def matmul(self, a, b, Kt, bias=None, relu=False, stream=None):
+        """C[rows of this rank] = A_r . B: `a` holds this rank's tile rows of A
+        (tile layout, rows[1] - rows[0] tile rows x Kt), `b` all of B."""
+        from . import matmul_tiles_gather
+        m0, m1 = self.rows
+        off = m0 * self.Nt * 2048
+        peers = [self.bases[r] + off for r in range(self.world) if r != self.rank]
+        matmul_tiles_gather(a, b, self.ptr + off, peers, m1 - m0, Kt, self.Nt, bias=bias, relu=relu,
+                            stream=stream)
+
+    def fence(self):
+        """Stream-ordered completion of every rank's launches issued so far."""
+        import torch.distributed as dist
+        dist.all_reduce(self._one)
+
+    def close(self):
+        """Unmap the peers' copies and free this rank's (collective)."""
+        if self._closed:
+            return
+        import torch
+        import torch.distributed as dist
+        from . import peer_close, peer_free
+        torch.cuda.synchronize(self.device)
+        dist.barrier()
+        for r, p in enumerate(self.bases):
+            if r != self.rank:
+                peer_close(self.device, p)
+        torch.cuda.synchronize(self.device)
+        dist.barrier()
+        peer_free(self.device, self.ptr)
+        self._closed = True
