@@ -606,8 +606,9 @@ def time_fused_gather(dist, a, b, Mt, Kt, Nt, flops):
         g.close()
     return {"ms_per_step": ms, "value_TFLOPs": dist.world * flops / (ms / 1e3) / 1e12,
             "copies_consistent": consistent,
-            "note": "GEMM whose epilogue also stores each C tile to every peer GPU's copy (NVLink), "
-                    "plus a one-element all-reduce; the 256x256-tile kernel (two TMEM accumulators)"}
+            "note": "one GEMM kernel per rank that also stores each C tile to every peer GPU's copy "
+                    "over NVLink (256x512 pair tiles; four pusher warps copy finished tiles to the peers "
+                    "while later tiles compute), plus a one-element all-reduce"}
 
 
 def run_e2e(args, dist, flops):

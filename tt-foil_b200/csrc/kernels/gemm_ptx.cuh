@@ -235,6 +235,33 @@ __device__ __forceinline__ void st_global_v8(void* p, const uint32_t* w) {
                  : "memory");
 }
 
+// 256-bit global load through L2 only (no L1 allocation), 32-byte aligned.
+__device__ __forceinline__ void ld_global_cg_v8(const void* p, uint32_t* w) {
+    asm volatile("ld.global.cg.v8.b32 {%0, %1, %2, %3, %4, %5, %6, %7}, [%8];"
+                 : "=r"(w[0]), "=r"(w[1]), "=r"(w[2]), "=r"(w[3]), "=r"(w[4]), "=r"(w[5]), "=r"(w[6]),
+                   "=r"(w[7])
+                 : "l"(p)
+                 : "memory");
+}
+
+// Wait (bounded, like mbar_wait) until the shared-memory counter reaches
+// `target`.  Returns false on abort or timeout.
+__device__ __forceinline__ bool wait_count(const volatile uint32_t* counter, uint32_t target,
+                                           volatile uint32_t* abort_flag, uint32_t* err) {
+    if (*counter >= target) return true;
+    const uint64_t t0 = global_ns();
+#pragma unroll 1
+    while (*counter < target) {
+        if (*abort_flag) return false;
+        if (global_ns() - t0 > kWaitLimitNs) {
+            *abort_flag = 1u;
+            if (err) atomicOr(err, kErrWaitTimeout);
+            return false;
+        }
+    }
+    return true;
+}
+
 // Bulk (non-tensor) global -> shared copy of `bytes` (multiple of 16, both
 // addresses 16-byte aligned), completing on `bar` (no multicast).
 __device__ __forceinline__ void bulk_load(uint32_t dst, const void* src, uint32_t bytes, uint64_t* bar) {

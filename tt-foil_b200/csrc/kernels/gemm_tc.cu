@@ -120,6 +120,7 @@ __device__ __forceinline__ uint32_t epi1(uint32_t acc_bits, uint32_t bias_bits, 
 // (tile row mt) x 256 columns (tile columns nt0 .. nt0+7) -> bf16 (+bias,
 // relu) -> the tile stream.  Lane = row inside the tile: face row fr = lane/16,
 // row r0 = lane%16; each lane writes one 32-byte face row per face.
+template <bool kPeers = true>
 __device__ __forceinline__ void store_tile_row(const Params& p, uint32_t t_row, uint32_t mt,
                                                uint32_t nt0, uint32_t lane) {
     const uint32_t fr = lane >> 4, r0 = lane & 15u;
@@ -167,7 +168,7 @@ __device__ __forceinline__ void store_tile_row(const Params& p, uint32_t t_row, 
                 st_global_v8(p.c + t0 + 256u, o + 8);
 #pragma unroll
                 for (uint32_t d = 0; d < kMaxPeers; ++d) {
-                    if (d < p.npeers) {
+                    if (kPeers && d < p.npeers) {
                         st_global_v8(p.peer_c[d] + t0, o);
                         st_global_v8(p.peer_c[d] + t0 + 256u, o + 8);
                     }
@@ -181,7 +182,7 @@ __device__ __forceinline__ void store_tile_row(const Params& p, uint32_t t_row, 
                 d1[1] = make_uint4(o[12], o[13], o[14], o[15]);
 #pragma unroll
                 for (uint32_t d = 0; d < kMaxPeers; ++d) {
-                    if (d < p.npeers) {
+                    if (kPeers && d < p.npeers) {
                         uint4* e0 = reinterpret_cast<uint4*>(p.peer_c[d] + t0);
                         uint4* e1 = reinterpret_cast<uint4*>(p.peer_c[d] + t0 + 256u);
                         e0[0] = make_uint4(o[0], o[1], o[2], o[3]);
@@ -644,10 +645,15 @@ constexpr int kWStageBytes = kWABytes + kWBBytes;
 constexpr int kWFaces = 96;                        // 32 A + 64 B faces per CTA
 constexpr int kWEpiWarps = 8;
 constexpr int kWThreads = (5 + kWEpiWarps) * 32;
+// With peer copies of C, four more warps ("pushers") copy each finished tile
+// from this GPU's C (still in L2) to every peer copy while the next tile
+// computes, so the NVLink stores never hold TMEM.
+constexpr int kWPushWarps = 4;
+constexpr int kWThreadsPush = kWThreads + kWPushWarps * 32;
 constexpr int kWSmemBytes = kWStages * kWStageBytes + 1024 + 256;
 constexpr int kWBandN = 4;                         // 512-column blocks per raster band
 
-__global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kWThreads, 1)
+__global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kWThreadsPush, 1)
 gemm_pair_wide_kernel(const Params p) {
     extern __shared__ uint8_t smem_raw[];
     uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) &
@@ -659,13 +665,16 @@ gemm_pair_wide_kernel(const Params p) {
     uint64_t* drain = tempty + 1;
     uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(drain + 1);
     volatile uint32_t* abort_flag = tmem_slot + 1;
+    volatile uint32_t* epi_done = tmem_slot + 2;  // epilogue warp-tiles written to C
 
     const uint32_t warp = threadIdx.x >> 5, lane = threadIdx.x & 31u;
     const uint32_t rank = cluster_ctarank();
     const bool leader = rank == 0;
     const uint32_t pair_id = blockIdx.x >> 1, num_pairs = gridDim.x >> 1;
+    const bool pushers = blockDim.x == (uint32_t)kWThreadsPush && p.npeers > 0;
 
     if (threadIdx.x == 0) {
+        *epi_done = 0u;
         for (int s = 0; s < kWStages; ++s) {
             mbar_init(&full[s], kProdWarps * 32 + (leader ? 1 : 0));
             mbar_init(&empty[s], 1);
@@ -811,7 +820,7 @@ gemm_pair_wide_kernel(const Params p) {
             tc_commit_pair(drain);
             mbar_drain(drain, 0, 100000000ull);
         }
-    } else {
+    } else if (warp < 5u + kWEpiWarps) {
         // ---------------------------------------------------- epilogue
         // Warp e (0..7): TMEM lane quadrant warp % 4, column half e / 4.
         const uint32_t e = warp - 5u, q = warp & 3u, h = e >> 2;
@@ -825,14 +834,60 @@ gemm_pair_wide_kernel(const Params p) {
             ok = __shfl_sync(0xffffffffu, ok ? 1 : 0, 0) != 0;
             if (!ok) break;
             tc_fence_after();
-            store_tile_row(p, tmem_base + ((q * 32u) << 16) + h * 256u, (mp * 2u + rank) * 4u + q,
-                           nb * 16u + h * 8u, lane);
+            // This GPU's C only; the pusher warps copy it to the peers.
+            store_tile_row<false>(p, tmem_base + ((q * 32u) << 16) + h * 256u, (mp * 2u + rank) * 4u + q,
+                                  nb * 16u + h * 8u, lane);
             tc_fence_before();
             __syncwarp();
             if (lane == 0) mbar_arrive_remote(remote_tempty);
+            if (pushers) {
+                // Publish this warp's part of the tile (GPU-scope: the
+                // pushers read it through L2).
+                __threadfence();
+                __syncwarp();
+                if (lane == 0) atomicAdd(const_cast<uint32_t*>(epi_done), 1u);
+            }
             t_phase ^= 1u;
         }
-        if (p.npeers) __threadfence_system();
+    } else {
+        // ---------------------------------------------------- pushers
+        // Pusher j copies tile row mt0 + j of each finished tile (its 16
+        // tile columns: up to 32 KiB contiguous in the tile layout) from C
+        // to every peer copy, 4 x 32 bytes in flight per lane.
+        const uint32_t j = warp - (5u + kWEpiWarps);
+        uint32_t k = 0;
+        for (uint32_t tile = pair_id; pushers && tile < num_tiles; tile += num_pairs, ++k) {
+            bool ok = true;
+            if (lane == 0) ok = wait_count(epi_done, kWEpiWarps * (k + 1u), abort_flag, p.err);
+            ok = __shfl_sync(0xffffffffu, ok ? 1 : 0, 0) != 0;
+            if (!ok) break;
+            __syncwarp();
+            __threadfence();
+            uint32_t mp, nb;
+            tile_coords(tile, p.m_blocks, p.n_blocks, mp, nb, kWBandN);
+            const uint32_t mt = (mp * 2u + rank) * 4u + j, nt0 = nb * 16u;
+            if (mt >= p.Mt || nt0 >= p.Nt) continue;
+            const uint32_t ntn = min(16u, p.Nt - nt0);
+            const uint64_t e0 = ((uint64_t)mt * p.Nt + nt0) * 1024u;  // elements
+            const uint32_t n32 = ntn * 64u;                            // 32-byte pieces
+#pragma unroll 1
+            for (uint32_t i = lane; i < n32; i += 128u) {
+                uint32_t w[4][8];
+#pragma unroll
+                for (int u = 0; u < 4; ++u)
+                    if (i + 32u * u < n32) ld_global_cg_v8(p.c + e0 + (uint64_t)(i + 32u * u) * 16u, w[u]);
+#pragma unroll
+                for (uint32_t d = 0; d < kMaxPeers; ++d) {
+                    if (d < p.npeers) {
+#pragma unroll
+                        for (int u = 0; u < 4; ++u)
+                            if (i + 32u * u < n32)
+                                st_global_v8(p.peer_c[d] + e0 + (uint64_t)(i + 32u * u) * 16u, w[u]);
+                    }
+                }
+            }
+        }
+        if (pushers) __threadfence_system();
     }
 
     tc_fence_before();
@@ -891,10 +946,9 @@ int launch(const uint16_t* a, const uint16_t* b, uint16_t* c, uint32_t Mt, uint3
     // More than one 256-column block: the 512-column pair kernel (a quarter
     // fewer L2 -> SM bytes per FLOP; 8192^3: 1.17 -> 1.46 PFLOP/s over 50
     // launches, 1.07 -> 1.32 under the power cap over 400).  With peer
-    // copies of C the 256-column kernel runs instead: its two TMEM
-    // accumulators let the epilogue's NVLink stores of one tile overlap the
-    // MMAs of the next, where the 512-column tile fills TMEM and would wait.
-    if (Nt > 8 && p.npeers == 0) {
+    // copies of C it runs with four pusher warps more, which move finished
+    // tiles to the peers while later tiles compute.
+    if (Nt > 8) {
         static std::once_flag wide_once;
         static cudaError_t wide_err = cudaSuccess;
         std::call_once(wide_once, [] {
@@ -909,7 +963,8 @@ int launch(const uint16_t* a, const uint16_t* b, uint16_t* c, uint32_t Mt, uint3
         const uint32_t wtiles = p.m_blocks * p.n_blocks;
         const uint32_t wmax = (uint32_t)max_ctas / 2;
         const uint32_t wpairs = wtiles < wmax ? wtiles : wmax;
-        gemm_pair_wide_kernel<<<wpairs * 2, kWThreads, kWSmemBytes, stream>>>(p);
+        const int threads = p.npeers ? kWThreadsPush : kWThreads;
+        gemm_pair_wide_kernel<<<wpairs * 2, threads, kWSmemBytes, stream>>>(p);
         return check_launch("foil_matmul_tiles (2-SM, 512 columns)");
     }
     const uint32_t tiles = p.m_blocks * p.n_blocks;
