@@ -5,8 +5,10 @@ GPU on 32x32-tile-layout bf16 operands with fp32 accumulation (the tt-foil
 matmul_dram program at Mt = Kt = Nt = 256), run by the sm_100a tcgen05 kernel
 of libfoil.  With N GPUs (torchrun, one process per GPU) every rank computes
 its own 8192-row shard of an (8192 N) x 8192 x 8192 product (weak scaling, no
-collective inside the step); the NCCL all-gather that reassembles the global
-tile-layout C is timed separately and reported under "allgather".
+collective inside the step).  Reassembling the global tile-layout C is timed
+separately under "allgather": ncclAllGather after the GEMM, and ("fused") the
+GEMM kernel that stores every C tile into all ranks' copies over NVLink
+itself, followed by a one-element all-reduce.
 
 value      TFLOP/s over all ranks, operands resident in HBM, CUDA events on the
            launching stream, max over ranks.
