@@ -36,6 +36,10 @@ GOLDEN_WRAPPERS = [
     ("conv3s2_4_18_8", "test_conv_3x3_s2.cpp", 3, {"MM_MT": 4, "MM_KT": 18, "MM_NT": 8}),
     ("conv1_2_2_2", "test_conv_1x1.cpp", 4, {"MM_MT": 2, "MM_KT": 2, "MM_NT": 2}),
     ("conv1_8_4_16", "test_conv_1x1.cpp", 4, {"MM_MT": 8, "MM_KT": 4, "MM_NT": 16}),
+    # one 32-row block / one 32 x 32 tile (K = 8192) of the 8192^3 GEMM: the
+    # CPU baselines of bench.py
+    ("mnk_1_256_256", "test_matmul_mnk.cpp", 1, {"MM_MT": 1, "MM_KT": 256, "MM_NT": 256}),
+    ("mnk_1_256_1", "test_matmul_mnk.cpp", 1, {"MM_MT": 1, "MM_KT": 256, "MM_NT": 1}),
 ]
 
 

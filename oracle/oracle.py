@@ -220,3 +220,28 @@ def ref_lib():
     if _ref is None and os.path.exists(REF_LIB_PATH):
         _ref = ctypes.CDLL(REF_LIB_PATH)
     return _ref
+
+
+def ref_matmul_8192(cols):
+    """The reference's own golden matmul (tests/test_matmul_mnk.cpp:62-76)
+    compiled for one block of an 8192 x 8192 x 8192 product: 32 output rows
+    by `cols` = 8192 (a whole row block, Mt = 1, Kt = Nt = 256) or 32 (one
+    output tile, Nt = 1) columns, K = 8192.  Returns f(a, b) -> c with a
+    (32, 8192) and b (8192, cols) row-major bf16 bits, or None when
+    oracle/_ref was not built.  The call releases the GIL (ctypes), so
+    threads run blocks in parallel."""
+    tag = {8192: "mnk_1_256_256", 32: "mnk_1_256_1"}[cols]
+    L = ref_lib()
+    if L is None or not hasattr(L, "ref_matmul_" + tag):
+        return None
+    fn = getattr(L, "ref_matmul_" + tag)
+    fn.restype = None
+    fn.argtypes = [_U16, _U16, _U16]
+
+    def run(a, b):
+        a, b = _c(a), _c(b)
+        assert a.shape == (32, 8192) and b.shape == (8192, cols)
+        c = np.empty((32, cols), dtype=np.uint16)
+        fn(a, b, c)
+        return c
+    return run

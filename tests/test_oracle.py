@@ -151,3 +151,15 @@ def test_matmul_against_reference_library(tag):
     fn.argtypes = [U16, U16, U16]
     fn(np.ascontiguousarray(a.reshape(-1)), np.ascontiguousarray(b.reshape(-1)), c)
     assert np.array_equal(oracle.matmul(a, b).reshape(-1), c)
+
+
+@pytest.mark.skipif(oracle.ref_lib() is None, reason="oracle/_ref not built in this checkout")
+def test_reference_golden_8192_tile_matches_port():
+    """The reference's golden compiled for one 32 x 32 output tile of the
+    8192^3 workload (K = 8192; the CPU baseline's unit of work) agrees bit
+    for bit with the oracle port."""
+    f = oracle.ref_matmul_8192(32)
+    assert f is not None
+    a = oracle.rand_bf16((32, 8192), 13)
+    b = oracle.rand_bf16((8192, 32), 14)
+    assert np.array_equal(f(a, b), oracle.matmul(a, b))
