@@ -734,10 +734,24 @@ extern "C" int foil_matmul_tiles_gather_dev(const uint16_t* a, const uint16_t* b
 // opened by the other processes of the node as peer-mapped pointers.
 static_assert(sizeof(cudaIpcMemHandle_t) == FOIL_PEER_HANDLE_BYTES, "IPC handle size");
 
+namespace {
+// Makes `device` current for the scope and restores the caller's device.
+struct DeviceScope {
+    int prev = -1;
+    explicit DeviceScope(int32_t device) {
+        cuda_check(cudaGetDevice(&prev), "cudaGetDevice");
+        cuda_check(cudaSetDevice(device), "cudaSetDevice");
+    }
+    ~DeviceScope() {
+        if (prev >= 0) cudaSetDevice(prev);
+    }
+};
+}  // namespace
+
 extern "C" int foil_peer_alloc(int32_t device, uint64_t bytes, void** ptr, uint8_t* handle) {
     return guarded([&] {
         if (!ptr || !handle || bytes == 0) throw FoilError(FOIL_ERR_INVALID, "foil_peer_alloc: bad arguments");
-        cuda_check(cudaSetDevice(device), "cudaSetDevice");
+        DeviceScope scope(device);
         void* p = nullptr;
         cuda_check(cudaMalloc(&p, bytes), "cudaMalloc(peer buffer)");
         cudaIpcMemHandle_t h;
@@ -754,7 +768,7 @@ extern "C" int foil_peer_alloc(int32_t device, uint64_t bytes, void** ptr, uint8
 extern "C" int foil_peer_open(int32_t device, const uint8_t* handle, void** ptr) {
     return guarded([&] {
         if (!ptr || !handle) throw FoilError(FOIL_ERR_INVALID, "foil_peer_open: bad arguments");
-        cuda_check(cudaSetDevice(device), "cudaSetDevice");
+        DeviceScope scope(device);
         cudaIpcMemHandle_t h;
         std::memcpy(&h, handle, sizeof h);
         void* p = nullptr;
@@ -766,7 +780,7 @@ extern "C" int foil_peer_open(int32_t device, const uint8_t* handle, void** ptr)
 extern "C" int foil_peer_close(int32_t device, void* ptr) {
     return guarded([&] {
         if (!ptr) return;
-        cuda_check(cudaSetDevice(device), "cudaSetDevice");
+        DeviceScope scope(device);
         cuda_check(cudaIpcCloseMemHandle(ptr), "cudaIpcCloseMemHandle");
     });
 }
@@ -774,7 +788,7 @@ extern "C" int foil_peer_close(int32_t device, void* ptr) {
 extern "C" int foil_peer_free(int32_t device, void* ptr) {
     return guarded([&] {
         if (!ptr) return;
-        cuda_check(cudaSetDevice(device), "cudaSetDevice");
+        DeviceScope scope(device);
         cuda_check(cudaFree(ptr), "cudaFree(peer buffer)");
     });
 }

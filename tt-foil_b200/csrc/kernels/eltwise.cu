@@ -206,13 +206,12 @@ stream_kernel(const uint8_t* a, const uint8_t* b, uint8_t* out, uint64_t bytes,
 }
 
 int sm_count() {
-    static int sms = 0;
-    if (sms == 0) {
-        int dev = 0;
+    static const int sms = [] {
+        int dev = 0, n = 0;
         cudaGetDevice(&dev);
-        cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
-        if (sms <= 0) sms = 148;
-    }
+        cudaDeviceGetAttribute(&n, cudaDevAttrMultiProcessorCount, dev);
+        return n > 0 ? n : 148;
+    }();
     return sms;
 }
 
@@ -221,12 +220,10 @@ int launch_op(const void* a, const void* b, void* out, uint64_t bytes, const uin
               uint32_t Nt, uint32_t* err, cudaStream_t stream) {
     using C = Cfg<OP, BUFS, CHUNK, CTAS, WARPS>;
     auto kern = stream_kernel<OP, BUFS, CHUNK, CTAS, WARPS>;
-    static bool attr_set = false;  // per instantiation, per process
-    if (!attr_set) {
-        cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)C::kSmem);
-        if (e != cudaSuccess) return (int)e;
-        attr_set = true;
-    }
+    // Once per instantiation (thread-safe static initialisation).
+    static const cudaError_t attr =
+        cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)C::kSmem);
+    if (attr != cudaSuccess) return (int)attr;
     const uint64_t nchunks = (bytes + CHUNK - 1) / CHUNK;
     const uint64_t cap = (uint64_t)sm_count() * CTAS;
     const unsigned grid = (unsigned)(nchunks < cap ? nchunks : cap);
