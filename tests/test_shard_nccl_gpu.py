@@ -107,6 +107,31 @@ def gather_worker(rank, world, port, q):
             ok.append(oracle.compare(got[rows], exp)[0] == 0)
             ok.append(ttfoil.device_error() == 0)
             g.close()
+        # C copies only 16-byte aligned (base + 16 bytes): the 128-bit store
+        # path (the 256-column kernel's epilogue writes the peer itself).
+        Mt, Kt, Nt = 9, 4, 12
+        a_all = oracle.rand_bf16(Mt * Kt * 1024, 60)
+        b = oracle.rand_bf16(Kt * Nt * 1024, 61)
+        dev = lambda arr: torch.from_numpy(np.ascontiguousarray(arr).view(np.int16)).cuda()
+        g = shard.GatheredTiles(Mt + 1, Nt)          # one spare tile row of room
+        m0, m1 = shard.split_rows(Mt, world, rank)
+        a_r, b_d = dev(a_all[m0 * Kt * 1024:m1 * Kt * 1024]), dev(b)
+        torch.cuda.synchronize()
+        dist.barrier()
+        off = 16 + m0 * Nt * 2048
+        peers = [g.bases[r] + off for r in range(world) if r != rank]
+        ttfoil.matmul_tiles_gather(a_r, b_d, g.ptr + off, peers, m1 - m0, Kt, Nt)
+        g.fence()
+        torch.cuda.synchronize()
+        full = g.tensor()[8:8 + Mt * Nt * 1024].cpu().numpy().view(np.uint16).copy()
+        c_r = torch.empty((m1 - m0) * Nt * 1024, dtype=torch.int16, device="cuda")
+        ttfoil.matmul_tiles(a_r, b_d, c_r, m1 - m0, Kt, Nt)
+        torch.cuda.synchronize()
+        parts = [None] * world
+        dist.all_gather_object(parts, c_r.cpu().numpy().view(np.uint16))
+        ok.append(bool(np.array_equal(full, np.concatenate(parts))))
+        ok.append(ttfoil.device_error() == 0)
+        g.close()
         q.put((rank, all(ok), ok))
     finally:
         dist.destroy_process_group()

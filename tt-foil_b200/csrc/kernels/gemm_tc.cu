@@ -947,8 +947,10 @@ int launch(const uint16_t* a, const uint16_t* b, uint16_t* c, uint32_t Mt, uint3
     // fewer L2 -> SM bytes per FLOP; 8192^3: 1.17 -> 1.46 PFLOP/s over 50
     // launches, 1.07 -> 1.32 under the power cap over 400).  With peer
     // copies of C it runs with four pusher warps more, which move finished
-    // tiles to the peers while later tiles compute.
-    if (Nt > 8) {
+    // tiles to the peers while later tiles compute (their 256-bit copies need
+    // 32-byte aligned buffers; otherwise the 256-column kernel's epilogue
+    // stores to the peers itself).
+    if (Nt > 8 && (p.npeers == 0 || p.wide_stores)) {
         static std::once_flag wide_once;
         static cudaError_t wide_err = cudaSuccess;
         std::call_once(wide_once, [] {
