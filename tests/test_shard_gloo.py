@@ -123,3 +123,96 @@ def test_split_rows_covers_range():
             assert all(spans[i][1] == spans[i + 1][0] for i in range(world - 1))
             sizes = [e - b for b, e in spans]
             assert max(sizes) - min(sizes) <= 1
+
+
+def gathered_worker(rank, world, port, q):
+    """GatheredTiles' host logic on CPU: the peer buffers are POSIX shared
+    memory segments (a handle = the segment name), the fused GEMM a stand-in
+    that writes this rank's oracle rows into its own and every peer segment
+    at the addresses GatheredTiles computes, the fence a gloo barrier."""
+    import sys
+    from multiprocessing import shared_memory
+    import torch
+    repo = os.path.dirname(os.path.dirname(os.path.abspath(__file__)))
+    sys.path[:0] = [repo, os.path.join(repo, "tt-foil_b200")]
+    from oracle import oracle
+    import ttfoil
+    from ttfoil import shard
+
+    os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port))
+    dist.init_process_group("gloo", rank=rank, world_size=world)
+    segs = {}            # fake device address -> (segment, size)
+    calls = {"close": 0, "free": 0}
+
+    def resolve(addr):
+        for base, (seg, size) in segs.items():
+            if base <= addr < base + size:
+                return seg, addr - base
+        raise AssertionError(f"address {addr:#x} outside every buffer")
+
+    def peer_alloc(device, nbytes):
+        seg = shared_memory.SharedMemory(create=True, size=nbytes)
+        base = (rank + 1) << 40
+        segs[base] = (seg, nbytes)
+        return base, seg.name.encode().ljust(64, b"\0")
+
+    def peer_open(device, handle):
+        seg = shared_memory.SharedMemory(name=handle.rstrip(b"\0").decode())
+        base = (len(segs) + 1) << 44
+        segs[base] = (seg, seg.size)
+        return base
+
+    def matmul_tiles_gather(a, b, c, peer_c, Mt, Kt, Nt, bias=None, relu=False, stream=None):
+        rows = oracle.matmul_tiles(a, b, Mt, Kt, Nt).view(np.uint8)
+        for addr in [c] + list(peer_c):
+            seg, off = resolve(addr)
+            assert off % 2048 == 0 and off + rows.size <= seg.size
+            seg.buf[off:off + rows.size] = rows.tobytes()
+
+    def peer_close(device, ptr):
+        calls["close"] += 1
+
+    def peer_free(device, ptr):
+        calls["free"] += 1
+
+    ttfoil.peer_alloc, ttfoil.peer_open = peer_alloc, peer_open
+    ttfoil.matmul_tiles_gather, ttfoil.peer_close, ttfoil.peer_free = (matmul_tiles_gather, peer_close,
+                                                                      peer_free)
+    torch.cuda.synchronize = lambda *a, **k: None
+    ok = True
+    try:
+        Mt, Kt, Nt = 7, 3, 2
+        a = oracle.tilize(oracle.rand_bf16((Mt * 32, Kt * 32), 1))
+        b = oracle.tilize(oracle.rand_bf16((Kt * 32, Nt * 32), 2))
+        g = shard.GatheredTiles(Mt, Nt, device=0)
+        g.fence = dist.barrier
+        r0, r1 = g.rows
+        ok &= (r0, r1) == shard.split_rows(Mt, world, rank)
+        g.matmul(a[r0 * Kt * 1024:r1 * Kt * 1024], b, Kt)
+        g.fence()
+        mine = np.frombuffer(segs[g.ptr][0].buf, dtype=np.uint16, count=Mt * Nt * 1024).copy()
+        ok &= np.array_equal(mine, oracle.matmul_tiles(a, b, Mt, Kt, Nt))
+        g.close()
+        ok &= calls == {"close": world - 1, "free": 1}
+        dist.barrier()
+        for seg, _ in segs.values():
+            seg.close()
+        segs[g.ptr][0].unlink()
+        q.put((rank, bool(ok)))
+    finally:
+        dist.destroy_process_group()
+
+
+@pytest.mark.parametrize("world", [2, 3])
+def test_gathered_tiles_host_logic(world):
+    ctx = mp.get_context("spawn")
+    q = ctx.Queue()
+    port = free_port()
+    procs = [ctx.Process(target=gathered_worker, args=(r, world, port, q)) for r in range(world)]
+    for p in procs:
+        p.start()
+    res = [q.get(timeout=120) for _ in range(world)]
+    for p in procs:
+        p.join(timeout=60)
+        assert p.exitcode == 0
+    assert all(ok for _, ok in res), res

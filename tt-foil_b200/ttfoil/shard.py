@@ -133,7 +133,7 @@ class GatheredTiles:
         handles = [None] * self.world
         dist.all_gather_object(handles, handle)
         self.bases = [self.ptr if r == self.rank else peer_open(self.device, h) for r, h in enumerate(handles)]
-        self._one = torch.zeros(1, dtype=torch.int32, device=torch.device("cuda", self.device))
+        self._one = None
         self._closed = False
 
     def tensor(self):
@@ -153,7 +153,10 @@ class GatheredTiles:
 
     def fence(self):
         """Stream-ordered completion of every rank's launches issued so far."""
+        import torch
         import torch.distributed as dist
+        if self._one is None:
+            self._one = torch.zeros(1, dtype=torch.int32, device=torch.device("cuda", self.device))
         dist.all_reduce(self._one)
 
     def close(self):
