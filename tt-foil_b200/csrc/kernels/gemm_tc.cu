@@ -42,7 +42,15 @@
 //  warps 5..8  epilogue      (tcgen05.ld -> bf16 (+bias, relu) -> global)
 //  TMEM holds two 128x256 fp32 accumulators (512 columns) so the epilogue of
 //  tile i overlaps the main loop of tile i+1.  Output tiles of 128x256 are
-//  visited in bands of 8 column-blocks for L2 reuse.
+//  visited in bands of 8 column-blocks for L2 reuse.  Two 2-SM variants
+//  follow (cta_group::2, 256x256 and 256x512 pair tiles); launch() picks one
+//  by shape.
+//
+// Multi-GPU: with peer copies of C (other GPUs' buffers, Params::peer_c) the
+// kernel is also its own all-gather.  Every output tile goes to the peers over
+// NVLink as well, from the epilogue (256-column kernels, whose second TMEM
+// accumulator hides the stores) or from four pusher warps that copy finished
+// tiles out of L2 (the 512-column kernel, whose epilogue holds TMEM).
 //
 // Every mbarrier wait is bounded (2 s of wall time); on expiry the kernel
 // records kErrWaitTimeout in the error word, all roles leave their loops,
