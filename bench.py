@@ -731,7 +731,7 @@ def run_e2e(args, dist, flops):
             "h2d_bytes_per_step": a_bytes + b_bytes, "d2h_bytes_per_step": c_bytes,
             "steps": args.e2e_steps, "ms_per_step": el_p / args.e2e_steps * 1e3,
             "path": "ttfoil.matmul_tiles_host -> foil_matmul_tiles_host (pinned host A, B, C; "
-                    "B first, then 8 chunks of A / GEMM / C overlapped on 3 streams)",
+                    "B first, then ~32 chunks of A / GEMM / C overlapped on 3 streams)",
             "timer": "host perf_counter around the blocking call",
             "runtime_api": {"value": dist.world * flops * args.e2e_steps / el_b / 1e12,
                             "ms_per_step": el_b / args.e2e_steps * 1e3,

@@ -334,7 +334,7 @@ FOIL_API int foil_device_error_dev(void* stream, uint32_t* out_error);
  * B (Kt x Nt), tile streams in host memory, optional bias (Nt * 32 values,
  * one per output column, NULL for none) and relu as in
  * foil_matmul_tiles_dev, on CUDA device `device`.  B is copied first, then A
- * in chunks of `chunk_rows` tile rows (0 = about 8 chunks, at least 8 rows):
+ * in chunks of `chunk_rows` tile rows (0 = about 32 chunks, at least 8 rows):
  * the copy of chunk i + 1 and the read-back of chunk i - 1 overlap the GEMM
  * of chunk i, and host-to-device and device-to-host copies run at the same
  * time.  Blocking: returns when C is in host memory.  Replaces the

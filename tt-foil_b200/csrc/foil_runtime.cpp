@@ -945,8 +945,11 @@ extern "C" int foil_matmul_tiles_host(int32_t device, const uint16_t* a, const u
         uint16_t* dBias = bias ? static_cast<uint16_t*>(pipe_buffer(hp, 3, (size_t)Nt * 32 * 2)) : nullptr;
         uint32_t* err = error_word_for_current_device();
         const int sms = sm_count_current();
-        // Chunks of 8 tile rows (one 2-SM row block) or more, about 8 chunks.
-        uint32_t chunk = chunk_rows ? chunk_rows : std::max<uint32_t>(8u, (Mt / 8u + 7u) / 8u * 8u);
+        // Chunks of 8 tile rows (one 2-SM row block) or more, about 32 chunks:
+        // the GEMM and read-back of the last chunk are the part that does not
+        // overlap the input copies (8192^3: 5.95 ms with 8 chunks, 5.74 with
+        // 32, against 4.85 ms for the 256 MiB of input alone).
+        uint32_t chunk = chunk_rows ? chunk_rows : std::max<uint32_t>(8u, (Mt / 32u + 7u) / 8u * 8u);
         cuda_check(cudaMemcpyAsync(dB, b, (size_t)Kt * Nt * tile * 2, cudaMemcpyHostToDevice, hp.h2d), "copy B");
         if (bias) cuda_check(cudaMemcpyAsync(dBias, bias, (size_t)Nt * 64, cudaMemcpyHostToDevice, hp.h2d), "copy bias");
         size_t e = 0;
