@@ -125,11 +125,14 @@ def test_split_rows_covers_range():
             assert max(sizes) - min(sizes) <= 1
 
 
-def gathered_worker(rank, world, port, q):
+def gathered_worker(rank, world, port, q, fail_open_on=None):
     """GatheredTiles' host logic on CPU: the peer buffers are POSIX shared
     memory segments (a handle = the segment name), the fused GEMM a stand-in
     that writes this rank's oracle rows into its own and every peer segment
-    at the addresses GatheredTiles computes, the fence a gloo barrier."""
+    at the addresses GatheredTiles computes, the fence a gloo barrier.  With
+    `fail_open_on`, that rank fails to open a peer buffer: every rank must
+    then raise from the constructor (none left waiting in a collective) and
+    release what it allocated."""
     import sys
     from multiprocessing import shared_memory
     import torch
@@ -157,6 +160,8 @@ def gathered_worker(rank, world, port, q):
         return base, seg.name.encode().ljust(64, b"\0")
 
     def peer_open(device, handle):
+        if rank == fail_open_on:
+            raise ttfoil.FoilError(4, "injected: cudaIpcOpenMemHandle failed")
         seg = shared_memory.SharedMemory(name=handle.rstrip(b"\0").decode())
         base = (len(segs) + 1) << 44
         segs[base] = (seg, seg.size)
@@ -174,6 +179,9 @@ def gathered_worker(rank, world, port, q):
 
     def peer_free(device, ptr):
         calls["free"] += 1
+        seg = segs[ptr][0]
+        seg.close()
+        seg.unlink()
 
     ttfoil.peer_alloc, ttfoil.peer_open = peer_alloc, peer_open
     ttfoil.matmul_tiles_gather, ttfoil.peer_close, ttfoil.peer_free = (matmul_tiles_gather, peer_close,
@@ -181,6 +189,15 @@ def gathered_worker(rank, world, port, q):
     torch.cuda.synchronize = lambda *a, **k: None
     ok = True
     try:
+        if fail_open_on is not None:
+            try:
+                shard.GatheredTiles(7, 2, device=0)
+                ok = False
+            except RuntimeError as e:
+                ok = "injected" in str(e) and calls["free"] == 1
+            dist.barrier()
+            q.put((rank, bool(ok)))
+            return
         Mt, Kt, Nt = 7, 3, 2
         a = oracle.tilize(oracle.rand_bf16((Mt * 32, Kt * 32), 1))
         b = oracle.tilize(oracle.rand_bf16((Kt * 32, Nt * 32), 2))
@@ -195,20 +212,20 @@ def gathered_worker(rank, world, port, q):
         g.close()
         ok &= calls == {"close": world - 1, "free": 1}
         dist.barrier()
-        for seg, _ in segs.values():
-            seg.close()
-        segs[g.ptr][0].unlink()
+        for base, (seg, _) in segs.items():
+            if base != g.ptr:
+                seg.close()
         q.put((rank, bool(ok)))
     finally:
         dist.destroy_process_group()
 
 
-@pytest.mark.parametrize("world", [2, 3])
-def test_gathered_tiles_host_logic(world):
+@pytest.mark.parametrize("world,fail_open_on", [(2, None), (3, None), (3, 1)])
+def test_gathered_tiles_host_logic(world, fail_open_on):
     ctx = mp.get_context("spawn")
     q = ctx.Queue()
     port = free_port()
-    procs = [ctx.Process(target=gathered_worker, args=(r, world, port, q)) for r in range(world)]
+    procs = [ctx.Process(target=gathered_worker, args=(r, world, port, q, fail_open_on)) for r in range(world)]
     for p in procs:
         p.start()
     res = [q.get(timeout=120) for _ in range(world)]

@@ -129,10 +129,36 @@ class GatheredTiles:
         self.Mt, self.Nt = Mt, Nt
         self.nbytes = Mt * Nt * 2048
         self.rows = split_rows(Mt, self.world, self.rank)
-        self.ptr, handle = peer_alloc(self.device, self.nbytes)
+        # Every step is collective and a failure anywhere fails every rank at
+        # the same point (no rank is left waiting in a collective).
+        from . import FoilError, peer_close, peer_free
+        self.ptr, handle, why = None, None, ""
+        try:
+            self.ptr, handle = peer_alloc(self.device, self.nbytes)
+        except FoilError as e:
+            why = f"rank {self.rank}: {e}"
         handles = [None] * self.world
-        dist.all_gather_object(handles, handle)
-        self.bases = [self.ptr if r == self.rank else peer_open(self.device, h) for r, h in enumerate(handles)]
+        dist.all_gather_object(handles, (handle, why))
+        errors = [w for _, w in handles if w]
+        self.bases = []
+        if not errors:
+            for r, (h, _) in enumerate(handles):
+                try:
+                    self.bases.append(self.ptr if r == self.rank else peer_open(self.device, h))
+                except FoilError as e:
+                    why = f"rank {self.rank} opening rank {r}'s buffer: {e}"
+                    break
+            states = [None] * self.world
+            dist.all_gather_object(states, why)
+            errors = [w for w in states if w]
+        if errors:
+            for r, p in enumerate(self.bases):
+                if r != self.rank:
+                    peer_close(self.device, p)
+            dist.barrier()
+            if self.ptr is not None:
+                peer_free(self.device, self.ptr)
+            raise RuntimeError("GatheredTiles: " + "; ".join(errors))
         self._one = None
         self._closed = False
 
