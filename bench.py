@@ -39,7 +39,8 @@ secondary  the other parts of the metric, each on every rank with CUDA events
                   on bounded samples (rank 0, N=1).
 
 --impl reference times the reference's CPU golden implementation of the same
-workload (the oracle port; see the cpu_baseline note) and prints its line.
+workload on the same sample as cpu_baseline (one whole 32-row block of the
+8192^3 product per host thread, each timed step) and prints its line.
 """
 import argparse
 import json
@@ -216,8 +217,9 @@ def cpu_gemm_baseline(seconds, threads):
     """The reference's own golden matmul (tests/test_matmul_mnk.cpp:62-76,
     compiled from the reference sources into oracle/_ref) on whole 32-row
     blocks of the 8192^3 workload, one block per host thread (at most 32)
-    in parallel.  Falls back to the oracle port (same loop nest, bit-equal
-    results) for `seconds` when oracle/_ref is absent."""
+    in parallel: the same sample as one step of --impl reference.  Falls
+    back to the oracle port (same loop nest, bit-equal results) for
+    `seconds` when oracle/_ref is absent."""
     import numpy as np
     from oracle import oracle
     K = N = 8192
@@ -259,57 +261,46 @@ def gemm_config(world):
 
 # ------------------------------------------------------------- reference ---
 def run_reference(args, dist):
-    """The reference's CPU implementation of the path (its golden matmul,
-    compiled from its sources into oracle/_ref; the oracle port when that is
-    absent) on rank 0 with all host threads, each step a bounded sample of
-    the 8192^3 workload sized so that warm-up + steps take ~150 s: whole
-    32 x 8192 output row blocks when a step may take >= 25 s, else 32 x 32
-    output tiles (K = 8192) whose B panel stays in cache, which runs the
-    same loop ~10x faster per FLOP than the full-width rows (an optimistic
-    reference)."""
+    """The reference's CPU implementation of the path: its golden matmul
+    (tests/test_matmul_mnk.cpp:62-76, compiled from its sources into
+    oracle/_ref; the bit-identical oracle port when that is absent) on rank 0
+    with one thread per host core (at most 32).  Each timed step is the same
+    sample as cpu_baseline: one whole 32-row block (32 x 8192 outputs,
+    K = 8192) of the 8192^3 product per thread, in parallel.  The warm-up
+    steps are untimed single 32 x 32 output tiles: the loop needs no warm-up
+    beyond its first touch of the operands, and a whole block takes ~18 s."""
     if dist.rank != 0:
         return
     import numpy as np
     threads = host_threads()
     from oracle import oracle
     K = N = 8192
-    budget = 150.0 / max(1, args.steps + args.warmup)
-    ref_rows, ref_tile = oracle.ref_matmul_8192(N), oracle.ref_matmul_8192(32)
     t = max(1, min(threads, 32))
     a_blocks = [oracle.rand_bf16((32, K), 91 + i) for i in range(t)]
-    if ref_rows is not None and budget >= 25.0:
-        kind, cols, fn = "reference", N, ref_rows
-        b = oracle.rand_bf16((K, N), 92)
-        per_step = t
-        sample = f"{per_step} blocks of 32 output rows x 8192 cols (K=8192) per step"
-    elif ref_tile is not None:
-        kind, cols, fn = "reference", 32, ref_tile
-        b = np.ascontiguousarray(oracle.rand_bf16((K, N), 92)[:, :32])
-        t0 = time.perf_counter()
-        fn(a_blocks[0], b)
-        t_tile = time.perf_counter() - t0
-        per_step = max(1, int(0.8 * budget / max(t_tile, 1e-6) * t))
-        sample = (f"{per_step} output tiles of 32 x 32 (K=8192) per step, B panel cache-resident "
-                  f"(~10x faster per FLOP than full-width rows)")
-    else:
-        kind, cols = "port", N
-        b = oracle.rand_bf16((K, N), 92)
+    b = oracle.rand_bf16((K, N), 92)
+    fn, kind = oracle.ref_matmul_8192(N), "reference"
+    if fn is None:
+        kind = "port"
         fn = lambda a, bb: oracle.matmul(a, bb, threads=1)
-        per_step = t
-        sample = f"{per_step} blocks of 32 output rows x 8192 cols (K=8192) per step (oracle port)"
-    for _ in range(args.warmup):
-        _run_blocks(fn, a_blocks, b, per_step, t)
+    tile = oracle.ref_matmul_8192(32)
+    if tile is not None:
+        b_tile = np.ascontiguousarray(b[:, :32])
+        for _ in range(args.warmup):
+            tile(a_blocks[0], b_tile)
     el = 0.0
     for _ in range(args.steps):
-        el += _run_blocks(fn, a_blocks, b, per_step, t)
-    flops = 2.0 * 32 * cols * K * per_step * args.steps
+        el += _run_blocks(fn, a_blocks, b, t, t)
+    flops = 2.0 * 32 * N * K * t * args.steps
     v = flops / el / 1e12
+    sample = (f"{t} blocks of 32 output rows x 8192 cols (K=8192) of the 8192^3 product per step, "
+              f"one per thread; the reference's golden loop" +
+              (" compiled from its sources" if kind == "reference" else " (oracle port)"))
     line = {"impl": "reference", "metric": METRIC, "value": v, "unit": "TFLOP/s",
             "n_gpus": args.gpus, "steps": args.steps, "warmup": args.warmup,
             "ms_per_step": el / args.steps * 1e3, "higher_is_better": True, "scaling": "weak",
             "vs_baseline": None, "dtype": "bf16", "data": "synthetic seeded U(-1,1) bf16",
             "config": gemm_config(dist.world),
-            "cpu_baseline": {"value": v, "unit": "TFLOP/s", "cores": min(t, per_step), "kind": kind,
+            "cpu_baseline": {"value": v, "unit": "TFLOP/s", "cores": t, "kind": kind,
                              "sample": sample},
             "e2e": {"value": v, "unit": "TFLOP/s", "h2d_bytes_per_step": 0,
                     "d2h_bytes_per_step": 0}}

@@ -11,7 +11,12 @@ needed at run time),
                                droptests.txt), run by tests/test_dropin.py
                                on a GPU.
 
+The golden library links oracle/ref/runtime_stub.cpp for the device-API
+symbols that the included test files refer to, never the product libraries.
+
 Usage: python oracle/build.py [--reference /path/to/reference]
+The reference root comes from --reference, else from the TT_FOIL_REFERENCE
+environment variable; without either, only liboracle.so is built.
 """
 import argparse
 import os
@@ -90,8 +95,14 @@ def build_reference(ref_root):
         raise SystemExit("oracle: build tt-foil_b200 (make -C tt-foil_b200) before oracle/_ref")
     link = ["-L", libdir, "-ltt_foil", "-lfoil"]
 
-    # 1. Golden wrappers -> one shared library.
+    # 1. Golden wrappers -> one shared library, linked with the throwing
+    #    device-API stub (no product library is mapped by it).
     objs = []
+    stub = os.path.join(HERE, "ref", "runtime_stub.cpp")
+    obj = os.path.join(REF_OUT, "runtime_stub.o")
+    if newer(obj, [stub]):
+        run([CXX, "-O2", "-std=c++20", "-fPIC", "-c", stub, "-o", obj] + inc)
+    objs.append(obj)
     tu = os.path.join(HERE, "ref", "wrap_tile_utils.cpp")
     obj = os.path.join(REF_OUT, "wrap_tile_utils.o")
     if newer(obj, [tu]):
@@ -107,9 +118,8 @@ def build_reference(ref_root):
                  f"-DREF_TEST={src}", f"-DREF_TAG={tag}", f"-DREF_KIND={kind}"] + d + inc)
         objs.append(obj)
     lib = os.path.join(REF_OUT, "libref_golden.so")
-    if newer(lib, objs):
-        run([CXX, "-shared", "-o", lib] + objs + link +
-            ["-Wl,-rpath," + libdir, "-Wl,-rpath,$ORIGIN/../../tt-foil_b200/lib"])
+    if newer(lib, objs + [os.path.abspath(__file__)]):
+        run([CXX, "-shared", "-Wl,--no-undefined", "-o", lib] + objs)
 
     # 2. Drop-in test binaries.
     rpath = "-Wl,-rpath,$ORIGIN/../../../tt-foil_b200/lib"
@@ -124,10 +134,14 @@ def build_reference(ref_root):
 
 def main():
     ap = argparse.ArgumentParser()
-    ap.add_argument("--reference", default="/root/reference")
+    ap.add_argument("--reference", default=os.environ.get("TT_FOIL_REFERENCE"))
     args = ap.parse_args()
     build_oracle()
-    build_reference(args.reference)
+    if args.reference:
+        build_reference(args.reference)
+    else:
+        print("oracle: no reference tree given (--reference or TT_FOIL_REFERENCE); "
+              "skipping oracle/_ref")
 
 
 if __name__ == "__main__":

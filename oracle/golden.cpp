@@ -8,7 +8,7 @@
 //
 // Pinning: tests/test_oracle.py checks these functions against golden
 // fixtures (tests/golden/) produced by the reference's own code, compiled
-// from its sources by oracle/ref/Makefile, and — when oracle/_ref is built —
+// from its sources by the recipe oracle/build.py, and — when oracle/_ref is built —
 // against that code directly.
 //
 // Every function states the reference lines it restates.  bf16 values are

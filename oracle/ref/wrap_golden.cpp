@@ -2,11 +2,11 @@
 //
 // Exposes the reference's own golden functions, compiled from its sources
 // where they lie (the test file is included from the reference tree by the
-// recipe in oracle/ref/Makefile), through extern "C" entry points.  The
+// recipe oracle/build.py), through extern "C" entry points.  The
 // reference keeps its goldens in anonymous namespaces of test files whose
 // main() drives the device, so this translation unit includes the whole test
 // file with main renamed and adds wrappers in the same unit.  Shapes are the
-// test's compile-time MM_* values, passed by the Makefile.
+// test's compile-time MM_* values, passed by oracle/build.py.
 //
 // Built once per (test file, shape): REF_TEST names the file, REF_TAG the
 // symbol suffix, REF_KIND selects the wrapper set.

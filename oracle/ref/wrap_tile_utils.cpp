@@ -2,7 +2,7 @@
 //
 // extern "C" access to the reference's tests/tile_utils.hpp (bf16 rounding
 // and the 32x32 / 16x16-face tile permutation), compiled from the reference
-// tree by oracle/ref/Makefile.
+// tree by the recipe oracle/build.py.
 #include <cstdint>
 #include <vector>
 

@@ -163,3 +163,18 @@ def test_reference_golden_8192_tile_matches_port():
     a = oracle.rand_bf16((32, 8192), 13)
     b = oracle.rand_bf16((8192, 32), 14)
     assert np.array_equal(f(a, b), oracle.matmul(a, b))
+
+
+def test_reference_golden_library_maps_no_product_library():
+    """The reference-built golden library (the checker and the CPU baseline)
+    resolves the device API of the test files it includes against a throwing
+    stub, so loading it maps none of this repository's runtime libraries."""
+    import os
+    import subprocess
+    if not os.path.exists(oracle.REF_LIB_PATH):
+        pytest.skip("oracle/_ref not built")
+    out = subprocess.run(["readelf", "-d", oracle.REF_LIB_PATH], capture_output=True, text=True,
+                         check=True).stdout
+    needed = [l for l in out.splitlines() if "(NEEDED)" in l]
+    assert needed and not any("foil" in l for l in needed), needed
+    assert "RPATH" not in out and "RUNPATH" not in out
