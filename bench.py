@@ -679,9 +679,11 @@ def run_e2e(args, dist, flops):
     a_bytes, b_bytes, c_bytes = Mt * Kt * 2048, Kt * Nt * 2048, Mt * Nt * 2048
     pin = lambda n: torch.empty(n // 2, dtype=torch.int16, pin_memory=True)
     a_h, b_h, c_h = pin(a_bytes), pin(b_bytes), pin(c_bytes)
+    # Seeded U(-1,1) rounded to bf16, as the config states (i.i.d., so the
+    # tile order of the stream does not matter).
     g = torch.Generator().manual_seed(5 + dist.rank)
-    a_h.copy_(torch.randint(-16000, 16000, (a_bytes // 2,), dtype=torch.int16, generator=g) & 0x3fff)
-    b_h.copy_(torch.randint(-16000, 16000, (b_bytes // 2,), dtype=torch.int16, generator=g) & 0x3fff)
+    for h in (a_h, b_h):
+        h.copy_((torch.rand(h.numel(), generator=g) * 2 - 1).to(torch.bfloat16).view(torch.int16))
 
     def pipelined():
         ttfoil.matmul_tiles_host(dist.local, a_h, b_h, c_h, Mt, Kt, Nt)

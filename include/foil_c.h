@@ -319,11 +319,32 @@ FOIL_API int foil_conv2d_nhwc_dev(const uint16_t* x, const uint16_t* w, const ui
  * first, so calls that overlap on the GPU race on it.  If `status_out` is
  * non-NULL (host memory; page-locked to stay allocation-free) the call
  * synchronizes `stream` and stores the error word (0 = no bounded wait
- * expired), returning FOIL_ERR_DEVICE when it is set. */
+ * expired), returning FOIL_ERR_DEVICE when it is set.  With `status_out`
+ * NULL the call does not wait and an expired wait is not observable: the
+ * word lives only in the library's array (foil_device_error_dev reads the
+ * other entry points' word, not this one) and the next call clears it, so
+ * a kernel that gave up part-way and left C incomplete then looks like a
+ * success.  Pass `status_out` wherever that matters. */
 FOIL_API int foil_matmul_tiles_noalloc_dev(const uint16_t* a, const uint16_t* b, uint16_t* c,
                                            uint32_t Mt, uint32_t Kt, uint32_t Nt,
                                            const uint16_t* bias, int32_t relu, void* stream,
                                            uint32_t* status_out);
+
+/* Wall-time limit of every bounded device-side wait (mbarrier, flag and
+ * counter waits inside the kernels), in nanoseconds, for the launches that
+ * follow; process-wide.  A kernel whose wait runs past it records
+ * FOIL_DEVERR_WAIT_TIMEOUT in the device error word, stops its pipeline
+ * roles, waits (bounded) for its copies and tensor-core operations in
+ * flight, frees its tensor memory and returns, so the context stays usable.
+ * 0 restores the default of 2 s.  Returns the previous limit.  The B200
+ * counterpart of the reference's dispatch timeout (src/dispatch.cpp:203-208),
+ * moved into the kernels. */
+FOIL_API uint64_t foil_set_wait_limit_ns(uint64_t ns);
+
+/* Bits of the device error word. */
+#define FOIL_DEVERR_WAIT_TIMEOUT 1u /* a bounded wait gave up */
+#define FOIL_DEVERR_BAD_SHAPE 2u    /* a kernel saw a shape it cannot handle */
+#define FOIL_DEVERR_CONFIG 4u       /* launch parameters inconsistent with the kernel; nothing ran */
 
 /* Read and clear the device-side error word of the current device: 0 if no
  * kernel reported an error (bounded waits that gave up) since the last call.

@@ -43,8 +43,10 @@ def test_matmul_host_matches_device_bitwise(env, Mt, Kt, Nt, chunk):
     bias = oracle.rand_bf16((Nt * 32,), 72, -0.5, 0.5)
     exp = gemm_device(torch, tf, a, b, Mt, Kt, Nt, bias, True)
     c = torch.zeros(Mt * Nt * 1024, dtype=torch.int16, pin_memory=True)
+    before = torch.cuda.current_device()
     tf.matmul_tiles_host(0, pinned(torch, a), pinned(torch, b), c, Mt, Kt, Nt,
                          bias=pinned(torch, bias), relu=True, chunk_rows=chunk)
+    assert torch.cuda.current_device() == before
     assert np.array_equal(c.numpy().view(np.uint16), exp)
 
 
@@ -87,3 +89,55 @@ def test_host_pipeline_release_and_errors(env):
         tf.matmul_tiles_host(0, None, None, None, 1, 1, 1)
     with pytest.raises(tf.FoilError, match="device"):
         tf.matmul_tiles_host(63, 1, 1, 1, 1, 1, 1)
+
+
+def _host_gemm_and_conv_on(torch, tf, device):
+    """foil_matmul_tiles_host and foil_conv2d_nhwc_host on `device`, each
+    compared bit for bit with the device entry point run on that device."""
+    Mt, Kt, Nt = 16, 8, 12  # 2-SM 512-column kernel (> 48 KiB of shared memory)
+    a = oracle.tilize(oracle.rand_bf16((Mt * 32, Kt * 32), 170))
+    b = oracle.tilize(oracle.rand_bf16((Kt * 32, Nt * 32), 171))
+    N, H, W, Cin, Cout = 2, 20, 20, 64, 128
+    x = oracle.rand_bf16((N, H, W, Cin), 172)
+    w = oracle.randn_bf16((Cout, 3, 3, Cin), 173, np.sqrt(2.0 / 576))
+    cb = oracle.rand_bf16((Cout,), 174, -0.1, 0.1)
+    Ho = (H + 2 - 3) // 2 + 1
+    with torch.cuda.device(device):
+        dev = lambda t: torch.from_numpy(np.ascontiguousarray(t).reshape(-1).view(np.int16)).cuda()
+        c_dev = torch.zeros(Mt * Nt * 1024, dtype=torch.int16, device="cuda")
+        tf.matmul_tiles(dev(a), dev(b), c_dev, Mt, Kt, Nt)
+        y_dev = torch.zeros(N * Ho * Ho * Cout, dtype=torch.int16, device="cuda")
+        tf.conv2d_nhwc(dev(x), dev(w), dev(cb), y_dev, N, H, W, Cin, Cout, 3, 3, 2, 1, relu=True)
+        torch.cuda.synchronize()
+        assert tf.device_error() == 0
+        c_exp, y_exp = c_dev.cpu().numpy(), y_dev.cpu().numpy()
+    c = torch.zeros(Mt * Nt * 1024, dtype=torch.int16, pin_memory=True)
+    before = torch.cuda.current_device()
+    tf.matmul_tiles_host(device, pinned(torch, a), pinned(torch, b), c, Mt, Kt, Nt)
+    assert torch.cuda.current_device() == before
+    assert np.array_equal(c.numpy(), c_exp)
+    y = torch.zeros(N * Ho * Ho * Cout, dtype=torch.int16, pin_memory=True)
+    tf.conv2d_nhwc_host(device, pinned(torch, x), pinned(torch, w), pinned(torch, cb), y, N, H, W, Cin,
+                        Cout, 3, 3, 2, 1, relu=True)
+    assert torch.cuda.current_device() == before
+    assert np.array_equal(y.numpy(), y_exp)
+    return c.numpy().copy(), y.numpy().copy()
+
+
+def test_host_entry_points_on_two_devices_in_one_process(env):
+    """Kernel attributes (the dynamic shared-memory opt-in) and SM counts are
+    kept per device: device 0, then device 1, then device 0 again in one
+    process, each bitwise equal to the device-resident result, with the
+    caller's current device unchanged after every call."""
+    torch, tf = env
+    if torch.cuda.device_count() < 2:
+        pytest.skip("needs 2 GPUs")
+    r0 = _host_gemm_and_conv_on(torch, tf, 0)
+    r1 = _host_gemm_and_conv_on(torch, tf, 1)
+    r0b = _host_gemm_and_conv_on(torch, tf, 0)
+    for u, v in zip(r0, r1):
+        assert np.array_equal(u, v)
+    for u, v in zip(r0, r0b):
+        assert np.array_equal(u, v)
+    tf.host_pipeline_release(1)
+    assert torch.cuda.current_device() == 0

@@ -46,6 +46,59 @@ std::atomic<uint64_t> g_launches{0};
 extern "C" void foil_set_error(int /*status*/, const char* msg) { g_last_error = msg ? msg : ""; }
 void foil_count_launch() { g_launches.fetch_add(1, std::memory_order_relaxed); }
 
+// Per-(kernel, device) shared-memory opt-in and per-device SM count; see
+// kernels/common.cuh.
+namespace {
+struct OptinEntry {
+    const void* kernel;
+    int device;
+    int bytes;
+};
+std::mutex g_optin_mu;
+std::vector<OptinEntry> g_optin;
+int g_sm_counts[64] = {};
+}  // namespace
+
+cudaError_t foil_smem_optin(const void* kernel, int bytes) {
+    int dev = 0;
+    cudaError_t e = cudaGetDevice(&dev);
+    if (e != cudaSuccess) return e;
+    std::lock_guard<std::mutex> lk(g_optin_mu);
+    for (OptinEntry& x : g_optin)
+        if (x.kernel == kernel && x.device == dev) {
+            if (x.bytes >= bytes) return cudaSuccess;
+            e = cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, bytes);
+            if (e == cudaSuccess) x.bytes = bytes;
+            return e;
+        }
+    e = cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, bytes);
+    if (e == cudaSuccess) g_optin.push_back(OptinEntry{kernel, dev, bytes});
+    return e;
+}
+
+int foil_sm_count() {
+    int dev = 0;
+    if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= 64) return 148;
+    std::lock_guard<std::mutex> lk(g_optin_mu);
+    if (g_sm_counts[dev] <= 0) {
+        int n = 0;
+        if (cudaDeviceGetAttribute(&n, cudaDevAttrMultiProcessorCount, dev) != cudaSuccess || n <= 0) return 148;
+        g_sm_counts[dev] = n;
+    }
+    return g_sm_counts[dev];
+}
+
+namespace {
+constexpr uint64_t kDefaultWaitNs = 2000000000ull;
+std::atomic<uint64_t> g_wait_ns{kDefaultWaitNs};
+}  // namespace
+
+uint64_t foil_wait_limit_ns() { return g_wait_ns.load(std::memory_order_relaxed); }
+
+extern "C" uint64_t foil_set_wait_limit_ns(uint64_t ns) {
+    return g_wait_ns.exchange(ns ? ns : kDefaultWaitNs, std::memory_order_relaxed);
+}
+
 extern "C" const char* foil_last_error(void) { return g_last_error.c_str(); }
 extern "C" uint64_t foil_launch_count(void) { return g_launches.load(); }
 extern "C" const char* foil_version(void) { return "tt-foil-b200 1.0 (sm_100a, tcgen05)"; }
@@ -58,6 +111,18 @@ void cuda_check(cudaError_t e, const char* what) {
     if (e != cudaSuccess)
         throw FoilError(FOIL_ERR_CUDA, std::string("tt-foil: ") + what + ": " + cudaGetErrorString(e));
 }
+
+// Makes `device` current for the scope and restores the caller's device.
+struct DeviceScope {
+    int prev = -1;
+    explicit DeviceScope(int32_t device) {
+        cuda_check(cudaGetDevice(&prev), "cudaGetDevice");
+        cuda_check(cudaSetDevice(device), "cudaSetDevice");
+    }
+    ~DeviceScope() {
+        if (prev >= 0) cudaSetDevice(prev);
+    }
+};
 
 // ------------------------------------------------ driver VMM entry points ---
 struct Vmm {
@@ -114,12 +179,7 @@ uint32_t* error_word_for_current_device() {
     return g_err_words[dev];
 }
 
-int sm_count_current() {
-    int dev = 0, n = 0;
-    cudaGetDevice(&dev);
-    cudaDeviceGetAttribute(&n, cudaDevAttrMultiProcessorCount, dev);
-    return n > 0 ? n : 148;
-}
+int sm_count_current() { return foil_sm_count(); }
 
 template <class F>
 int guarded(F&& f) {
@@ -186,11 +246,12 @@ struct foil_kernel {
 
 namespace {
 
-void set_device(foil_device* d) { cuda_check(cudaSetDevice(d->ordinal), "cudaSetDevice"); }
 
 void release_device(foil_device* d) {
     if (d->closed) return;
     d->closed = true;
+    int prev = -1;
+    if (cudaGetDevice(&prev) != cudaSuccess) prev = -1;
     cudaSetDevice(d->ordinal);
     if (d->stream) cudaStreamSynchronize(d->stream);
     const Vmm& v = vmm();
@@ -214,6 +275,7 @@ void release_device(foil_device* d) {
     if (d->stream) cudaStreamDestroy(d->stream);
     d->done = nullptr;
     d->stream = nullptr;
+    if (prev >= 0) cudaSetDevice(prev);
 }
 
 // Back the DRAM arena with physical memory up to `needed` bytes.
@@ -361,7 +423,7 @@ extern "C" int foil_open_device(int idx, const char* /*firmware_dir*/, const foi
             throw FoilError(FOIL_ERR_CUDA, "tt-foil: CUDA virtual-memory entry points unavailable");
         auto d = std::make_unique<foil_device>();
         d->ordinal = idx;
-        cuda_check(cudaSetDevice(idx), "cudaSetDevice");
+        DeviceScope scope(idx);
         cuda_check(cudaFree(nullptr), "CUDA context init");
         try {
             cuda_check(cudaStreamCreateWithFlags(&d->stream, cudaStreamNonBlocking), "cudaStreamCreate");
@@ -424,7 +486,7 @@ extern "C" int foil_allocate_buffer(foil_device* d, int32_t loc, uint64_t size, 
         } else if (loc == FOIL_LOC_DRAM) {
             const uint64_t saved = d->dram_alloc.current;
             b.device_addr = d->dram_alloc.alloc(size, foil::kDramAlign, "DRAM");
-            set_device(d);
+            DeviceScope scope(d->ordinal);
             try {
                 grow_dram(d, d->dram_alloc.current);
             } catch (...) {
@@ -455,7 +517,7 @@ extern "C" int foil_write_buffer(foil_device* d, const foil_buffer* b, const voi
         char* p = buffer_ptr(d, b, bytes, "write_buffer");
         if (bytes == 0) return;
         if (!src) throw FoilError(FOIL_ERR_INVALID, "tt-foil: write_buffer from null pointer");
-        set_device(d);
+        DeviceScope scope(d->ordinal);
         cuda_check(cudaMemcpyAsync(p, src, bytes, cudaMemcpyHostToDevice, d->stream), "cudaMemcpy H2D");
         cuda_check(cudaStreamSynchronize(d->stream), "cudaStreamSynchronize");
     });
@@ -468,7 +530,7 @@ extern "C" int foil_read_buffer(foil_device* d, const foil_buffer* b, void* dst,
         char* p = buffer_ptr(d, b, bytes, "read_buffer");
         if (bytes == 0) return;
         if (!dst) throw FoilError(FOIL_ERR_INVALID, "tt-foil: read_buffer into null pointer");
-        set_device(d);
+        DeviceScope scope(d->ordinal);
         cuda_check(cudaMemcpyAsync(dst, p, bytes, cudaMemcpyDeviceToHost, d->stream), "cudaMemcpy D2H");
         cuda_check(cudaStreamSynchronize(d->stream), "cudaStreamSynchronize");
     });
@@ -608,7 +670,7 @@ extern "C" int foil_execute(foil_device* d, foil_kernel* const* kernels, size_t 
         if (!d || d->closed) throw FoilError(FOIL_ERR_INVALID, "tt-foil: invalid device");
         if (n == 0 || !kernels) throw FoilError(FOIL_ERR_INVALID, "tt-foil: dispatch_execute_multi: no kernels");
         std::lock_guard<std::mutex> lk(d->mu);
-        set_device(d);
+        DeviceScope scope(d->ordinal);
         const auto deadline = std::chrono::steady_clock::now() +
                               std::chrono::milliseconds(timeout_ms > 0 ? timeout_ms : 5000);
         // 1. Plan and resolve every operand before launching anything.
@@ -734,19 +796,6 @@ extern "C" int foil_matmul_tiles_gather_dev(const uint16_t* a, const uint16_t* b
 // opened by the other processes of the node as peer-mapped pointers.
 static_assert(sizeof(cudaIpcMemHandle_t) == FOIL_PEER_HANDLE_BYTES, "IPC handle size");
 
-namespace {
-// Makes `device` current for the scope and restores the caller's device.
-struct DeviceScope {
-    int prev = -1;
-    explicit DeviceScope(int32_t device) {
-        cuda_check(cudaGetDevice(&prev), "cudaGetDevice");
-        cuda_check(cudaSetDevice(device), "cudaSetDevice");
-    }
-    ~DeviceScope() {
-        if (prev >= 0) cudaSetDevice(prev);
-    }
-};
-}  // namespace
 
 extern "C" int foil_peer_alloc(int32_t device, uint64_t bytes, void** ptr, uint8_t* handle) {
     return guarded([&] {
@@ -878,7 +927,6 @@ HostPipe& pipe_for(int32_t device) {
     int count = 0;
     cuda_check(cudaGetDeviceCount(&count), "cudaGetDeviceCount");
     if (device >= count) throw FoilError(FOIL_ERR_INVALID, "tt-foil: no such CUDA device");
-    cuda_check(cudaSetDevice(device), "cudaSetDevice");
     return g_pipes[device];
 }
 
@@ -936,6 +984,7 @@ extern "C" int foil_matmul_tiles_host(int32_t device, const uint16_t* a, const u
             throw FoilError(FOIL_ERR_INVALID, "foil_matmul_tiles_host: tile counts must be <= 65535");
         if (!a || !b || !c) throw FoilError(FOIL_ERR_INVALID, "foil_matmul_tiles_host: null pointer");
         HostPipe& hp = pipe_for(device);
+        DeviceScope scope(device);  // the caller's current device is restored on return
         std::lock_guard<std::mutex> lk(hp.mu);
         pipe_init(hp);
         const size_t tile = 1024;  // elements per 32 x 32 tile
@@ -981,6 +1030,7 @@ extern "C" int foil_conv2d_nhwc_host(int32_t device, const uint16_t* x, const ui
         if (H == 0 || W == 0 || KH == 0 || KW == 0 || stride == 0 || H + 2 * pad < KH || W + 2 * pad < KW)
             throw FoilError(FOIL_ERR_INVALID, "foil_conv2d_nhwc_host: unsupported kernel / stride / padding");
         HostPipe& hp = pipe_for(device);
+        DeviceScope scope(device);  // the caller's current device is restored on return
         std::lock_guard<std::mutex> lk(hp.mu);
         pipe_init(hp);
         const uint64_t Ho = (H + 2 * pad - KH) / stride + 1, Wo = (W + 2 * pad - KW) / stride + 1;
@@ -1015,6 +1065,7 @@ extern "C" int foil_conv2d_nhwc_host(int32_t device, const uint16_t* x, const ui
 extern "C" int foil_host_pipeline_release(int32_t device) {
     return guarded([&] {
         HostPipe& hp = pipe_for(device);
+        DeviceScope scope(device);  // the caller's current device is restored on return
         std::lock_guard<std::mutex> lk(hp.mu);
         if (hp.h2d) {
             cuda_check(cudaStreamSynchronize(hp.d2h), "cudaStreamSynchronize");

@@ -73,3 +73,15 @@ __device__ __forceinline__ uint64_t global_ns() {
 // Host-side launch accounting shared by every entry point (defined in
 // foil_runtime.cpp).
 void foil_count_launch();
+
+// Per-device host caches (defined in foil_runtime.cpp).  A kernel's dynamic
+// shared-memory opt-in (cudaFuncSetAttribute) belongs to the current
+// device's context, so it is set once per (kernel, device ordinal), not once
+// per process; likewise the SM count is read once per device.  Both act on
+// the calling thread's current device.
+cudaError_t foil_smem_optin(const void* kernel, int bytes);
+int foil_sm_count();
+
+// Wall-time limit (ns) of each bounded device-side wait, passed to every
+// kernel launch; process-wide, set by foil_set_wait_limit_ns (default 2 s).
+uint64_t foil_wait_limit_ns();

@@ -85,6 +85,7 @@ struct Params {
     int relu;
     uint32_t box_cols;     // columns of the output tensor map's box (must equal Epi<BN>::kCols)
     uint32_t* err;
+    uint64_t wait_ns;      // wall-time limit of each bounded wait
 };
 
 template <int BN>
@@ -232,6 +233,15 @@ __device__ __forceinline__ void epilogue_rows(const Params& p, const CUtensorMap
     }
 }
 
+// Bounded wait for the copies of the last `stages` of `issued` loads (load
+// j completes phase (j / stages) & 1 of full[j % stages]); phases that have
+// completed return at once.
+__device__ __forceinline__ void drain_loads(uint64_t* full, uint32_t issued, uint32_t stages) {
+    const uint32_t j0 = issued > stages ? issued - stages : 0u;
+#pragma unroll 1
+    for (uint32_t j = j0; j < issued; ++j) mbar_drain(&full[j % stages], (j / stages) & 1u, 100000000ull);
+}
+
 template <int BN, bool kTma>
 __global__ void __launch_bounds__(kThreads, 1)
     conv_kernel(const Params p, const __grid_constant__ CUtensorMap tmap_x,
@@ -290,7 +300,7 @@ __global__ void __launch_bounds__(kThreads, 1)
             tma_prefetch_map(&tmap_x);
             tma_prefetch_map(&tmap_w);
             const uint32_t hw = p.Ho * p.Wo;
-            uint32_t stage = 0, phase = 0;
+            uint32_t stage = 0, phase = 0, issued = 0;
             bool ok = true;
             for (uint32_t tile = blockIdx.x; ok && tile < num_tiles; tile += gridDim.x) {
                 const uint32_t mb = tile / p.n_blocks, nb = tile - mb * p.n_blocks;
@@ -301,7 +311,7 @@ __global__ void __launch_bounds__(kThreads, 1)
                 const int32_t h0 = (int32_t)(ho * p.stride) - (int32_t)p.pad;
                 uint32_t kh = 0, kw = 0, cb = 0;
                 for (uint32_t kb = 0; kb < p.num_kb; ++kb) {
-                    if (!mbar_wait(&empty[stage], phase ^ 1u, abort_flag, p.err)) {
+                    if (!mbar_wait(&empty[stage], phase ^ 1u, abort_flag, p.err, p.wait_ns)) {
                         ok = false;
                         break;
                     }
@@ -312,6 +322,7 @@ __global__ void __launch_bounds__(kThreads, 1)
                     tma_load_2d(a_s + C::kABytes, &tmap_w,
                                 (int32_t)((kh * p.KW + kw) * p.Cin + cb * 64u), (int32_t)(nb * BN),
                                 &full[stage]);
+                    ++issued;
                     if (++stage == C::kStages) {
                         stage = 0;
                         phase ^= 1u;
@@ -325,6 +336,10 @@ __global__ void __launch_bounds__(kThreads, 1)
                     }
                 }
             }
+            // After an abort, copies of the last stages may still be landing
+            // in shared memory: wait (bounded) for each before the CTA ends
+            // (at once when they have all been consumed).
+            drain_loads(full, issued, (uint32_t)C::kStages);
         }
     } else if (warp < kProdWarps) {
         // ---------------------------------------------------- producers
@@ -368,7 +383,7 @@ __global__ void __launch_bounds__(kThreads, 1)
             uint32_t kh = 0, kw = 0, cb = 0;
             for (uint32_t kb = 0; kb < p.num_kb; ++kb) {
                 bool wt = true;
-                if (lane == 0) wt = mbar_wait(&empty[stage], phase ^ 1u, abort_flag, p.err);
+                if (lane == 0) wt = mbar_wait(&empty[stage], phase ^ 1u, abort_flag, p.err, p.wait_ns);
                 if (__shfl_sync(0xffffffffu, wt ? 1 : 0, 0) == 0) {
                     ok = false;
                     break;
@@ -424,11 +439,11 @@ __global__ void __launch_bounds__(kThreads, 1)
             uint32_t stage = 0, phase = 0, acc = 0, acc_phase = 0;
             bool ok = true;
             for (uint32_t tile = blockIdx.x; ok && tile < num_tiles; tile += gridDim.x) {
-                if (!mbar_wait(&tempty[acc], acc_phase ^ 1u, abort_flag, p.err)) break;
+                if (!mbar_wait(&tempty[acc], acc_phase ^ 1u, abort_flag, p.err, p.wait_ns)) break;
                 tc_fence_after();
                 const uint32_t d_tmem = tmem_base + acc * BN;
                 for (uint32_t kb = 0; kb < p.num_kb; ++kb) {
-                    if (!mbar_wait(&full[stage], phase, abort_flag, p.err)) {
+                    if (!mbar_wait(&full[stage], phase, abort_flag, p.err, p.wait_ns)) {
                         ok = false;
                         break;
                     }
@@ -470,7 +485,7 @@ __global__ void __launch_bounds__(kThreads, 1)
         for (uint32_t tile = blockIdx.x; tile < num_tiles; tile += gridDim.x) {
             const uint32_t mb = tile / p.n_blocks, nb = tile - mb * p.n_blocks;
             bool ok = true;
-            if (lane == 0) ok = mbar_wait(&tfull[acc], acc_phase, abort_flag, p.err);
+            if (lane == 0) ok = mbar_wait(&tfull[acc], acc_phase, abort_flag, p.err, p.wait_ns);
             ok = __shfl_sync(0xffffffffu, ok ? 1 : 0, 0) != 0;
             if (!ok) break;
             tc_fence_after();
@@ -609,7 +624,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
                 }
             }
             const uint32_t hw = p.Ho * p.Wo;
-            uint32_t stage = 0, phase = 0;
+            uint32_t stage = 0, phase = 0, issued = 0;
             bool ok = true;
             for (uint32_t tile = pair_id; ok && tile < num_tiles; tile += num_pairs) {
                 // Base pixel (tap (0, 0)) of this CTA's first output pixel; past
@@ -620,13 +635,14 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
                 const int32_t h0 = (int32_t)(ho * p.stride) - (int32_t)p.pad;
                 uint32_t kh = 0, kw = 0, cb = 0;
                 for (uint32_t kb = 0; kb < p.num_kb; ++kb) {
-                    if (!mbar_wait_cluster(&empty[stage], phase ^ 1u, abort_flag, p.err)) {
+                    if (!mbar_wait_cluster(&empty[stage], phase ^ 1u, abort_flag, p.err, p.wait_ns)) {
                         ok = false;
                         break;
                     }
                     if (leader) mbar_expect_tx(&full[stage], 2u * PC::kABytes);
                     tma_load_im2col_4d_pair(smem_u32(a_st + stage * PC::kABytes), &tmap_x, (int32_t)(cb * 64u), w0,
                                             h0, (int32_t)n, (uint16_t)kw, (uint16_t)kh, lead_full0 + stage * 8u);
+                    ++issued;
                     if (++stage == stages) {
                         stage = 0;
                         phase ^= 1u;
@@ -640,6 +656,15 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
                     }
                 }
             }
+            // After an abort: both CTAs' copies complete on the leader's
+            // barriers, so the leader waits (bounded) for the weights and the
+            // last stages before the pair ends (at once when they have all
+            // been consumed); the final cluster barrier keeps the other CTA
+            // alive meanwhile.
+            if (leader) {
+                mbar_drain(bfull, 0, 100000000ull);
+                drain_loads(full, issued, stages);
+            }
         }
     } else if (warp == kMmaWarp) {
         if (leader && lane == 0) {
@@ -650,13 +675,13 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
             constexpr uint64_t kmaj = smem_desc_sw128_kmajor();
             const uint32_t a0 = smem_u32(a_st), b0 = smem_u32(b_res);
             uint32_t stage = 0, phase = 0, acc = 0, acc_phase = 0;
-            bool ok = mbar_wait_cluster(bfull, 0, abort_flag, p.err);
+            bool ok = mbar_wait_cluster(bfull, 0, abort_flag, p.err, p.wait_ns);
             for (uint32_t tile = pair_id; ok && tile < num_tiles; tile += num_pairs) {
-                if (!mbar_wait_cluster(&tempty[acc], acc_phase ^ 1u, abort_flag, p.err)) break;
+                if (!mbar_wait_cluster(&tempty[acc], acc_phase ^ 1u, abort_flag, p.err, p.wait_ns)) break;
                 tc_fence_after();
                 const uint32_t d_tmem = tmem_base + acc * (uint32_t)(kSub * BN);
                 for (uint32_t kb = 0; kb < p.num_kb; ++kb) {
-                    if (!mbar_wait_cluster(&full[stage], phase, abort_flag, p.err)) {
+                    if (!mbar_wait_cluster(&full[stage], phase, abort_flag, p.err, p.wait_ns)) {
                         ok = false;
                         break;
                     }
@@ -703,7 +728,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
         uint32_t acc = 0, acc_phase = 0;
         for (uint32_t tile = pair_id; tile < num_tiles; tile += num_pairs) {
             bool ok = true;
-            if (lane == 0) ok = mbar_wait_cluster(&tfull[acc], acc_phase, abort_flag, p.err);
+            if (lane == 0) ok = mbar_wait_cluster(&tfull[acc], acc_phase, abort_flag, p.err, p.wait_ns);
             ok = __shfl_sync(0xffffffffu, ok ? 1 : 0, 0) != 0;
             if (!ok) break;
             tc_fence_after();
@@ -742,13 +767,7 @@ template <int BN, bool kTma>
 static int launch_bn(const Params& p, const CUtensorMap& mx, const CUtensorMap& mw,
                      const CUtensorMap& my, cudaStream_t stream, int max_ctas) {
     using C = Cfg<BN>;
-    static std::once_flag once;
-    static cudaError_t attr = cudaSuccess;
-    std::call_once(once, [] {
-        attr = cudaFuncSetAttribute(conv_kernel<BN, kTma>, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                    C::kSmemBytes);
-    });
-    if (attr != cudaSuccess) {
+    if (foil_smem_optin((const void*)conv_kernel<BN, kTma>, C::kSmemBytes) != cudaSuccess) {
         foil_set_error(FOIL_ERR_CUDA, "foil_conv2d_nhwc: cudaFuncSetAttribute failed");
         return FOIL_ERR_CUDA;
     }
@@ -777,13 +796,7 @@ static uint32_t pair_smem_bytes(const Params& p, int bn, uint32_t stages) {
 template <int BN>
 static int launch_pair(const Params& p, uint32_t stages, const CUtensorMap& mx, const CUtensorMap& mw,
                        const CUtensorMap& my, cudaStream_t stream, int max_ctas, int smem_optin) {
-    static std::once_flag once;
-    static cudaError_t attr = cudaSuccess;
-    std::call_once(once, [smem_optin] {
-        attr = cudaFuncSetAttribute(conv_pair_kernel<BN>, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                    smem_optin);
-    });
-    if (attr != cudaSuccess) {
+    if (foil_smem_optin((const void*)conv_pair_kernel<BN>, smem_optin) != cudaSuccess) {
         foil_set_error(FOIL_ERR_CUDA, "foil_conv2d_nhwc: cudaFuncSetAttribute failed");
         return FOIL_ERR_CUDA;
     }
@@ -921,6 +934,7 @@ int launch(const uint16_t* x, const uint16_t* w, const uint16_t* bias, uint16_t*
     p.num_kb = KH * KW * p.cblocks;
     p.relu = relu;
     p.err = err;
+    p.wait_ns = foil_wait_limit_ns();
     p.m_blocks = (p.M + 127) / 128;
     // Column tile: the smallest of 64 / 128 / 256 covering Cout, else 256.
     const int bn = Cout <= 64 ? 64 : (Cout <= 128 ? 128 : 256);

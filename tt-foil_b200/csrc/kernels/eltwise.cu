@@ -103,7 +103,7 @@ __device__ __forceinline__ uint32_t chunk_bytes(uint64_t chunk, uint64_t bytes) 
 template <int OP, int BUFS, uint32_t CHUNK, int CTAS, int WARPS>
 __global__ void __launch_bounds__(Cfg<OP, BUFS, CHUNK, CTAS, WARPS>::kThreads, CTAS)
 stream_kernel(const uint8_t* a, const uint8_t* b, uint8_t* out, uint64_t bytes,
-              const uint16_t* __restrict__ bias_tiles, uint32_t Nt, uint32_t* err) {
+              const uint16_t* __restrict__ bias_tiles, uint32_t Nt, uint32_t* err, uint64_t wait_ns) {
     using C = Cfg<OP, BUFS, CHUNK, CTAS, WARPS>;
     extern __shared__ __align__(128) uint8_t smem[];
     uint64_t* full = reinterpret_cast<uint64_t*>(smem + C::kBarOff);
@@ -145,7 +145,7 @@ stream_kernel(const uint8_t* a, const uint8_t* b, uint8_t* out, uint64_t bytes,
         for (; k < mine; ++k) {
             const int bi = (int)(k % BUFS);
             const uint32_t ph = (uint32_t)((k / BUFS) & 1u);
-            if (!mbar_wait(OP == kCopy ? &full[bi] : &done[bi], ph, abort_flag, err)) {
+            if (!mbar_wait(OP == kCopy ? &full[bi] : &done[bi], ph, abort_flag, err, wait_ns)) {
                 ok = false;
                 break;
             }
@@ -174,7 +174,7 @@ stream_kernel(const uint8_t* a, const uint8_t* b, uint8_t* out, uint64_t bytes,
     for (uint64_t k = 0; k < mine; ++k) {
         const int bi = (int)(k % BUFS);
         const uint32_t ph = (uint32_t)((k / BUFS) & 1u);
-        if (!mbar_wait(&full[bi], ph, abort_flag, err)) return;
+        if (!mbar_wait(&full[bi], ph, abort_flag, err, wait_ns)) return;
         const uint64_t chunk = first + k * step;
         const uint32_t nv = chunk_bytes<CHUNK>(chunk, bytes) / 16u;
         uint4* va = reinterpret_cast<uint4*>(smem + bi * CHUNK);
@@ -205,31 +205,20 @@ stream_kernel(const uint8_t* a, const uint8_t* b, uint8_t* out, uint64_t bytes,
     }
 }
 
-int sm_count() {
-    static const int sms = [] {
-        int dev = 0, n = 0;
-        cudaGetDevice(&dev);
-        cudaDeviceGetAttribute(&n, cudaDevAttrMultiProcessorCount, dev);
-        return n > 0 ? n : 148;
-    }();
-    return sms;
-}
-
 template <int OP, int BUFS, uint32_t CHUNK, int CTAS, int WARPS>
 int launch_op(const void* a, const void* b, void* out, uint64_t bytes, const uint16_t* bias_tiles,
               uint32_t Nt, uint32_t* err, cudaStream_t stream) {
     using C = Cfg<OP, BUFS, CHUNK, CTAS, WARPS>;
     auto kern = stream_kernel<OP, BUFS, CHUNK, CTAS, WARPS>;
-    // Once per instantiation (thread-safe static initialisation).
-    static const cudaError_t attr =
-        cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)C::kSmem);
+    const cudaError_t attr = foil_smem_optin((const void*)kern, (int)C::kSmem);
     if (attr != cudaSuccess) return (int)attr;
     const uint64_t nchunks = (bytes + CHUNK - 1) / CHUNK;
-    const uint64_t cap = (uint64_t)sm_count() * CTAS;
+    const uint64_t cap = (uint64_t)foil_sm_count() * CTAS;
     const unsigned grid = (unsigned)(nchunks < cap ? nchunks : cap);
     kern<<<grid, C::kThreads, C::kSmem, stream>>>(static_cast<const uint8_t*>(a),
                                                    static_cast<const uint8_t*>(b),
-                                                   static_cast<uint8_t*>(out), bytes, bias_tiles, Nt, err);
+                                                   static_cast<uint8_t*>(out), bytes, bias_tiles, Nt, err,
+                                                   foil_wait_limit_ns());
     return (int)cudaGetLastError();
 }
 

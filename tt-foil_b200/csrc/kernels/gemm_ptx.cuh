@@ -41,13 +41,16 @@ __device__ __forceinline__ bool mbar_try_wait(uint64_t* bar, uint32_t parity) {
     return done != 0;
 }
 
-constexpr uint64_t kWaitLimitNs = 2000000000ull;  // 2 s per wait
+// Default wall-time limit of one bounded wait (the kernels take the limit
+// as a launch parameter; foil_set_wait_limit_ns changes it).
+constexpr uint64_t kDefaultWaitLimitNs = 2000000000ull;  // 2 s per wait
 
 // Wait for completion of phase `parity`.  Returns false if the CTA is
-// aborting or this wait exceeded its wall-time limit (then it raises the
+// aborting or this wait exceeded `limit_ns` of wall time (then it raises the
 // abort flag and records the error).
 __device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity,
-                                          volatile uint32_t* abort_flag, uint32_t* err) {
+                                          volatile uint32_t* abort_flag, uint32_t* err,
+                                          uint64_t limit_ns) {
 #pragma unroll 1
     for (int i = 0; i < 32; ++i)
         if (mbar_try_wait(bar, parity)) return true;
@@ -56,7 +59,7 @@ __device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity,
     while (true) {
         if (mbar_try_wait(bar, parity)) return true;
         if (*abort_flag) return false;
-        if (global_ns() - t0 > kWaitLimitNs) {
+        if (global_ns() - t0 > limit_ns) {
             *abort_flag = 1u;
             if (err) atomicOr(err, kErrWaitTimeout);
             return false;
@@ -247,13 +250,14 @@ __device__ __forceinline__ void ld_global_cg_v8(const void* p, uint32_t* w) {
 // Wait (bounded, like mbar_wait) until the shared-memory counter reaches
 // `target`.  Returns false on abort or timeout.
 __device__ __forceinline__ bool wait_count(const volatile uint32_t* counter, uint32_t target,
-                                           volatile uint32_t* abort_flag, uint32_t* err) {
+                                           volatile uint32_t* abort_flag, uint32_t* err,
+                                           uint64_t limit_ns) {
     if (*counter >= target) return true;
     const uint64_t t0 = global_ns();
 #pragma unroll 1
     while (*counter < target) {
         if (*abort_flag) return false;
-        if (global_ns() - t0 > kWaitLimitNs) {
+        if (global_ns() - t0 > limit_ns) {
             *abort_flag = 1u;
             if (err) atomicOr(err, kErrWaitTimeout);
             return false;
@@ -341,7 +345,8 @@ __device__ __forceinline__ bool mbar_try_wait_cluster(uint64_t* bar, uint32_t pa
 // Bounded wait (acquire at cluster scope) for barriers that receive arrivals
 // from the other CTA of the pair.
 __device__ __forceinline__ bool mbar_wait_cluster(uint64_t* bar, uint32_t parity,
-                                                  volatile uint32_t* abort_flag, uint32_t* err) {
+                                                  volatile uint32_t* abort_flag, uint32_t* err,
+                                                  uint64_t limit_ns) {
 #pragma unroll 1
     for (int i = 0; i < 32; ++i)
         if (mbar_try_wait_cluster(bar, parity)) return true;
@@ -350,7 +355,7 @@ __device__ __forceinline__ bool mbar_wait_cluster(uint64_t* bar, uint32_t parity
     while (true) {
         if (mbar_try_wait_cluster(bar, parity)) return true;
         if (*abort_flag) return false;
-        if (global_ns() - t0 > kWaitLimitNs) {
+        if (global_ns() - t0 > limit_ns) {
             *abort_flag = 1u;
             if (err) atomicOr(err, kErrWaitTimeout);
             return false;

@@ -102,6 +102,7 @@ struct Params {
     uint16_t* peer_c[kMaxPeers];
     uint32_t npeers;
     uint32_t wide_stores;  // c and every peer_c 32-byte aligned: 256-bit stores
+    uint64_t wait_ns;      // wall-time limit of each bounded wait
 };
 
 __device__ __forceinline__ void tile_coords(uint32_t tile, uint32_t m_blocks, uint32_t n_blocks,
@@ -263,7 +264,7 @@ gemm_tiles_kernel(const Params p) {
             bool ok = true;
             for (uint32_t kb = 0; kb < num_kb; ++kb) {
                 bool w = true;
-                if (lane == 0) w = mbar_wait(&empty[stage], phase ^ 1u, abort_flag, p.err);
+                if (lane == 0) w = mbar_wait(&empty[stage], phase ^ 1u, abort_flag, p.err, p.wait_ns);
                 if (__shfl_sync(0xffffffffu, w ? 1 : 0, 0) == 0) {
                     ok = false;
                     break;
@@ -313,11 +314,11 @@ gemm_tiles_kernel(const Params p) {
             uint32_t stage = 0, phase = 0, acc = 0, acc_phase = 0;
             bool ok = true;
             for (uint32_t tile = blockIdx.x; ok && tile < num_tiles; tile += gridDim.x) {
-                if (!mbar_wait(&tempty[acc], acc_phase ^ 1u, abort_flag, p.err)) break;
+                if (!mbar_wait(&tempty[acc], acc_phase ^ 1u, abort_flag, p.err, p.wait_ns)) break;
                 tc_fence_after();
                 const uint32_t d_tmem = tmem_base + acc * kBN;
                 for (uint32_t kb = 0; kb < num_kb; ++kb) {
-                    if (!mbar_wait(&full[stage], phase, abort_flag, p.err)) {
+                    if (!mbar_wait(&full[stage], phase, abort_flag, p.err, p.wait_ns)) {
                         ok = false;
                         break;
                     }
@@ -362,7 +363,7 @@ gemm_tiles_kernel(const Params p) {
             // One lane waits; the warp then proceeds converged (tcgen05.ld is
             // a warp-wide .sync.aligned instruction).
             bool ok = true;
-            if (lane == 0) ok = mbar_wait(&tfull[acc], acc_phase, abort_flag, p.err);
+            if (lane == 0) ok = mbar_wait(&tfull[acc], acc_phase, abort_flag, p.err, p.wait_ns);
             ok = __shfl_sync(0xffffffffu, ok ? 1 : 0, 0) != 0;
             if (!ok) break;
             tc_fence_after();
@@ -477,7 +478,7 @@ gemm_pair_kernel(const Params p) {
             bool ok = true;
             for (uint32_t kb = 0; kb < num_kb; ++kb) {
                 bool w = true;
-                if (lane == 0) w = mbar_wait_cluster(&empty[stage], phase ^ 1u, abort_flag, p.err);
+                if (lane == 0) w = mbar_wait_cluster(&empty[stage], phase ^ 1u, abort_flag, p.err, p.wait_ns);
                 if (__shfl_sync(0xffffffffu, w ? 1 : 0, 0) == 0) {
                     ok = false;
                     break;
@@ -526,7 +527,7 @@ gemm_pair_kernel(const Params p) {
             bool ok = true;
             for (uint32_t tile = pair_id; ok && tile < num_tiles; tile += num_pairs) {
                 for (uint32_t kb = 0; kb < num_kb; ++kb) {
-                    if (!mbar_wait(&full[stage], phase, abort_flag, p.err)) {
+                    if (!mbar_wait(&full[stage], phase, abort_flag, p.err, p.wait_ns)) {
                         ok = false;
                         break;
                     }
@@ -548,11 +549,11 @@ gemm_pair_kernel(const Params p) {
             uint32_t stage = 0, phase = 0, acc = 0, acc_phase = 0;
             bool ok = true;
             for (uint32_t tile = pair_id; ok && tile < num_tiles; tile += num_pairs) {
-                if (!mbar_wait_cluster(&tempty[acc], acc_phase ^ 1u, abort_flag, p.err)) break;
+                if (!mbar_wait_cluster(&tempty[acc], acc_phase ^ 1u, abort_flag, p.err, p.wait_ns)) break;
                 tc_fence_after();
                 const uint32_t d_tmem = tmem_base + acc * kBN;
                 for (uint32_t kb = 0; kb < num_kb; ++kb) {
-                    if (!mbar_wait_cluster(&full[stage], phase, abort_flag, p.err)) {
+                    if (!mbar_wait_cluster(&full[stage], phase, abort_flag, p.err, p.wait_ns)) {
                         ok = false;
                         break;
                     }
@@ -593,7 +594,7 @@ gemm_pair_kernel(const Params p) {
             uint32_t mp, nb;
             tile_coords(tile, p.m_blocks, p.n_blocks, mp, nb);
             bool ok = true;
-            if (lane == 0) ok = mbar_wait_cluster(&tfull[acc], acc_phase, abort_flag, p.err);
+            if (lane == 0) ok = mbar_wait_cluster(&tfull[acc], acc_phase, abort_flag, p.err, p.wait_ns);
             ok = __shfl_sync(0xffffffffu, ok ? 1 : 0, 0) != 0;
             if (!ok) break;
             tc_fence_after();
@@ -724,7 +725,7 @@ gemm_pair_wide_kernel(const Params p) {
             bool ok = true;
             for (uint32_t kb = 0; kb < num_kb; ++kb) {
                 bool w = true;
-                if (lane == 0) w = mbar_wait_cluster(&empty[stage], phase ^ 1u, abort_flag, p.err);
+                if (lane == 0) w = mbar_wait_cluster(&empty[stage], phase ^ 1u, abort_flag, p.err, p.wait_ns);
                 if (__shfl_sync(0xffffffffu, w ? 1 : 0, 0) == 0) {
                     ok = false;
                     break;
@@ -773,7 +774,7 @@ gemm_pair_wide_kernel(const Params p) {
             bool ok = true;
             for (uint32_t tile = pair_id; ok && tile < num_tiles; tile += num_pairs) {
                 for (uint32_t kb = 0; kb < num_kb; ++kb) {
-                    if (!mbar_wait(&full[stage], phase, abort_flag, p.err)) {
+                    if (!mbar_wait(&full[stage], phase, abort_flag, p.err, p.wait_ns)) {
                         ok = false;
                         break;
                     }
@@ -793,10 +794,10 @@ gemm_pair_wide_kernel(const Params p) {
             uint32_t stage = 0, phase = 0, t_phase = 0;
             bool ok = true;
             for (uint32_t tile = pair_id; ok && tile < num_tiles; tile += num_pairs) {
-                if (!mbar_wait_cluster(tempty, t_phase ^ 1u, abort_flag, p.err)) break;
+                if (!mbar_wait_cluster(tempty, t_phase ^ 1u, abort_flag, p.err, p.wait_ns)) break;
                 tc_fence_after();
                 for (uint32_t kb = 0; kb < num_kb; ++kb) {
-                    if (!mbar_wait_cluster(&full[stage], phase, abort_flag, p.err)) {
+                    if (!mbar_wait_cluster(&full[stage], phase, abort_flag, p.err, p.wait_ns)) {
                         ok = false;
                         break;
                     }
@@ -838,7 +839,7 @@ gemm_pair_wide_kernel(const Params p) {
             uint32_t mp, nb;
             tile_coords(tile, p.m_blocks, p.n_blocks, mp, nb, kWBandN);
             bool ok = true;
-            if (lane == 0) ok = mbar_wait_cluster(tfull, t_phase, abort_flag, p.err);
+            if (lane == 0) ok = mbar_wait_cluster(tfull, t_phase, abort_flag, p.err, p.wait_ns);
             ok = __shfl_sync(0xffffffffu, ok ? 1 : 0, 0) != 0;
             if (!ok) break;
             tc_fence_after();
@@ -866,7 +867,7 @@ gemm_pair_wide_kernel(const Params p) {
         uint32_t k = 0;
         for (uint32_t tile = pair_id; pushers && tile < num_tiles; tile += num_pairs, ++k) {
             bool ok = true;
-            if (lane == 0) ok = wait_count(epi_done, kWEpiWarps * (k + 1u), abort_flag, p.err);
+            if (lane == 0) ok = wait_count(epi_done, kWEpiWarps * (k + 1u), abort_flag, p.err, p.wait_ns);
             ok = __shfl_sync(0xffffffffu, ok ? 1 : 0, 0) != 0;
             if (!ok) break;
             __syncwarp();
@@ -912,16 +913,8 @@ gemm_pair_wide_kernel(const Params p) {
 int launch(const uint16_t* a, const uint16_t* b, uint16_t* c, uint32_t Mt, uint32_t Kt,
            uint32_t Nt, const uint16_t* bias, int relu, uint32_t* err, cudaStream_t stream,
            int max_ctas, uint16_t* const* peer_c, uint32_t npeers) {
-    static std::once_flag attr_once;
-    static cudaError_t attr_err = cudaSuccess;
-    std::call_once(attr_once, [] {
-        attr_err = cudaFuncSetAttribute(gemm_tiles_kernel,
-                                        cudaFuncAttributeMaxDynamicSharedMemorySize, kSmemBytes);
-        if (attr_err == cudaSuccess)
-            attr_err = cudaFuncSetAttribute(gemm_pair_kernel,
-                                            cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                            kPSmemBytes);
-    });
+    cudaError_t attr_err = foil_smem_optin((const void*)gemm_tiles_kernel, kSmemBytes);
+    if (attr_err == cudaSuccess) attr_err = foil_smem_optin((const void*)gemm_pair_kernel, kPSmemBytes);
     if (attr_err != cudaSuccess) {
         foil_set_error(FOIL_ERR_CUDA, "foil_matmul_tiles: cudaFuncSetAttribute failed");
         return FOIL_ERR_CUDA;
@@ -937,6 +930,7 @@ int launch(const uint16_t* a, const uint16_t* b, uint16_t* c, uint32_t Mt, uint3
     p.n_blocks = (Nt + 7) / 8;
     p.relu = relu;
     p.err = err;
+    p.wait_ns = foil_wait_limit_ns();
     p.npeers = peer_c ? npeers : 0u;
     for (uint32_t d = 0; d < kMaxPeers; ++d) p.peer_c[d] = d < p.npeers ? peer_c[d] : nullptr;
     bool al32 = ((uintptr_t)c & 31u) == 0;
@@ -959,13 +953,7 @@ int launch(const uint16_t* a, const uint16_t* b, uint16_t* c, uint32_t Mt, uint3
     // 32-byte aligned buffers; otherwise the 256-column kernel's epilogue
     // stores to the peers itself).
     if (Nt > 8 && (p.npeers == 0 || p.wide_stores)) {
-        static std::once_flag wide_once;
-        static cudaError_t wide_err = cudaSuccess;
-        std::call_once(wide_once, [] {
-            wide_err = cudaFuncSetAttribute(gemm_pair_wide_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                            kWSmemBytes);
-        });
-        if (wide_err != cudaSuccess) {
+        if (foil_smem_optin((const void*)gemm_pair_wide_kernel, kWSmemBytes) != cudaSuccess) {
             foil_set_error(FOIL_ERR_CUDA, "foil_matmul_tiles: cudaFuncSetAttribute failed");
             return FOIL_ERR_CUDA;
         }

@@ -94,17 +94,6 @@ untilize_kernel(const uint4* __restrict__ in, uint4* __restrict__ out,
     }
 }
 
-int sm_count() {
-    static int n = 0;
-    if (n == 0) {
-        int dev = 0;
-        cudaGetDevice(&dev);
-        cudaDeviceGetAttribute(&n, cudaDevAttrMultiProcessorCount, dev);
-        if (n <= 0) n = 148;
-    }
-    return n;
-}
-
 }  // namespace
 }  // namespace foil
 
@@ -136,7 +125,7 @@ extern "C" int foil_tilize_dev(const uint16_t* row_major, uint16_t* tiles,
         return FOIL_ERR_INVALID;
     }
     uint64_t bands = (uint64_t)(rows / 32) * ((cols / 32 + 7) / 8);
-    uint64_t grid = bands < (uint64_t)foil::sm_count() * 8 ? bands : (uint64_t)foil::sm_count() * 8;
+    uint64_t grid = bands < (uint64_t)foil_sm_count() * 8 ? bands : (uint64_t)foil_sm_count() * 8;
     foil::tilize_kernel<<<(unsigned)grid, foil::kLayoutThreads, 0, (cudaStream_t)stream>>>(
         (const uint4*)row_major, (uint4*)tiles, rows, cols);
     return check_launch("foil_tilize_dev");
@@ -154,7 +143,7 @@ extern "C" int foil_untilize_dev(const uint16_t* tiles, uint16_t* row_major,
         return FOIL_ERR_INVALID;
     }
     uint64_t bands = (uint64_t)(rows / 32) * ((cols / 32 + 7) / 8);
-    uint64_t grid = bands < (uint64_t)foil::sm_count() * 8 ? bands : (uint64_t)foil::sm_count() * 8;
+    uint64_t grid = bands < (uint64_t)foil_sm_count() * 8 ? bands : (uint64_t)foil_sm_count() * 8;
     foil::untilize_kernel<<<(unsigned)grid, foil::kLayoutThreads, 0, (cudaStream_t)stream>>>(
         (const uint4*)tiles, (uint4*)row_major, rows, cols);
     return check_launch("foil_untilize_dev");

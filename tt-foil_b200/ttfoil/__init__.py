@@ -113,7 +113,11 @@ SIGNATURES = {
     "foil_peer_open": (ctypes.c_int, [ctypes.c_int32, ctypes.POINTER(ctypes.c_uint8), ctypes.POINTER(_P)]),
     "foil_peer_close": (ctypes.c_int, [ctypes.c_int32, _P]),
     "foil_peer_free": (ctypes.c_int, [ctypes.c_int32, _P]),
+    "foil_set_wait_limit_ns": (ctypes.c_uint64, [ctypes.c_uint64]),
 }
+
+# Bits of the device error word (include/foil_c.h FOIL_DEVERR_*).
+DEVERR_WAIT_TIMEOUT, DEVERR_BAD_SHAPE, DEVERR_CONFIG = 1, 2, 4
 
 _lib = None
 
@@ -141,6 +145,12 @@ def check(rc):
 
 def launch_count():
     return int(lib().foil_launch_count())
+
+
+def set_wait_limit_ns(ns):
+    """Wall-time limit of every bounded device-side wait for the launches
+    that follow (0 = the default 2 s); returns the previous limit."""
+    return int(lib().foil_set_wait_limit_ns(int(ns)))
 
 
 # ------------------------------------------------------------ device layer ---
