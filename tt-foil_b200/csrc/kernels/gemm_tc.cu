@@ -847,15 +847,18 @@ gemm_pair_wide_kernel(const Params p) {
             store_tile_row<false>(p, tmem_base + ((q * 32u) << 16) + h * 256u, (mp * 2u + rank) * 4u + q,
                                   nb * 16u + h * 8u, lane);
             tc_fence_before();
-            __syncwarp();
-            if (lane == 0) mbar_arrive_remote(remote_tempty);
             if (pushers) {
                 // Publish this warp's part of the tile (GPU-scope: the
-                // pushers read it through L2).
+                // pushers read it through L2) BEFORE releasing the
+                // accumulator: the next tile's parts can then only be
+                // counted after every part of this tile, so the count
+                // 8 (k + 1) the pushers wait for means all of tile k.
                 __threadfence();
                 __syncwarp();
                 if (lane == 0) atomicAdd(const_cast<uint32_t*>(epi_done), 1u);
             }
+            __syncwarp();
+            if (lane == 0) mbar_arrive_remote(remote_tempty);
             t_phase ^= 1u;
         }
     } else {

@@ -114,8 +114,17 @@ class GatheredTiles:
     tile both into this GPU's copy and, over NVLink, into every other rank's
     copy (foil_matmul_tiles_gather_dev), so the GEMM is its own all-gather:
     no separate collective moves C.  `fence` (a one-element all-reduce on the
-    current stream) orders every rank's launch before later reads; after it,
+    launch stream) orders every rank's launch before later reads; after it,
     `tensor()` is the whole C on every rank.
+
+    Ordering rules.  Rank A's matmul writes into rank B's copy over NVLink,
+    so two orderings are needed: (1) fence after a matmul before any rank
+    reads C; (2) fence after the last read of a result and before the next
+    matmul that overwrites it (otherwise rank A's next launch may store into
+    B's copy while B still reads the previous C).  A loop of matmul, fence,
+    matmul, fence with no reads in between needs nothing more.  Pass fence
+    the stream the matmul was issued on (and the one the reads run on)
+    when that is not torch's current stream.
 
     The copies are plain device buffers shared through CUDA IPC handles
     (foil_peer_alloc / foil_peer_open), exchanged once here."""
@@ -177,13 +186,19 @@ class GatheredTiles:
         matmul_tiles_gather(a, b, self.ptr + off, peers, m1 - m0, Kt, self.Nt, bias=bias, relu=relu,
                             stream=stream)
 
-    def fence(self):
-        """Stream-ordered completion of every rank's launches issued so far."""
+    def fence(self, stream=None):
+        """Stream-ordered completion of every rank's work issued so far on
+        `stream` (torch's current stream when None): a one-element
+        all-reduce that work on `stream` after it waits for, on every rank.
+        Needed after a matmul before C is read, and after the last read of
+        C before the next matmul (see the class docstring)."""
         import torch
         import torch.distributed as dist
         if self._one is None:
             self._one = torch.zeros(1, dtype=torch.int32, device=torch.device("cuda", self.device))
-        dist.all_reduce(self._one)
+        s = torch.cuda.current_stream(self.device) if stream is None else stream
+        with torch.cuda.stream(s):
+            dist.all_reduce(self._one)
 
     def close(self):
         """Unmap the peers' copies and free this rank's (collective)."""
