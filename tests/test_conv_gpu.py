@@ -138,6 +138,7 @@ VARIANTS = {
     "gather": {"FOIL_CONV_PRODUCER": "gather"},
     "single": {"FOIL_CONV_PRODUCER": "single"},
     "pair": {"FOIL_CONV_PRODUCER": "pair"},
+    "plane": {"FOIL_CONV_PRODUCER": "plane"},
 }
 
 VARIANT_CASES = [  # x shape, w shape, stride, pad
@@ -149,53 +150,119 @@ VARIANT_CASES = [  # x shape, w shape, stride, pad
     ((4, 16, 16, 64), (64, 5, 5, 64), 1, 2),       # 5x5
 ]
 
+# Shapes the plane kernel serves (Cin a multiple of 64, Ho Wo a multiple of
+# 32, Wo a multiple of 8, Cout <= 256, <= 25 taps): short and odd window
+# counts, a window pair split over two images, Cout tails, strides 2 and 3,
+# 1x1, 5x5, three channel blocks, and the two batch-32 configurations at
+# batch 2.
+PLANE_CASES = [  # x shape, w shape, stride, pad
+    ((1, 8, 8, 64), (64, 3, 3, 64), 1, 1),         # one short window; the pair's odd CTA idle
+    ((3, 16, 16, 64), (96, 3, 3, 64), 1, 1),       # 6 windows, Cout tail in BN = 128
+    ((2, 32, 32, 64), (128, 3, 3, 64), 2, 1),      # stride 2: 6 planes
+    ((1, 48, 48, 64), (64, 3, 3, 64), 3, 1),       # stride 3: 9 planes
+    ((2, 64, 32, 64), (128, 3, 3, 64), 2, 1),      # Ho != Wo
+    ((1, 24, 40, 128), (64, 3, 3, 128), 1, 1),     # two channel blocks, 2 slots
+    ((1, 12, 16, 192), (48, 1, 1, 192), 1, 0),     # 1x1, three channel blocks, Cout 48
+    ((2, 56, 56, 128), (256, 1, 1, 128), 1, 0),    # config-3 1x1 shape
+    ((2, 112, 112, 64), (128, 3, 3, 64), 2, 1),    # config-3 3x3 stride-2 shape
+    ((4, 16, 16, 64), (64, 5, 5, 64), 1, 2),       # 25 taps
+]
+
+RUN_CASES = (
+    "import sys, numpy as np, torch\n"
+    f"sys.path.insert(0, {PKG!r})\n"
+    "import ttfoil\n"
+    "for inp, outp in zip(sys.argv[1::2], sys.argv[2::2]):\n"
+    "    d = np.load(inp)\n"
+    "    x, w, b = (torch.from_numpy(d[k].view(np.int16)).cuda() for k in ('x', 'w', 'b'))\n"
+    "    N, H, W, Cin = d['x'].shape; Cout, KH, KW, _ = d['w'].shape; s, p = int(d['s']), int(d['p'])\n"
+    "    Ho, Wo = (H + 2 * p - KH) // s + 1, (W + 2 * p - KW) // s + 1\n"
+    "    y = torch.zeros(N * Ho * Wo * Cout, dtype=torch.int16, device='cuda')\n"
+    "    try:\n"
+    "        ttfoil.conv2d_nhwc(x, w, b, y, N, H, W, Cin, Cout, KH, KW, s, p, relu=True)\n"
+    "    except ttfoil.FoilError as e:\n"
+    "        assert e.status == 6, e  # FOIL_ERR_UNSUPPORTED: this variant does not serve the shape\n"
+    "        continue\n"
+    "    torch.cuda.synchronize(); assert ttfoil.device_error() == 0\n"
+    "    np.save(outp, y.cpu().numpy())\n")
+
+
+def make_case(d, i, xs, ws, stride, pad, seed):
+    x = oracle.rand_bf16(xs, seed)
+    w = oracle.randn_bf16(ws, seed + 10, np.sqrt(2.0 / (ws[1] * ws[2] * ws[3])))
+    b = oracle.rand_bf16((ws[0],), seed + 20, -0.1, 0.1)
+    inp = d / f"in{i}.npz"
+    np.savez(inp, x=x, w=w, b=b, s=stride, p=pad)
+    return inp, x, w, b
+
+
+def run_variant(script, variant, inputs, out_dir):
+    """Run every case of `inputs` in one subprocess with the variant forced;
+    returns the output path of each case (missing when not served)."""
+    outs = [out_dir / f"{variant}_{i}.npy" for i in range(len(inputs))]
+    args = [a for pair in zip(map(str, inputs), map(str, outs)) for a in pair]
+    r = subprocess.run([sys.executable, str(script)] + args, env=dict(os.environ, **VARIANTS[variant]),
+                       capture_output=True, text=True, timeout=600)
+    assert r.returncode == 0, r.stderr[-2000:]
+    return outs
+
 
 @pytest.fixture(scope="module")
 def variant_inputs(env, tmp_path_factory):
     """Seeded inputs of VARIANT_CASES, their default-path outputs (checked
-    against the oracle) and the script that reruns a case in a subprocess."""
+    against the oracle) and the script that reruns cases in a subprocess."""
     d = tmp_path_factory.mktemp("variants")
-    script = d / "run_case.py"
-    script.write_text(
-        "import sys, numpy as np, torch\n"
-        f"sys.path.insert(0, {PKG!r})\n"
-        "import ttfoil\n"
-        "d = np.load(sys.argv[1])\n"
-        "x, w, b = (torch.from_numpy(d[k].view(np.int16)).cuda() for k in ('x', 'w', 'b'))\n"
-        "N, H, W, Cin = d['x'].shape; Cout, KH, KW, _ = d['w'].shape; s, p = int(d['s']), int(d['p'])\n"
-        "Ho, Wo = (H + 2 * p - KH) // s + 1, (W + 2 * p - KW) // s + 1\n"
-        "y = torch.zeros(N * Ho * Wo * Cout, dtype=torch.int16, device='cuda')\n"
-        "ttfoil.conv2d_nhwc(x, w, b, y, N, H, W, Cin, Cout, KH, KW, s, p, relu=True)\n"
-        "torch.cuda.synchronize(); assert ttfoil.device_error() == 0\n"
-        "np.save(sys.argv[2], y.cpu().numpy())\n")
+    script = d / "run_cases.py"
+    script.write_text(RUN_CASES)
     cases = []
     for i, (xs, ws, stride, pad) in enumerate(VARIANT_CASES):
-        x = oracle.rand_bf16(xs, 40 + i)
-        w = oracle.randn_bf16(ws, 50 + i, np.sqrt(2.0 / (ws[1] * ws[2] * ws[3])))
-        b = oracle.rand_bf16((ws[0],), 60 + i, -0.1, 0.1)
+        inp, x, w, b = make_case(d, i, xs, ws, stride, pad, 40 + i)
         got = run_conv(env, x, w, b, stride, pad, relu=True)
         check(got, oracle.conv_nhwc(x, w, b, stride, pad, relu=True, threads=8), x, w)
-        inp = d / f"in{i}.npz"
-        np.savez(inp, x=x, w=w, b=b, s=stride, p=pad)
-        cases.append((inp, got))
+        cases.append((inp, got, x, w, b, stride, pad))
     return script, cases
 
 
-@pytest.mark.parametrize("variant", sorted(VARIANTS))
-def test_kernel_variants_agree_bitwise(variant_inputs, tmp_path, variant):
-    """Every kernel variant (gather producer, single-CTA tensor copies, 2-SM
-    weight-stationary pair) feeds identical operand tiles in the same K order,
-    so each reproduces the default path's output bit for bit on every case;
-    the default outputs are themselves checked against the oracle."""
+@pytest.mark.parametrize("variant", ["gather", "single", "pair", "plane"])
+def test_kernel_variants(variant_inputs, tmp_path, variant):
+    """The im2col kernels (gather producer, single-CTA tensor copies, 2-SM
+    weight-stationary pair) feed identical operand tiles in the same K order,
+    so each reproduces the default path's output bit for bit on every case.
+    The plane kernel sums the same products in plane order: where it serves
+    a case, its output is checked against the oracle."""
     script, cases = variant_inputs
-    env_vars = dict(os.environ, **VARIANTS[variant])
-    for i, (inp, got) in enumerate(cases):
-        out = tmp_path / f"out{i}.npy"
-        r = subprocess.run([sys.executable, str(script), str(inp), str(out)], env=env_vars,
-                           capture_output=True, text=True, timeout=300)
-        assert r.returncode == 0, r.stderr[-2000:]
-        ref = np.load(out).view(np.uint16).reshape(got.shape)
-        assert np.array_equal(got, ref), (i, int(np.sum(got != ref)))
+    outs = run_variant(script, variant, [c[0] for c in cases], tmp_path)
+    served = 0
+    for i, ((inp, got, x, w, b, stride, pad), out) in enumerate(zip(cases, outs)):
+        if not out.exists():
+            assert variant == "plane", f"{variant} must serve case {i}"
+            continue
+        served += 1
+        y = np.load(out).view(np.uint16).reshape(got.shape)
+        if variant == "plane":
+            check(y, oracle.conv_nhwc(x, w, b, stride, pad, relu=True, threads=8), x, w)
+        else:
+            assert np.array_equal(y, got), (i, int(np.sum(y != got)))
+    assert served >= 2
+
+
+def test_plane_kernel_shapes(env, tmp_path):
+    """Every PLANE_CASES shape through the plane kernel (forced: the run fails
+    if it does not serve the shape), against the oracle; the larger cases
+    on sampled images."""
+    script = tmp_path / "run_cases.py"
+    script.write_text(RUN_CASES)
+    made = [make_case(tmp_path, i, *c, 700 + 30 * i) for i, c in enumerate(PLANE_CASES)]
+    outs = run_variant(script, "plane", [m[0] for m in made], tmp_path)
+    for i, ((inp, x, w, b), out, (xs, ws, stride, pad)) in enumerate(zip(made, outs, PLANE_CASES)):
+        assert out.exists(), f"plane kernel did not serve case {i}"
+        N, H, W, _ = xs
+        Ho, Wo = (H + 2 * pad - ws[1]) // stride + 1, (W + 2 * pad - ws[2]) // stride + 1
+        y = np.load(out).view(np.uint16).reshape(N, Ho, Wo, ws[0])
+        imgs = (0, N - 1) if H * W > 4096 else tuple(range(N))
+        for n in sorted(set(imgs)):
+            e = oracle.conv_nhwc(x, w, b, stride, pad, relu=True, images=(n, n + 1), threads=8)[n]
+            check(y[n:n + 1], e[None], x, w)
 
 
 def test_conv_rejects_bad_shapes(env):

@@ -129,18 +129,15 @@ __device__ __forceinline__ int epi_mode(const Params& p) {
     return p.relu ? 2 : (p.bias != nullptr ? 1 : 0);
 }
 
-// Bias words (bf16 pairs) of output channels co .. co + 31, or zeros.
+// Bias words (bf16 pairs) of output channels co .. co + 31, or zeros; each
+// group of 16 channels is read only if it lies below Cout (a multiple of 16).
 __device__ __forceinline__ void load_bias32(const Params& p, uint32_t co, bool want, uint32_t (&bw)[16]) {
-    if (want && co < p.Cout) {
-        const uint4* bp = reinterpret_cast<const uint4*>(p.bias + co);
+    const uint4* bp = reinterpret_cast<const uint4*>(p.bias + co);
 #pragma unroll
-        for (int i = 0; i < 4; ++i) {
-            const uint4 bv = __ldg(bp + i);
-            bw[4 * i] = bv.x; bw[4 * i + 1] = bv.y; bw[4 * i + 2] = bv.z; bw[4 * i + 3] = bv.w;
-        }
-    } else {
-#pragma unroll
-        for (int i = 0; i < 16; ++i) bw[i] = 0u;
+    for (int i = 0; i < 4; ++i) {
+        uint4 bv = make_uint4(0u, 0u, 0u, 0u);
+        if (want && co + 16u * (uint32_t)(i / 2) < p.Cout) bv = __ldg(bp + i);
+        bw[4 * i] = bv.x; bw[4 * i + 1] = bv.y; bw[4 * i + 2] = bv.z; bw[4 * i + 3] = bv.w;
     }
 }
 
@@ -174,11 +171,12 @@ struct Epi {
 // engine clips rows >= M and columns >= Cout), one bulk group per box.  Box
 // b is rewritten one tile later, after waiting until at most kBoxes - 1 newer
 // groups still read shared memory, i.e. box b's previous store has.
-// `release` runs after the last TMEM load.
+// `release` runs after the last TMEM load.  Rows from m_end on are not
+// stored (the box of a warp whose first row m0 >= m_end is skipped).
 template <int BN, class Release>
 __device__ __forceinline__ void epilogue_rows(const Params& p, const CUtensorMap* tmap_y, uint32_t t_row,
                                               uint32_t m0, uint32_t co0, uint32_t stg, int mode, uint32_t lane,
-                                              Release release) {
+                                              uint32_t m_end, Release release) {
     using E = Epi<BN>;
     const uint32_t row_off = lane * E::kRowBytes;
     const uint32_t sw = E::kCols == 64 ? (lane & 7u) : ((lane >> 1) & 3u);
@@ -226,7 +224,7 @@ __device__ __forceinline__ void epilogue_rows(const Params& p, const CUtensorMap
             __syncwarp();
             if (lane == 0) {
                 const uint32_t xc = co0 + (uint32_t)(bx * E::kCols);
-                if (m0 < p.M && xc < p.Cout) tma_store_2d(tmap_y, (int32_t)xc, (int32_t)m0, box);
+                if (m0 < m_end && xc < p.Cout) tma_store_2d(tmap_y, (int32_t)xc, (int32_t)m0, box);
                 bulk_commit();
             }
         }
@@ -491,7 +489,7 @@ __global__ void __launch_bounds__(kThreads, 1)
             tc_fence_after();
             uint64_t* te = &tempty[acc];
             epilogue_rows<BN>(p, &tmap_y, tmem_base + ((qd * 32u) << 16) + acc * BN + col0, mb * 128u + qd * 32u,
-                              nb * BN + col0, stg, mode, lane, [&] {
+                              nb * BN + col0, stg, mode, lane, p.M, [&] {
                                   tc_fence_before();
                                   __syncwarp();
                                   if (lane == 0) mbar_arrive(te);
@@ -738,7 +736,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
                 const uint32_t m0 = (tile * 2u + rank) * (128u * kSub) + 128u * sub + qd * 32u;
                 epilogue_rows<BN>(p, &tmap_y,
                                   tmem_base + ((qd * 32u) << 16) + acc * (uint32_t)(kSub * BN) + sub * BN + col0, m0,
-                                  col0, stg, mode, lane, [&] {
+                                  col0, stg, mode, lane, p.M, [&] {
                                       tc_fence_before();
                                       __syncwarp();
                                       if (lane == 0) mbar_arrive_remote_relaxed(te);
@@ -759,6 +757,286 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
         tc_fence_after();
         asm volatile("tcgen05.dealloc.cta_group::2.sync.aligned.b32 %0, %1;" ::"r"(tmem_base),
                      "r"(PC::kTmemCols)
+                     : "memory");
+    }
+}
+
+// ------------------------------------------------------------------------
+// Plane kernel (2-SM, resident weights, Cin a multiple of 64): every input
+// pixel a CTA needs for a window of 128 output pixels is copied into shared
+// memory once per "plane", and the KH x KW taps become offsets into it.
+//
+// Write tap (kh, kw) as kh - pad = s qh + rh and kw - pad = s qw + rw (floor
+// division by the stride s, 0 <= rh, rw < s).  Its input pixel for output
+// (ho, wo) is x[s (ho + qh) + rh][s (wo + qw) + rw].  For each distinct
+// (rh, rw, qw) -- a "plane" -- entry e of a window holds, for output position
+// d = a + e (a = the window's first output pixel, d = ho Wo + wo),
+// x[s (ho + min_qh) + rh][s (wo + qw) + rw] (zero outside the image), where
+// min_qh is the smallest qh of the plane's taps.  Tap (kh, kw) of window row
+// j then reads entry j + (qh - min_qh) Wo: the same shift for every row, so
+// its A operand is the plane starting at a fixed entry.  A 3x3 stride-1 conv
+// has 3 planes (qw = -1, 0, 1), a stride-2 one 6 (row phase x column phase /
+// shift), a 1x1 one plane (the input rows themselves).  For the batch-32 3x3
+// stride-2 convolution a window reads 936 pixel rows against 1152 for nine
+// per-tap im2col copies.
+//
+// Each plane of a window is ONE im2col tensor copy: base pixel = the window's
+// first output position, im2col offsets (s qw + rw + pad, s min_qh + rh +
+// pad) -- a tap's kw and the plane's smallest kh -- and 128 + (max_qh -
+// min_qh) Wo pixels.  The copy engine walks output positions through the
+// bounding box; the box is extended by the planes' largest row span below
+// the last output row, so entries past an image's last row are that image's
+// (zero-padded) rows, not the next image's.  The copy writes entry e as row e
+// of a K-major SWIZZLE_128B operand (channel block cb: one copy each).  Tap
+// shifts are multiples of Wo rows and windows start at multiples of 128, so
+// with Wo a multiple of 8 every tap's operand starts on an 8-row swizzle
+// atom and its descriptor is the usual one.
+//
+// Windows are 128 consecutive output pixels of one image (the last window of
+// an image may be shorter; Ho * Wo must be a multiple of 32 so that each
+// epilogue warp's 32-row box is either complete or empty).  A CTA pair takes
+// windows 2 t and 2 t + 1 as the 256 rows of one cta_group::2 MMA tile.
+// Each CTA keeps its half of the weights (BN/2 output channels x all of K)
+// resident, loaded once by tensor copies.
+//
+// Roles: one producer thread issues each (window, plane)'s copies into a ring
+// of `slots` plane buffers (both CTAs' copies complete on the leader's
+// barrier, no multicast); the MMA issuer runs the taps of each plane as soon
+// as it has landed and frees the slot with a multicast commit; eight
+// epilogue warps drain the double-buffered accumulator as in the kernels
+// above.
+constexpr int kMaxPlanes = 16;
+constexpr int kMaxTaps = 25;
+constexpr int kPlaneMaxSlots = 12;
+
+struct PlaneGeo {
+    uint32_t nplanes, ntaps;
+    int32_t rh[kMaxPlanes], rw[kMaxPlanes], qw[kMaxPlanes], min_qh[kMaxPlanes];
+    uint32_t entries[kMaxPlanes];    // entries copied per window (the copy's pixel count)
+    uint32_t cb_bytes[kMaxPlanes];   // bytes of one channel block of the plane (entries * 128)
+    uint32_t map[kMaxPlanes];        // tensor map of the plane's copies (0 or 1: its pixel count)
+    uint32_t off_w[kMaxPlanes], off_h[kMaxPlanes];  // im2col offsets of the plane
+    uint32_t tap_end[kMaxPlanes];    // taps [tap_end[v - 1], tap_end[v]) read plane v
+    uint32_t tap_aoff[kMaxTaps];     // byte offset of the tap's first row: (qh - min_qh) Wo 128
+    uint32_t tap_kb[kMaxTaps];       // first weight k-block of the tap: (kh KW + kw) cblocks
+    uint32_t slots, slot_bytes;
+    uint32_t e_map[2];               // pixels per copy of tensor maps 0 and 1
+    uint32_t row_span;               // largest max_qh - min_qh of a plane (bounding-box extension)
+    uint32_t P;                      // output pixels per image (Ho * Wo)
+    uint32_t wpi;                    // windows per image
+    uint32_t windows, tiles;         // N * wpi, ceil(windows / 2)
+};
+
+template <int BN>
+__global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
+    conv_plane_kernel(const Params p, const PlaneGeo g, const __grid_constant__ CUtensorMap tmap_x0,
+                      const __grid_constant__ CUtensorMap tmap_x1, const __grid_constant__ CUtensorMap tmap_w,
+                      const __grid_constant__ CUtensorMap tmap_y) {
+    using PC = PairCfg<BN>;
+    extern __shared__ uint8_t smem_raw[];
+    uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) &
+                                               ~uintptr_t(1023));
+    uint8_t* b_res = smem;
+    uint8_t* slots = b_res + p.num_kb * PC::kHalfB;
+    uint8_t* staging = slots + g.slots * g.slot_bytes;
+    uint64_t* full = reinterpret_cast<uint64_t*>(staging + 256u * BN);
+    uint64_t* empty = full + kPlaneMaxSlots;
+    uint64_t* tfull = empty + kPlaneMaxSlots;
+    uint64_t* tempty = tfull + 2;
+    uint64_t* bfull = tempty + 2;
+    uint64_t* drain = bfull + 1;
+    uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(drain + 1);
+    volatile uint32_t* abort_flag = tmem_slot + 1;
+
+    if (p.box_cols != (uint32_t)Epi<BN>::kCols) {
+        if (threadIdx.x == 0 && blockIdx.x == 0) atomicOr(p.err, kErrConfig);
+        return;
+    }
+    const uint32_t warp = threadIdx.x >> 5, lane = threadIdx.x & 31u;
+    const uint32_t rank = cluster_ctarank();
+    const bool leader = rank == 0;
+    const uint32_t pair_id = blockIdx.x >> 1, num_pairs = gridDim.x >> 1;
+    if (threadIdx.x == 0) {
+        for (uint32_t s = 0; s < g.slots; ++s) {
+            mbar_init(&full[s], 1);
+            mbar_init(&empty[s], 1);
+        }
+        for (int b = 0; b < 2; ++b) {
+            mbar_init(&tfull[b], 1);
+            mbar_init(&tempty[b], 2 * kEpiWarps);
+        }
+        mbar_init(bfull, 1);
+        mbar_init(drain, 1);
+        *abort_flag = 0u;
+        asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+        asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+    }
+    if (warp == kMmaWarp) {
+        asm volatile("tcgen05.alloc.cta_group::2.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(
+                         smem_u32(tmem_slot)),
+                     "r"(2u * BN)
+                     : "memory");
+        asm volatile("tcgen05.relinquish_alloc_permit.cta_group::2.sync.aligned;" ::: "memory");
+    }
+    tc_fence_before();
+    __syncthreads();
+    cluster_sync();
+    tc_fence_after();
+    const uint32_t tmem_base = *tmem_slot;
+
+    if (warp == 0) {
+        if (lane == 0) {
+            // --------------------------------------- tensor-copy producer
+            tma_prefetch_map(&tmap_x0);
+            tma_prefetch_map(&tmap_x1);
+            tma_prefetch_map(&tmap_w);
+            // Resident weights, once: rows [rank BN/2, (rank + 1) BN/2) of the
+            // K x Cout weight matrix, one box per k-block.
+            if (leader) mbar_expect_tx(bfull, 2u * p.num_kb * PC::kHalfB);
+            const uint32_t lead_bfull = map_to_rank(bfull, 0);
+            for (uint32_t kb = 0; kb < p.num_kb; ++kb)
+                tma_load_2d_pair(smem_u32(b_res) + kb * PC::kHalfB, &tmap_w, (int32_t)(kb * 64u),
+                                 (int32_t)(rank * (BN / 2)), lead_bfull);
+            const uint32_t lead_full0 = map_to_rank(&full[0], 0), slot0 = smem_u32(slots);
+            uint32_t slot = 0, phase = 0, issued = 0;
+            bool ok = true;
+            for (uint32_t tile = pair_id; ok && tile < g.tiles; tile += num_pairs) {
+                // This CTA's window; past the last one it copies the last
+                // window again (its rows are never stored).
+                uint32_t win = tile * 2u + rank;
+                if (win >= g.windows) win = g.windows - 1u;
+                const uint32_t n = win / g.wpi, a = (win - n * g.wpi) * 128u;
+                const uint32_t ho = a / p.Wo, wo = a - ho * p.Wo;
+                const int32_t w0 = (int32_t)(wo * p.stride) - (int32_t)p.pad;
+                const int32_t h0 = (int32_t)(ho * p.stride) - (int32_t)p.pad;
+                for (uint32_t v = 0; v < g.nplanes; ++v) {
+                    if (!mbar_wait_cluster(&empty[slot], phase ^ 1u, abort_flag, p.err, p.wait_ns)) {
+                        ok = false;
+                        break;
+                    }
+                    const uint32_t cbb = g.cb_bytes[v];
+                    if (leader) mbar_expect_tx(&full[slot], 2u * cbb * p.cblocks);
+                    const CUtensorMap* m = g.map[v] ? &tmap_x1 : &tmap_x0;
+                    for (uint32_t cb = 0; cb < p.cblocks; ++cb)
+                        tma_load_im2col_4d_pair(slot0 + slot * g.slot_bytes + cb * cbb, m, (int32_t)(cb * 64u), w0,
+                                                h0, (int32_t)n, (uint16_t)g.off_w[v], (uint16_t)g.off_h[v],
+                                                lead_full0 + slot * 8u);
+                    ++issued;
+                    if (++slot == g.slots) {
+                        slot = 0;
+                        phase ^= 1u;
+                    }
+                }
+            }
+            // After an abort: both CTAs' copies complete on the leader's
+            // barriers, so the leader waits (bounded) for the weights and the
+            // last slots before the pair ends (at once when they have all
+            // been consumed); the final cluster barrier keeps the other CTA
+            // alive meanwhile.
+            if (leader) {
+                mbar_drain(bfull, 0, 100000000ull);
+                drain_loads(full, issued, g.slots);
+            }
+        }
+    } else if (warp == kMmaWarp) {
+        if (leader && lane == 0) {
+            // ------------------------------------------------ MMA issuer
+            // kind::f16, f32 accumulate, bf16 A and B, both K-major, M = 256.
+            const uint32_t idesc = (1u << 4) | (1u << 7) | (1u << 10) | ((uint32_t)(BN >> 3) << 17) |
+                                   ((256u >> 4) << 24);
+            constexpr uint64_t kmaj = smem_desc_sw128_kmajor();
+            const uint32_t slot0 = smem_u32(slots), b0 = smem_u32(b_res);
+            uint32_t slot = 0, phase = 0, acc = 0, acc_phase = 0;
+            bool ok = mbar_wait_cluster(bfull, 0, abort_flag, p.err, p.wait_ns);
+            for (uint32_t tile = pair_id; ok && tile < g.tiles; tile += num_pairs) {
+                if (!mbar_wait_cluster(&tempty[acc], acc_phase ^ 1u, abort_flag, p.err, p.wait_ns)) break;
+                tc_fence_after();
+                const uint32_t d_tmem = tmem_base + acc * (uint32_t)BN;
+                uint32_t accumulate = 0, t = 0;
+                for (uint32_t v = 0; v < g.nplanes; ++v) {
+                    if (!mbar_wait_cluster(&full[slot], phase, abort_flag, p.err, p.wait_ns)) {
+                        ok = false;
+                        break;
+                    }
+                    tc_fence_after();
+                    const uint32_t plane = slot0 + slot * g.slot_bytes, cbb = g.cb_bytes[v];
+                    for (; t < g.tap_end[v]; ++t) {
+                        const uint32_t a_t = plane + g.tap_aoff[t];
+                        for (uint32_t cb = 0; cb < p.cblocks; ++cb) {
+                            const uint32_t a_addr = a_t + cb * cbb;
+                            const uint32_t b_addr = b0 + (g.tap_kb[t] + cb) * PC::kHalfB;
+#pragma unroll
+                            for (uint32_t ks = 0; ks < 4; ++ks) {
+                                const uint64_t ad = kmaj | (uint64_t)(((a_addr + ks * 32u) >> 4) & 0x3fffu);
+                                const uint64_t bd = kmaj | (uint64_t)(((b_addr + ks * 32u) >> 4) & 0x3fffu);
+                                tc_mma_pair(d_tmem, ad, bd, idesc, accumulate);
+                                accumulate = 1u;
+                            }
+                        }
+                    }
+                    tc_commit_pair_mc(&empty[slot], 0x3);
+                    if (++slot == g.slots) {
+                        slot = 0;
+                        phase ^= 1u;
+                    }
+                }
+                if (!ok) break;
+                tc_commit_pair_mc(&tfull[acc], 0x3);
+                if (++acc == 2) {
+                    acc = 0;
+                    acc_phase ^= 1u;
+                }
+            }
+            tc_commit_pair(drain);
+            mbar_drain(drain, 0, 100000000ull);
+        }
+    } else if (warp > kMmaWarp) {
+        // ---------------------------------------------------- epilogue
+        // Warp e (0..7): TMEM lane quadrant warp % 4 (window rows qd 32 ..
+        // qd 32 + 31), column half e / 4; the accumulator is released on the
+        // leader's barrier.  Rows past the window's end are not stored.
+        const uint32_t e = warp - 5u, qd = warp & 3u, half = e >> 2;
+        const uint32_t col0 = half * (uint32_t)(BN / 2);
+        const uint32_t stg = smem_u32(staging) + e * Epi<BN>::kWarpBytes;
+        const int mode = epi_mode(p);
+        const uint32_t lead_tempty0 = map_to_rank(&tempty[0], 0);
+        if (lane == 0) tma_prefetch_map(&tmap_y);
+        uint32_t acc = 0, acc_phase = 0;
+        for (uint32_t tile = pair_id; tile < g.tiles; tile += num_pairs) {
+            bool ok = true;
+            if (lane == 0) ok = mbar_wait_cluster(&tfull[acc], acc_phase, abort_flag, p.err, p.wait_ns);
+            ok = __shfl_sync(0xffffffffu, ok ? 1 : 0, 0) != 0;
+            if (!ok) break;
+            tc_fence_after();
+            const uint32_t win = tile * 2u + rank;
+            uint32_t row0 = 0, row_end = 0;  // global output rows of the window
+            if (win < g.windows) {
+                const uint32_t n = win / g.wpi, a = (win - n * g.wpi) * 128u;
+                row0 = n * g.P + a;
+                row_end = n * g.P + min(g.P, a + 128u);
+            }
+            const uint32_t te = lead_tempty0 + acc * 8u;
+            epilogue_rows<BN>(p, &tmap_y, tmem_base + ((qd * 32u) << 16) + acc * (uint32_t)BN + col0,
+                              row0 + qd * 32u, col0, stg, mode, lane, row_end, [&] {
+                                  tc_fence_before();
+                                  __syncwarp();
+                                  if (lane == 0) mbar_arrive_remote_relaxed(te);
+                              });
+            if (++acc == 2) {
+                acc = 0;
+                acc_phase ^= 1u;
+            }
+        }
+        if (lane == 0) bulk_wait_all();
+    }
+
+    tc_fence_before();
+    __syncthreads();
+    cluster_sync();
+    if (warp == kMmaWarp) {
+        tc_fence_after();
+        asm volatile("tcgen05.dealloc.cta_group::2.sync.aligned.b32 %0, %1;" ::"r"(tmem_base),
+                     "r"(2u * BN)
                      : "memory");
     }
 }
@@ -814,6 +1092,115 @@ static int launch_pair(const Params& p, uint32_t stages, const CUtensorMap& mx, 
     return FOIL_OK;
 }
 
+// Plane-kernel geometry (see conv_plane_kernel).  False when the shape is
+// not served: Cin not a multiple of 64, more than 25 taps or 16 planes, Ho Wo
+// not a multiple of 32, Wo not a multiple of 8, a plane span above 256
+// pixels, Cout above 256, or fewer than two plane slots fit.
+static int floor_div(int a, int b) { return a >= 0 ? a / b : -((-a + b - 1) / b); }
+
+static bool plane_geometry(const Params& p, int bn, uint32_t optin, PlaneGeo& g, uint32_t& smem) {
+    memset(&g, 0, sizeof g);
+    if (p.Cin % 64 != 0 || p.KH * p.KW > (uint32_t)kMaxTaps || p.stride == 0 || p.stride > 8 || p.pad > 7 ||
+        p.Cout > 256 || p.Wo == 0)
+        return false;
+    const uint32_t P = p.Ho * p.Wo;
+    if (P % 32 != 0 || p.Wo % 8 != 0) return false;
+    struct Tap {
+        uint32_t v, kb;
+        int qh;
+    } taps[kMaxTaps];
+    int max_qh[kMaxPlanes];
+    const int s = (int)p.stride;
+    uint32_t nt = 0;
+    for (uint32_t kh = 0; kh < p.KH; ++kh)
+        for (uint32_t kw = 0; kw < p.KW; ++kw) {
+            const int dh = (int)kh - (int)p.pad, dw = (int)kw - (int)p.pad;
+            const int qh = floor_div(dh, s), rh = dh - qh * s, qw = floor_div(dw, s), rw = dw - qw * s;
+            uint32_t v = 0;
+            while (v < g.nplanes && !(g.rh[v] == rh && g.rw[v] == rw && g.qw[v] == qw)) ++v;
+            if (v == g.nplanes) {
+                if (g.nplanes == (uint32_t)kMaxPlanes) return false;
+                g.rh[v] = rh;
+                g.rw[v] = rw;
+                g.qw[v] = qw;
+                g.min_qh[v] = qh;
+                max_qh[v] = qh;
+                ++g.nplanes;
+            }
+            g.min_qh[v] = g.min_qh[v] < qh ? g.min_qh[v] : qh;
+            max_qh[v] = max_qh[v] > qh ? max_qh[v] : qh;
+            taps[nt++] = Tap{v, (kh * p.KW + kw) * p.cblocks, qh};
+        }
+    // Pixel counts of the copies: the smallest and the largest plane span
+    // (one im2col tensor map each, at most 256 pixels per copy).
+    uint32_t e_lo = ~0u, e_hi = 0, span = 0;
+    for (uint32_t v = 0; v < g.nplanes; ++v) {
+        const uint32_t e = 128u + (uint32_t)(max_qh[v] - g.min_qh[v]) * p.Wo;
+        e_lo = e < e_lo ? e : e_lo;
+        e_hi = e > e_hi ? e : e_hi;
+        span = (uint32_t)(max_qh[v] - g.min_qh[v]) > span ? (uint32_t)(max_qh[v] - g.min_qh[v]) : span;
+    }
+    if (e_hi > 256u) return false;
+    g.e_map[0] = e_lo;
+    g.e_map[1] = e_hi;
+    g.row_span = span;
+    // Taps grouped by plane (in (kh, kw) order inside a plane).
+    uint32_t slot_bytes = 0;
+    for (uint32_t v = 0; v < g.nplanes; ++v) {
+        const uint32_t e = 128u + (uint32_t)(max_qh[v] - g.min_qh[v]) * p.Wo;
+        g.map[v] = e == e_lo ? 0u : 1u;
+        g.entries[v] = g.e_map[g.map[v]];
+        g.cb_bytes[v] = g.entries[v] * 128u;  // entries: a multiple of 8 (whole 1 KiB swizzle atoms)
+        g.off_w[v] = (uint32_t)(s * g.qw[v] + g.rw[v] + (int)p.pad);
+        g.off_h[v] = (uint32_t)(s * g.min_qh[v] + g.rh[v] + (int)p.pad);
+        const uint32_t bytes = g.cb_bytes[v] * p.cblocks;
+        slot_bytes = bytes > slot_bytes ? bytes : slot_bytes;
+        for (uint32_t t = 0; t < nt; ++t)
+            if (taps[t].v == v) {
+                g.tap_aoff[g.ntaps] = (uint32_t)(taps[t].qh - g.min_qh[v]) * p.Wo * 128u;
+                g.tap_kb[g.ntaps] = taps[t].kb;
+                ++g.ntaps;
+            }
+        g.tap_end[v] = g.ntaps;
+    }
+    if (slot_bytes >= (1u << 18)) return false;
+    g.slot_bytes = (slot_bytes + 1023u) / 1024u * 1024u;
+    const uint32_t fixed = 1024u + p.num_kb * (uint32_t)(bn / 2) * 128u + 256u * (uint32_t)bn + (uint32_t)kBarrierBytes;
+    if (fixed >= optin) return false;
+    uint32_t slots = (optin - fixed) / g.slot_bytes;
+    if (slots > (uint32_t)kPlaneMaxSlots) slots = kPlaneMaxSlots;
+    if (slots < 2) return false;
+    g.slots = slots;
+    g.P = P;
+    g.wpi = (P + 127u) / 128u;
+    g.windows = p.N * g.wpi;
+    g.tiles = (g.windows + 1u) / 2u;
+    smem = fixed + slots * g.slot_bytes;
+    return true;
+}
+
+template <int BN>
+static int launch_plane(const Params& p, const PlaneGeo& g, uint32_t smem, const CUtensorMap& mx0,
+                        const CUtensorMap& mx1, const CUtensorMap& mw, const CUtensorMap& my,
+                        cudaStream_t stream, int max_ctas) {
+    if (foil_smem_optin((const void*)conv_plane_kernel<BN>, (int)smem) != cudaSuccess) {
+        foil_set_error(FOIL_ERR_CUDA, "foil_conv2d_nhwc: cudaFuncSetAttribute failed");
+        return FOIL_ERR_CUDA;
+    }
+    const uint32_t max_pairs = (uint32_t)max_ctas / 2;
+    const uint32_t pairs = g.tiles < max_pairs ? g.tiles : max_pairs;
+    conv_plane_kernel<BN><<<2 * pairs, kThreads, smem, stream>>>(p, g, mx0, mx1, mw, my);
+    cudaError_t e = cudaGetLastError();
+    if (e != cudaSuccess) {
+        char buf[200];
+        snprintf(buf, sizeof buf, "foil_conv2d_nhwc: launch failed: %s", cudaGetErrorString(e));
+        foil_set_error(FOIL_ERR_CUDA, buf);
+        return FOIL_ERR_CUDA;
+    }
+    foil_count_launch();
+    return FOIL_OK;
+}
+
 template <bool kTma>
 static int launch_tiles(const Params& p, int bn, const CUtensorMap& mx, const CUtensorMap& mw,
                         const CUtensorMap& my, cudaStream_t stream, int max_ctas) {
@@ -847,13 +1234,17 @@ static const Encoders& encoders() {
     return e;
 }
 
-// The tensor-copy producer serves Cin a multiple of 64 (one 128-byte channel
-// run per k-block) with a traversal stride the copy engine supports (<= 8)
-// and byte strides below 2^40; other shapes use the gather producer.
-// FOIL_CONV_PRODUCER=gather selects the gather producer for every shape,
-// =single the tensor-copy producer in the single-CTA kernel, and =pair the
-// pair kernel wherever it can run (A/B comparisons of the variants, which
-// agree bit for bit).
+// The plane kernel serves Cin a multiple of 64, Cout <= 256, Ho Wo a
+// multiple of 32 and up to 9 taps.  Otherwise the tensor-copy producer
+// serves Cin a multiple of 64 (one 128-byte channel run per k-block) with a
+// traversal stride the copy engine supports (<= 8) and byte strides below
+// 2^40, and the gather producer the rest.  FOIL_CONV_PRODUCER=gather selects
+// the gather producer for every shape, =single the tensor-copy producer in
+// the single-CTA kernel, =pair the im2col pair kernel wherever it can run,
+// and =plane the plane kernel, failing with FOIL_ERR_UNSUPPORTED where it
+// cannot (A/B comparisons: the first three agree bit for bit; the plane
+// kernel sums the same products in plane order, so it agrees within the
+// tolerance).
 static const char* producer_override() {
     static const char* v = getenv("FOIL_CONV_PRODUCER");
     return v ? v : "";
@@ -880,6 +1271,29 @@ static bool encode_output_map(const Params& p, CUtensorMap* my) {
                    CU_TENSOR_MAP_L2_PROMOTION_NONE, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
 }
 
+static bool encode_weight_map(const Params& p, uint32_t w_rows, CUtensorMap* mw);
+
+// im2col map of the plane kernel's copies: `pixels` output positions per
+// copy, 64 channels, traversal stride = the conv stride, and the bounding
+// box of base pixels [-pad, dim - 1 + pad - (k - 1)] extended below the last
+// output row by the planes' largest row span (g.row_span output rows), so a
+// copy that runs past an image's last output row reads that image's
+// zero-padded rows rather than the next image.
+static bool encode_plane_map(const Params& p, const PlaneGeo& g, uint32_t pixels, CUtensorMap* mx) {
+    const Encoders& e = encoders();
+    if (!e.im2col) return false;
+    const cuuint64_t xdim[4] = {p.Cin, p.W, p.H, p.N};
+    const cuuint64_t xstr[3] = {(cuuint64_t)p.Cin * 2, (cuuint64_t)p.W * p.Cin * 2,
+                                (cuuint64_t)p.H * p.W * p.Cin * 2};
+    const int lower[2] = {-(int)p.pad, -(int)p.pad};
+    const int upper[2] = {(int)p.pad - (int)(p.KW - 1),
+                          (int)p.pad - (int)(p.KH - 1) + (int)(p.stride * g.row_span)};
+    const cuuint32_t trav[4] = {1, p.stride, p.stride, 1};
+    return e.im2col(mx, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 4, const_cast<uint16_t*>(p.x), xdim, xstr, lower, upper,
+                    64, pixels, trav, CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
+                    CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
+}
+
 // A (im2col of x) and weights as a K x Cout matrix read in boxes of 64
 // channels x `w_rows` output channels (BN, or BN/2 per CTA of a pair).
 static bool encode_maps(const Params& p, uint32_t w_rows, uint32_t pixels, CUtensorMap* mx, CUtensorMap* mw) {
@@ -898,7 +1312,14 @@ static bool encode_maps(const Params& p, uint32_t w_rows, uint32_t pixels, CUten
                  upper, 64, pixels, trav, CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
                  CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) != CUDA_SUCCESS)
         return false;
-    // Weights as a K x Cout matrix (K = KH * KW * Cin contiguous per row).
+    return encode_weight_map(p, w_rows, mw);
+}
+
+// Weights as a K x Cout matrix (K = KH * KW * Cin contiguous per row), read
+// in boxes of 64 channels x `w_rows` output channels, SWIZZLE_128B.
+static bool encode_weight_map(const Params& p, uint32_t w_rows, CUtensorMap* mw) {
+    const Encoders& e = encoders();
+    if (!e.tiled) return false;
     const cuuint64_t wdim[2] = {(cuuint64_t)p.KH * p.KW * p.Cin, p.Cout};
     const cuuint64_t wstr[1] = {(cuuint64_t)p.KH * p.KW * p.Cin * 2};
     const cuuint32_t box[2] = {64, w_rows};
@@ -948,15 +1369,43 @@ int launch(const uint16_t* x, const uint16_t* w, const uint16_t* bias, uint16_t*
         foil_set_error(FOIL_ERR_CUDA, "foil_conv2d_nhwc: tensor-map encoding failed");
         return FOIL_ERR_CUDA;
     }
-    if (!tc) return launch_tiles<false>(p, bn, mx, mw, my, stream, max_ctas);
-    // Weight-stationary pair kernel: one column block, more than one 128-row
-    // block, and at least 4 A stages beside the resident weights.
     int dev = 0, optin = 0;
     if (cudaGetDevice(&dev) != cudaSuccess ||
         cudaDeviceGetAttribute(&optin, cudaDevAttrMaxSharedMemoryPerBlockOptin, dev) != cudaSuccess) {
         foil_set_error(FOIL_ERR_CUDA, "foil_conv2d_nhwc: device query failed");
         return FOIL_ERR_CUDA;
     }
+    // Plane kernel (2-SM, resident weights, taps as offsets into one copy
+    // per plane): only on request.  Measured on the batch-32 configurations
+    // (L2 flushed) it trails the im2col kernels below: 3x3 stride 2 36.7
+    // against 29.3 us, 1x1 23.5 against 21.9 us, and the N = 1 3x3 14.1
+    // against 13.9 us; it moves fewer operand bytes but issues more copies.
+    const char* ov = producer_override();
+    if (max_ctas >= 2 && strcmp(ov, "plane") == 0) {
+        PlaneGeo g;
+        uint32_t smem = 0;
+        if (plane_geometry(p, bn, (uint32_t)optin, g, smem)) {
+            alignas(64) CUtensorMap mx1;
+            if (!encode_weight_map(p, (uint32_t)bn / 2, &mw) || !encode_plane_map(p, g, g.e_map[0], &mx) ||
+                !encode_plane_map(p, g, g.e_map[1], &mx1)) {
+                foil_set_error(FOIL_ERR_CUDA, "foil_conv2d_nhwc: tensor-map encoding failed");
+                return FOIL_ERR_CUDA;
+            }
+            switch (bn) {
+                case 64: return launch_plane<64>(p, g, smem, mx, mx1, mw, my, stream, max_ctas);
+                case 128: return launch_plane<128>(p, g, smem, mx, mx1, mw, my, stream, max_ctas);
+                default: return launch_plane<256>(p, g, smem, mx, mx1, mw, my, stream, max_ctas);
+            }
+        }
+    }
+    if (strcmp(ov, "plane") == 0) {
+        foil_set_error(FOIL_ERR_UNSUPPORTED, "foil_conv2d_nhwc: FOIL_CONV_PRODUCER=plane but the plane kernel "
+                                             "does not serve this shape");
+        return FOIL_ERR_UNSUPPORTED;
+    }
+    if (!tc) return launch_tiles<false>(p, bn, mx, mw, my, stream, max_ctas);
+    // Weight-stationary pair kernel: one column block, more than one 128-row
+    // block, and at least 4 A stages beside the resident weights.
     uint32_t stages = 0;
     while (stages < (uint32_t)kPairMaxStages && pair_smem_bytes(p, bn, stages + 1) <= (uint32_t)optin) ++stages;
     // The pair kernel pays ~1 us more start-up (cluster launch, resident

@@ -41,6 +41,24 @@ __device__ __forceinline__ bool mbar_try_wait(uint64_t* bar, uint32_t parity) {
     return done != 0;
 }
 
+// Suspend hint of the waiting forms below: the thread sleeps until the phase
+// completes or about this many nanoseconds pass, so a warp waiting for a
+// barrier leaves the issue slots to the warps that do the work (a plain
+// try_wait returns at once and the wait loop would spin).
+constexpr uint32_t kSuspendNs = 10000u;
+
+__device__ __forceinline__ bool mbar_try_wait_sleep(uint64_t* bar, uint32_t parity) {
+    uint32_t done;
+    asm volatile(
+        "{\n\t.reg .pred p;\n\t"
+        "mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2, %3;\n\t"
+        "selp.b32 %0, 1, 0, p;\n\t}"
+        : "=r"(done)
+        : "r"(smem_u32(bar)), "r"(parity), "r"(kSuspendNs)
+        : "memory");
+    return done != 0;
+}
+
 // Default wall-time limit of one bounded wait (the kernels take the limit
 // as a launch parameter; foil_set_wait_limit_ns changes it).
 constexpr uint64_t kDefaultWaitLimitNs = 2000000000ull;  // 2 s per wait
@@ -51,13 +69,11 @@ constexpr uint64_t kDefaultWaitLimitNs = 2000000000ull;  // 2 s per wait
 __device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity,
                                           volatile uint32_t* abort_flag, uint32_t* err,
                                           uint64_t limit_ns) {
-#pragma unroll 1
-    for (int i = 0; i < 32; ++i)
-        if (mbar_try_wait(bar, parity)) return true;
+    if (mbar_try_wait(bar, parity)) return true;
     const uint64_t t0 = global_ns();
 #pragma unroll 1
     while (true) {
-        if (mbar_try_wait(bar, parity)) return true;
+        if (mbar_try_wait_sleep(bar, parity)) return true;
         if (*abort_flag) return false;
         if (global_ns() - t0 > limit_ns) {
             *abort_flag = 1u;
@@ -71,7 +87,7 @@ __device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity,
 __device__ __forceinline__ void mbar_drain(uint64_t* bar, uint32_t parity, uint64_t limit_ns) {
     const uint64_t t0 = global_ns();
 #pragma unroll 1
-    while (!mbar_try_wait(bar, parity)) {
+    while (!mbar_try_wait_sleep(bar, parity)) {
         if (global_ns() - t0 > limit_ns) return;
     }
 }
@@ -342,18 +358,28 @@ __device__ __forceinline__ bool mbar_try_wait_cluster(uint64_t* bar, uint32_t pa
     return done != 0;
 }
 
+__device__ __forceinline__ bool mbar_try_wait_cluster_sleep(uint64_t* bar, uint32_t parity) {
+    uint32_t done;
+    asm volatile(
+        "{\n\t.reg .pred p;\n\t"
+        "mbarrier.try_wait.parity.acquire.cluster.shared::cta.b64 p, [%1], %2, %3;\n\t"
+        "selp.b32 %0, 1, 0, p;\n\t}"
+        : "=r"(done)
+        : "r"(smem_u32(bar)), "r"(parity), "r"(kSuspendNs)
+        : "memory");
+    return done != 0;
+}
+
 // Bounded wait (acquire at cluster scope) for barriers that receive arrivals
 // from the other CTA of the pair.
 __device__ __forceinline__ bool mbar_wait_cluster(uint64_t* bar, uint32_t parity,
                                                   volatile uint32_t* abort_flag, uint32_t* err,
                                                   uint64_t limit_ns) {
-#pragma unroll 1
-    for (int i = 0; i < 32; ++i)
-        if (mbar_try_wait_cluster(bar, parity)) return true;
+    if (mbar_try_wait_cluster(bar, parity)) return true;
     const uint64_t t0 = global_ns();
 #pragma unroll 1
     while (true) {
-        if (mbar_try_wait_cluster(bar, parity)) return true;
+        if (mbar_try_wait_cluster_sleep(bar, parity)) return true;
         if (*abort_flag) return false;
         if (global_ns() - t0 > limit_ns) {
             *abort_flag = 1u;
