@@ -306,6 +306,22 @@ FOIL_API int foil_conv2d_nhwc_dev(const uint16_t* x, const uint16_t* w, const ui
                                   uint32_t Cout, uint32_t KH, uint32_t KW, uint32_t stride,
                                   uint32_t pad, int32_t relu, void* stream);
 
+/* The same convolution in the reference's own tensor convention: x (N,
+ * Cin, H, W) channel-major activations, w (Cout, Cin * KH * KW) -- the
+ * reference's reshaped weights, i.e. (Cout, Cin, KH, KW) -- bias (Cout) or
+ * NULL, y (N, Cout, Ho, Wo); any Cin and Cout.  The operands are re-laid on
+ * the device (batched transposes into a stream-ordered workspace, channels
+ * zero-padded to multiples of 16), then the NHWC convolution above runs and
+ * its output is transposed back; the caller's host does no im2col or
+ * transposition.  Replaces the reference conv tests' host preparation --
+ * im2col (tests/test_conv_3x3.cpp:108-127, test_conv_3x3_s2.cpp:114-133) and
+ * weight_reshape (tests/test_conv_3x3.cpp:130-141) -- feeding the tiled
+ * matmul, for N images at once. */
+FOIL_API int foil_conv2d_chw_dev(const uint16_t* x, const uint16_t* w, const uint16_t* bias, uint16_t* y,
+                                 uint32_t N, uint32_t Cin, uint32_t H, uint32_t W, uint32_t Cout,
+                                 uint32_t KH, uint32_t KW, uint32_t stride, uint32_t pad, int32_t relu,
+                                 void* stream);
+
 /* Allocation-free variant of foil_matmul_tiles_dev, for callers that cannot
  * allocate device memory when they launch (allocator or memory-pool
  * callbacks, processes whose GPU memory another allocator already owns,

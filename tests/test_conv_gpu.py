@@ -72,6 +72,46 @@ def test_conv_against_reference_goldens(env, golden, tag):
     check(got, exp, x, w)
 
 
+@pytest.mark.parametrize("tag", ["conv3_1_9_2", "conv3_2_18_14", "conv3s2_1_9_2", "conv3s2_4_18_8",
+                                 "conv1_2_2_2", "conv1_8_4_16"])
+def test_conv_chw_entry_on_reference_goldens(env, golden, tag):
+    """foil_conv2d_chw_dev takes the reference tests' own tensors as they are:
+    x (Cin, H, W), the reshaped weights (Cout, Cin*KH*KW), y (Cout, Ho, Wo);
+    no host transposition or im2col, any channel count."""
+    torch, tf = env
+    g = golden("conv_" + tag)
+    Cin, H, W, Cout, k, stride, pad = (int(v) for v in g["dims"])
+    x = np.ascontiguousarray(g["x"])
+    w = np.ascontiguousarray(g["w"]).reshape(Cout, Cin * k * k)
+    Ho, Wo = (H + 2 * pad - k) // stride + 1, (W + 2 * pad - k) // stride + 1
+    y = torch.full((Cout * Ho * Wo,), 0x7fc0, dtype=torch.int16, device="cuda")
+    tf.conv2d_chw(dev(torch, x), dev(torch, w), None, y, 1, Cin, H, W, Cout, k, k, stride, pad)
+    torch.cuda.synchronize()
+    assert tf.device_error() == 0
+    got = y.cpu().numpy().view(np.uint16).reshape(Cout, Ho, Wo)
+    check(got, g["y"].reshape(Cout, Ho, Wo), x, w.reshape(Cout, Cin, k, k))
+
+
+def test_conv_chw_entry_batch_bias_relu(env):
+    """Batch 3, channel counts that are not multiples of 16, bias + relu:
+    against the oracle's NHWC convolution of the same tensors."""
+    torch, tf = env
+    N, Cin, H, W, Cout, k, stride, pad = 3, 24, 15, 13, 40, 3, 2, 1
+    x = oracle.rand_bf16((N, Cin, H, W), 81)
+    w = oracle.randn_bf16((Cout, Cin, k, k), 82, np.sqrt(2.0 / (Cin * k * k)))
+    b = oracle.rand_bf16((Cout,), 83, -0.1, 0.1)
+    Ho, Wo = (H + 2 * pad - k) // stride + 1, (W + 2 * pad - k) // stride + 1
+    y = torch.zeros(N * Cout * Ho * Wo, dtype=torch.int16, device="cuda")
+    tf.conv2d_chw(dev(torch, x), dev(torch, w), dev(torch, b), y, N, Cin, H, W, Cout, k, k, stride, pad, relu=True)
+    torch.cuda.synchronize()
+    assert tf.device_error() == 0
+    got = y.cpu().numpy().view(np.uint16).reshape(N, Cout, Ho, Wo).transpose(0, 2, 3, 1)
+    xn = np.ascontiguousarray(x.transpose(0, 2, 3, 1))
+    wn = np.ascontiguousarray(w.transpose(0, 2, 3, 1))
+    exp = oracle.conv_nhwc(xn, wn, b, stride, pad, relu=True, threads=8)
+    check(np.ascontiguousarray(got), exp, xn, wn)
+
+
 def test_config2_conv3x3_s1_bias_relu(env):
     """N=1, 56x56, 64 -> 64, 3x3 stride 1 pad 1, bias + relu (M=3136, N=64, K=576)."""
     x = oracle.rand_bf16((1, 56, 56, 64), 2)

@@ -193,13 +193,19 @@ def mcast_setup(tf, d, Mt, Kt, Nt, a, b, with_producer=True):
     return kp, kc, bo, stage_c, flag_c
 
 
-def test_matmul_2core_mcast_program(tf):
+@pytest.mark.parametrize("consumer_first", [False, True])
+def test_matmul_2core_mcast_program(tf, consumer_first):
+    """Producer and consumer run as one launch (one CTA per core, resident
+    together): the consumer's device-side wait sees the flag the producer
+    sets after forwarding B, in either order of the execute list."""
     Mt, Kt, Nt = 2, 6, 3
     a = oracle.rand_bf16((2 * Mt * 32, Kt * 32), 9)
     b = oracle.rand_bf16((Kt * 32, Nt * 32), 10)
     with tf.Device(0, cores=[(0, 0), (0, 1)]) as d:
         kp, kc, bo, stage_c, flag_c = mcast_setup(tf, d, Mt, Kt, Nt, a, b)
-        d.execute([kp, kc])
+        launches = tf.launch_count()
+        d.execute([kc, kp] if consumer_first else [kp, kc])
+        assert tf.launch_count() == launches + 1, "both core programs in one launch"
         got = oracle.untilize(d.read_array(bo, np.uint16, 2 * Mt * Nt * 1024), 2 * Mt * 32, Nt * 32)
         # B was forwarded into the consumer's L1 and its flag set.
         assert np.array_equal(d.read_array(stage_c, np.uint16, Kt * Nt * 1024), oracle.tilize(b))
@@ -209,15 +215,20 @@ def test_matmul_2core_mcast_program(tf):
 
 def test_mcast_consumer_alone_times_out(tf):
     """A consumer whose ready flag nobody sets ends in the reference's timeout
-    error (reader_consumer.cpp:40-44 spins until the host's deadline)."""
+    error (reader_consumer.cpp:40-44 spins until the host's deadline): its
+    device-side wait runs out at the execute's deadline and the kernel
+    returns; the device then runs the pair normally."""
     Mt, Kt, Nt = 1, 2, 2
     a = oracle.rand_bf16((2 * Mt * 32, Kt * 32), 11)
     b = oracle.rand_bf16((Kt * 32, Nt * 32), 12)
     with tf.Device(0, cores=[(0, 0), (0, 1)]) as d:
         kp, kc, *_ = mcast_setup(tf, d, Mt, Kt, Nt, a, b)
+        launches = tf.launch_count()
         with pytest.raises(tf.FoilError) as e:
             d.execute([kc], timeout_ms=300)
-        assert e.value.status == 5 and "timeout" in str(e.value)
+        assert e.value.status == 5 and "timeout" in str(e.value) and "(0,1)" in str(e.value)
+        assert tf.launch_count() == launches + 1, "the consumer was launched and its wait ran out"
+        d.execute([kp, kc])  # the context is still usable
 
 
 def test_error_behaviour(tf):

@@ -35,6 +35,7 @@
 #include "kernels/gemm_tc.cuh"
 #include "kernels/conv_tc.cuh"
 #include "kernels/eltwise.cuh"
+#include "kernels/layout.cuh"
 
 namespace {
 
@@ -712,40 +713,84 @@ extern "C" int foil_execute(foil_device* d, foil_kernel* const* kernels, size_t 
                 ops.push_back(r);
             }
         }
-        // 2. Forward phase: staging copies and ready flags (mcast producers).
-        //    Stream order puts them before every compute launch, so no kernel
-        //    ever waits on another launch.
-        bool any_gate = false;
-        for (auto& r : ops) {
-            if (r.op.kind == foil::OpKind::McastForward) {
-                cuda_check(cudaMemcpyAsync(r.p1, r.p0, r.op.in0.bytes, cudaMemcpyDeviceToDevice, d->stream),
-                           "B staging copy");
-                cuda_check(cudaMemcpyAsync(r.po, r.p1, r.op.in0.bytes, cudaMemcpyDeviceToDevice, d->stream),
-                           "B forward copy");
-                cuda_check(cudaMemcpyAsync(r.flag_dst, r.flag_src, 4, cudaMemcpyDeviceToDevice, d->stream),
-                           "flag forward copy");
+        // 2. Programs that talk to each other (the mcast producer forwards B
+        //    and sets the consumer's ready flag; the consumer waits for it,
+        //    reader_consumer.cpp:40-44) run as ONE cluster launch, one CTA
+        //    per core, so they are resident together and the consumer's
+        //    bounded device-side wait sees the producer's flag.  The other
+        //    programs of the execute follow in stream order.
+        bool interacting = false;
+        for (auto& r : ops) interacting |= r.gate != nullptr || r.op.kind == foil::OpKind::McastForward;
+        if (interacting) {
+            std::vector<foil::gemm::CoreProgram> cores;
+            std::vector<const foil_kernel*> core_kernel;
+            std::vector<bool> in_cluster(ops.size(), false);
+            for (size_t i = 0; i < n; ++i) {
+                foil::gemm::CoreProgram c = {};
+                bool any = false, plain = true;
+                for (size_t j = 0; j < ops.size(); ++j) {
+                    if (ops[j].k != kernels[i]) continue;
+                    const auto& r = ops[j];
+                    if (r.op.kind == foil::OpKind::McastForward) {
+                        c.fwd_src = r.p0;
+                        c.fwd_stage = r.p1;
+                        c.fwd_peer = r.po;
+                        c.fwd_bytes = r.op.in0.bytes;
+                        c.flag_src = reinterpret_cast<const uint32_t*>(r.flag_src);
+                        c.flag_dst = reinterpret_cast<uint32_t*>(r.flag_dst);
+                        any = true;
+                    } else if (r.op.kind == foil::OpKind::Matmul && c.Mt == 0) {
+                        c.a = reinterpret_cast<const uint16_t*>(r.p0);
+                        c.b = reinterpret_cast<const uint16_t*>(r.p1);
+                        c.c = reinterpret_cast<uint16_t*>(r.po);
+                        c.Mt = r.op.Mt;
+                        c.Kt = r.op.Kt;
+                        c.Nt = r.op.Nt;
+                        if (r.gate) c.gate = reinterpret_cast<const uint32_t*>(r.gate);
+                    } else {
+                        plain = false;
+                    }
+                }
+                if (c.gate || any || (plain && c.Mt)) {
+                    if (!plain)
+                        throw FoilError(FOIL_ERR_UNSUPPORTED, "tt-foil: a core that waits or forwards runs one matmul");
+                    for (size_t j = 0; j < ops.size(); ++j)
+                        if (ops[j].k == kernels[i]) in_cluster[j] = true;
+                    cores.push_back(c);
+                    core_kernel.push_back(kernels[i]);
+                }
             }
-            any_gate |= r.gate != nullptr;
+            if (cores.size() > foil::gemm::kMaxCores)
+                throw FoilError(FOIL_ERR_UNSUPPORTED, "tt-foil: at most 8 cores that wait on each other per execute");
+            uint32_t* status = d->err_word + 16;  // per-core gate status (bytes 64 .. 95 of the word block)
+            cuda_check(cudaMemsetAsync(status, 0, 4 * foil::gemm::kMaxCores, d->stream), "clear core status");
+            const auto left = std::chrono::duration_cast<std::chrono::nanoseconds>(
+                deadline - std::chrono::steady_clock::now());
+            const uint64_t gate_ns = left.count() > 0 ? (uint64_t)left.count() : 1u;
+            throw_status(foil::gemm::launch_cores(cores.data(), (uint32_t)cores.size(), d->err_word, status, gate_ns,
+                                                  d->stream));
+            for (size_t j = 0; j < ops.size(); ++j)
+                if (!in_cluster[j]) run_op(d, ops[j]);
+            // The device-side gate wait ends by the deadline; allow the launch
+            // a grace period beyond it before the host gives up.
+            wait_stream(d, deadline + std::chrono::seconds(2), kernels[0]->core_x, kernels[0]->core_y);
+            uint32_t st[foil::gemm::kMaxCores] = {};
+            cuda_check(cudaMemcpy(st, status, sizeof st, cudaMemcpyDeviceToHost), "read core status");
+            for (size_t i = 0; i < cores.size(); ++i)
+                if (st[i]) {
+                    cudaMemsetAsync(d->err_word, 0, 4, d->stream);
+                    cudaStreamSynchronize(d->stream);
+                    throw FoilError(FOIL_ERR_TIMEOUT, "tt-foil: timeout waiting for kernel completion on core (" +
+                                                          std::to_string(core_kernel[i]->core_x) + "," +
+                                                          std::to_string(core_kernel[i]->core_y) +
+                                                          "): ready flag never set");
+                }
+            check_error_word(d);
+            return;
         }
-        // 3. Gated consumers proceed only once their ready flag is set, as the
-        //    reference consumer spins on it (reader_consumer.cpp:40-44); a flag
-        //    that nobody sets ends in the same timeout error.
-        if (any_gate) {
-            for (auto& r : ops) {
-                if (!r.gate) continue;
-                uint32_t flag = 0;
-                cuda_check(cudaMemcpyAsync(&flag, r.gate, 4, cudaMemcpyDeviceToHost, d->stream), "flag read");
-                wait_stream(d, deadline, r.k->core_x, r.k->core_y);
-                if (flag == 0)
-                    throw FoilError(FOIL_ERR_TIMEOUT,
-                                    "tt-foil: timeout waiting for kernel completion on core (" +
-                                        std::to_string(r.k->core_x) + "," + std::to_string(r.k->core_y) +
-                                        "): ready flag never set");
-            }
-        }
-        // 4. Compute launches.
+        // 3. Compute launches.
         for (auto& r : ops) run_op(d, r);
-        // 5. Bounded wait, then the device error word.
+        // 4. Bounded wait, then the device error word.
         wait_stream(d, deadline, kernels[0]->core_x, kernels[0]->core_y);
         check_error_word(d);
     });
@@ -862,6 +907,56 @@ extern "C" int foil_conv2d_nhwc_dev(const uint16_t* x, const uint16_t* w, const 
         uint32_t* err = error_word_for_current_device();
         throw_status(foil::conv::launch(x, w, bias, y, N, H, W, Cin, Cout, KH, KW, stride, pad, relu, err,
                                         (cudaStream_t)stream, sm_count_current()));
+    });
+}
+
+// ----------------------------------- conv in the reference's convention ---
+extern "C" int foil_conv2d_chw_dev(const uint16_t* x, const uint16_t* w, const uint16_t* bias, uint16_t* y,
+                                   uint32_t N, uint32_t Cin, uint32_t H, uint32_t W, uint32_t Cout, uint32_t KH,
+                                   uint32_t KW, uint32_t stride, uint32_t pad, int32_t relu, void* stream) {
+    return guarded([&] {
+        if (N == 0 || Cout == 0) return;
+        if (Cin == 0 || H == 0 || W == 0 || KH == 0 || KW == 0 || stride == 0 || KH > 16 || KW > 16 ||
+            stride > 16 || pad >= KH || pad >= KW || H + 2 * pad < KH || W + 2 * pad < KW)
+            throw FoilError(FOIL_ERR_INVALID, "foil_conv2d_chw_dev: unsupported kernel / stride / padding");
+        if (!x || !w || !y) throw FoilError(FOIL_ERR_INVALID, "foil_conv2d_chw_dev: null pointer");
+        const uint64_t Ho = (H + 2 * pad - KH) / stride + 1, Wo = (W + 2 * pad - KW) / stride + 1;
+        const uint32_t cin_p = (Cin + 15u) / 16u * 16u, cout_p = (Cout + 15u) / 16u * 16u;
+        const uint64_t hw = (uint64_t)H * W, howo = Ho * Wo, k = (uint64_t)KH * KW;
+        if (N > 65535 || Cout > 65535 || hw >= (1ull << 31) || (uint64_t)N * hw * cin_p >= (1ull << 40) ||
+            (uint64_t)N * howo >= (1ull << 31))
+            throw FoilError(FOIL_ERR_INVALID, "foil_conv2d_chw_dev: tensor too large");
+        auto up = [](uint64_t b) { return (b + 255u) / 256u * 256u; };
+        const uint64_t bx = up((uint64_t)N * hw * cin_p * 2), bw = up((uint64_t)cout_p * k * cin_p * 2),
+                       bb = up((uint64_t)cout_p * 2), by = up((uint64_t)N * howo * cout_p * 2);
+        cudaStream_t s = (cudaStream_t)stream;
+        char* ws = nullptr;
+        if (cudaMallocAsync((void**)&ws, bx + bw + bb + by, s) != cudaSuccess) {
+            cudaGetLastError();
+            throw FoilError(FOIL_ERR_OOM, "foil_conv2d_chw_dev: out of device memory for the re-laid operands");
+        }
+        struct Free {
+            char* p;
+            cudaStream_t s;
+            ~Free() { cudaFreeAsync(p, s); }
+        } release{ws, s};
+        uint16_t* xn = reinterpret_cast<uint16_t*>(ws);
+        uint16_t* wn = reinterpret_cast<uint16_t*>(ws + bx);
+        uint16_t* bn = reinterpret_cast<uint16_t*>(ws + bx + bw);
+        uint16_t* yn = reinterpret_cast<uint16_t*>(ws + bx + bw + bb);
+        // x (N, Cin, H W) -> (N, H W, Cin_p); w (Cout, Cin, KH KW) -> (Cout_p, KH KW, Cin_p);
+        // zero-padded channels contribute nothing.
+        throw_status(foil::transpose_u16(x, xn, N, Cin, (uint32_t)hw, N, (uint32_t)hw, cin_p, s));
+        throw_status(foil::transpose_u16(w, wn, Cout, Cin, (uint32_t)k, cout_p, (uint32_t)k, cin_p, s));
+        if (bias) {
+            cuda_check(cudaMemsetAsync(bn, 0, (size_t)cout_p * 2, s), "clear bias");
+            cuda_check(cudaMemcpyAsync(bn, bias, (size_t)Cout * 2, cudaMemcpyDeviceToDevice, s), "copy bias");
+        }
+        uint32_t* err = error_word_for_current_device();
+        throw_status(foil::conv::launch(xn, wn, bias ? bn : nullptr, yn, N, H, W, cin_p, cout_p, KH, KW, stride,
+                                        pad, relu, err, s, sm_count_current()));
+        // y (N, Ho Wo, Cout_p) -> (N, Cout, Ho Wo)
+        throw_status(foil::transpose_u16(yn, y, N, (uint32_t)howo, cout_p, N, Cout, (uint32_t)howo, s));
     });
 }
 

@@ -205,9 +205,11 @@ __device__ __forceinline__ void store_tile_row(const Params& p, uint32_t t_row, 
     }
 }
 
-__global__ void __launch_bounds__(kThreads, 1)
-gemm_tiles_kernel(const Params p) {
-    extern __shared__ uint8_t smem_raw[];
+// The single-SM GEMM as a device function: CTA `cta` of `ncta` (persistent
+// over the tiles), kThreads threads, kSmemBytes of dynamic shared memory at
+// smem_raw.  gemm_tiles_kernel runs it as block blockIdx.x of gridDim.x; the
+// multi-core dispatch kernel (below) runs it on one CTA of a cluster.
+__device__ __forceinline__ void gemm_tiles_body(const Params& p, uint32_t cta, uint32_t ncta, uint8_t* smem_raw) {
     uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) &
                                                ~uintptr_t(1023));
     uint64_t* full = reinterpret_cast<uint64_t*>(smem + kStages * kStageBytes);
@@ -258,7 +260,7 @@ gemm_tiles_kernel(const Params p) {
         const char* a_g = reinterpret_cast<const char*>(p.a);
         const char* b_g = reinterpret_cast<const char*>(p.b);
         uint32_t stage = 0, phase = 0;
-        for (uint32_t tile = blockIdx.x; tile < num_tiles; tile += gridDim.x) {
+        for (uint32_t tile = cta; tile < num_tiles; tile += ncta) {
             uint32_t mb, nb;
             tile_coords(tile, p.m_blocks, p.n_blocks, mb, nb);
             bool ok = true;
@@ -313,7 +315,7 @@ gemm_tiles_kernel(const Params p) {
             constexpr uint64_t b_base = smem_desc_base(512, 256);  // MN-major SW32
             uint32_t stage = 0, phase = 0, acc = 0, acc_phase = 0;
             bool ok = true;
-            for (uint32_t tile = blockIdx.x; ok && tile < num_tiles; tile += gridDim.x) {
+            for (uint32_t tile = cta; ok && tile < num_tiles; tile += ncta) {
                 if (!mbar_wait(&tempty[acc], acc_phase ^ 1u, abort_flag, p.err, p.wait_ns)) break;
                 tc_fence_after();
                 const uint32_t d_tmem = tmem_base + acc * kBN;
@@ -357,7 +359,7 @@ gemm_tiles_kernel(const Params p) {
         // ---------------------------------------------------- epilogue
         const uint32_t q = warp & 3u;  // TMEM lane quadrant this warp may access
         uint32_t acc = 0, acc_phase = 0;
-        for (uint32_t tile = blockIdx.x; tile < num_tiles; tile += gridDim.x) {
+        for (uint32_t tile = cta; tile < num_tiles; tile += ncta) {
             uint32_t mb, nb;
             tile_coords(tile, p.m_blocks, p.n_blocks, mb, nb);
             // One lane waits; the warp then proceeds converged (tcgen05.ld is
@@ -390,6 +392,137 @@ gemm_tiles_kernel(const Params p) {
                      "r"(kTmemCols)
                      : "memory");
     }
+}
+
+__global__ void __launch_bounds__(kThreads, 1)
+gemm_tiles_kernel(const Params p) {
+    extern __shared__ uint8_t smem_raw[];
+    gemm_tiles_body(p, blockIdx.x, gridDim.x, smem_raw);
+}
+
+// ============================================== multi-core dispatch kernel ===
+// One CTA per logical core of an execute (CoreProgram), all CTAs of one
+// cluster, hence resident together: a consumer core may wait for a flag that
+// a producer core of the same launch sets.  Replaces the reference's
+// fire-all-then-poll dispatch of several core kernels (src/dispatch.cpp:
+// 223-274) for programs that talk to each other, here the matmul_2core_mcast
+// producer / consumer pair (examples/matmul_2core_mcast/kernels/
+// reader_producer.cpp:60-82, reader_consumer.cpp:38-44).
+struct CoreLaunch {
+    CoreProgram core[kMaxCores];
+    Params gemm[kMaxCores];  // the GEMM of core i (Mt = 0: none)
+    uint32_t* err;
+    uint32_t* status;
+    uint64_t gate_wait_ns;
+};
+
+// Bounded acquire poll of a flag in global memory: true once it is nonzero,
+// false after limit_ns.
+__device__ __forceinline__ bool wait_flag_acquire(const uint32_t* flag, uint64_t limit_ns) {
+    const uint64_t t0 = global_ns();
+#pragma unroll 1
+    while (true) {
+        uint32_t v;
+        asm volatile("ld.acquire.gpu.global.u32 %0, [%1];" : "=r"(v) : "l"(flag) : "memory");
+        if (v != 0u) return true;
+        if (global_ns() - t0 > limit_ns) return false;
+        __nanosleep(256);
+    }
+}
+
+__device__ __forceinline__ void copy_block16(const void* src, void* dst, uint64_t bytes) {
+    const uint4* s = static_cast<const uint4*>(src);
+    uint4* d = static_cast<uint4*>(dst);
+    for (uint64_t i = threadIdx.x; i < bytes / 16u; i += blockDim.x) d[i] = s[i];
+}
+
+__global__ void __launch_bounds__(kThreads, 1) cores_kernel(const __grid_constant__ CoreLaunch L) {
+    extern __shared__ uint8_t smem_raw[];
+    __shared__ uint32_t go;
+    const CoreProgram& c = L.core[blockIdx.x];
+    if (threadIdx.x == 0) {
+        const bool ok = c.gate == nullptr || wait_flag_acquire(c.gate, L.gate_wait_ns);
+        if (!ok) {
+            atomicOr(L.err, kErrWaitTimeout);
+            L.status[blockIdx.x] = 1u;
+        }
+        go = ok ? 1u : 0u;
+    }
+    __syncthreads();
+    if (!go) return;
+    if (c.fwd_bytes) {
+        // Stage, forward to the peer core, then publish its flag: the flag's
+        // release store orders every thread's copies (joined by the CTA
+        // barrier and made GPU-visible by the fence) before it.
+        copy_block16(c.fwd_src, c.fwd_stage, c.fwd_bytes);
+        __syncthreads();
+        copy_block16(c.fwd_stage, c.fwd_peer, c.fwd_bytes);
+        __syncthreads();
+        if (threadIdx.x == 0) {
+            __threadfence();
+            const uint32_t v = *reinterpret_cast<const volatile uint32_t*>(c.flag_src);
+            asm volatile("st.release.gpu.global.u32 [%0], %1;" ::"l"(c.flag_dst), "r"(v) : "memory");
+        }
+        __syncthreads();
+    }
+    if (c.Mt) gemm_tiles_body(L.gemm[blockIdx.x], 0, 1, smem_raw);
+}
+
+int launch_cores(const CoreProgram* cores, uint32_t ncores, uint32_t* err, uint32_t* core_status,
+                 uint64_t gate_wait_ns, cudaStream_t stream) {
+    if (ncores == 0 || ncores > kMaxCores) {
+        foil_set_error(FOIL_ERR_INVALID, "tt-foil: multi-core execute takes 1 to 8 cores");
+        return FOIL_ERR_INVALID;
+    }
+    if (foil_smem_optin((const void*)cores_kernel, kSmemBytes) != cudaSuccess) {
+        foil_set_error(FOIL_ERR_CUDA, "tt-foil: cudaFuncSetAttribute failed (multi-core execute)");
+        return FOIL_ERR_CUDA;
+    }
+    CoreLaunch L;
+    memset(&L, 0, sizeof L);
+    for (uint32_t i = 0; i < ncores; ++i) {
+        L.core[i] = cores[i];
+        Params& p = L.gemm[i];
+        p.a = cores[i].a;
+        p.b = cores[i].b;
+        p.c = cores[i].c;
+        p.bias = nullptr;
+        p.Mt = cores[i].Mt;
+        p.Kt = cores[i].Kt;
+        p.Nt = cores[i].Nt;
+        p.m_blocks = (p.Mt + 3) / 4;
+        p.n_blocks = (p.Nt + 7) / 8;
+        p.relu = 0;
+        p.err = err;
+        p.wait_ns = foil_wait_limit_ns();
+        p.npeers = 0;
+        p.wide_stores = ((uintptr_t)p.c & 31u) == 0 ? 1u : 0u;
+    }
+    L.err = err;
+    L.status = core_status;
+    L.gate_wait_ns = gate_wait_ns;
+    cudaLaunchConfig_t cfg;
+    memset(&cfg, 0, sizeof cfg);
+    cfg.gridDim = dim3(ncores, 1, 1);
+    cfg.blockDim = dim3(kThreads, 1, 1);
+    cfg.dynamicSmemBytes = kSmemBytes;
+    cfg.stream = stream;
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeClusterDimension;
+    attr[0].val.clusterDim.x = ncores;
+    attr[0].val.clusterDim.y = 1;
+    attr[0].val.clusterDim.z = 1;
+    cfg.attrs = attr;
+    cfg.numAttrs = 1;
+    if (cudaLaunchKernelEx(&cfg, cores_kernel, L) != cudaSuccess) {
+        char buf[256];
+        snprintf(buf, sizeof buf, "tt-foil: multi-core execute launch failed: %s",
+                 cudaGetErrorString(cudaGetLastError()));
+        foil_set_error(FOIL_ERR_CUDA, buf);
+        return FOIL_ERR_CUDA;
+    }
+    foil_count_launch();
+    return FOIL_OK;
 }
 
 // ============================================================ 2-SM kernel ===

@@ -19,5 +19,34 @@ int launch(const uint16_t* a, const uint16_t* b, uint16_t* c, uint32_t Mt, uint3
            uint32_t Nt, const uint16_t* bias, int relu, uint32_t* err, cudaStream_t stream,
            int max_ctas, uint16_t* const* peer_c = nullptr, uint32_t npeers = 0);
 
+// One "core" of a multi-core execute: the work one logical core's program
+// does, run by one CTA of a single cluster launch in which every core's CTA
+// is resident at the same time, so cores may wait on each other's flags.
+// In order: (1) if `gate` is set, wait (bounded) until *gate != 0;
+// (2) if fwd_bytes, copy fwd_src -> fwd_stage -> fwd_peer and then publish
+// *flag_dst = *flag_src with release semantics (after the copies); (3) if
+// Mt, the tiled GEMM c = a . b (Mt x Kt x Nt tiles).
+struct CoreProgram {
+    const uint32_t* gate;
+    const void* fwd_src;
+    void* fwd_stage;
+    void* fwd_peer;
+    uint64_t fwd_bytes;
+    const uint32_t* flag_src;
+    uint32_t* flag_dst;
+    const uint16_t* a;
+    const uint16_t* b;
+    uint16_t* c;
+    uint32_t Mt, Kt, Nt;
+};
+constexpr uint32_t kMaxCores = 8;
+
+// Launch `ncores` (<= kMaxCores) core programs as one cluster of ncores CTAs
+// on `stream`.  A gate wait that runs out after `gate_wait_ns` sets
+// kErrWaitTimeout in *err and 1 in core_status[core] (device words, cleared
+// by the caller), and that core does nothing else.  Returns a foil_status.
+int launch_cores(const CoreProgram* cores, uint32_t ncores, uint32_t* err, uint32_t* core_status,
+                 uint64_t gate_wait_ns, cudaStream_t stream);
+
 }  // namespace gemm
 }  // namespace foil

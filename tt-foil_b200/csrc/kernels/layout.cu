@@ -9,6 +9,7 @@
 // index is XOR-swizzled so that every 8-lane phase of a 16-byte access hits 8
 // distinct 4-bank groups (conflict-free on both sides).
 #include "common.cuh"
+#include "layout.cuh"
 #include "../../../include/foil_c.h"
 
 namespace foil {
@@ -148,3 +149,44 @@ extern "C" int foil_untilize_dev(const uint16_t* tiles, uint16_t* row_major,
         (const uint4*)tiles, (uint4*)row_major, rows, cols);
     return check_launch("foil_untilize_dev");
 }
+
+// ---------------------------------------------------- batched transpose ---
+// 32 x 32 element tiles through shared memory (padded rows: no bank
+// conflicts on the column reads); reads and writes are 64-byte warp rows.
+namespace foil {
+namespace {
+__global__ void __launch_bounds__(256)
+transpose_u16_kernel(const uint16_t* __restrict__ in, uint16_t* __restrict__ out, uint32_t in_batch,
+                     uint32_t in_rows, uint32_t in_cols, uint32_t out_rows, uint32_t out_cols) {
+    __shared__ uint16_t t[32][34];
+    const uint32_t b = blockIdx.z, i0 = blockIdx.x * 32u, j0 = blockIdx.y * 32u;
+    const uint32_t tx = threadIdx.x, ty = threadIdx.y;
+#pragma unroll
+    for (uint32_t k = 0; k < 4; ++k) {
+        const uint32_t i = i0 + ty + 8u * k, j = j0 + tx;
+        uint16_t v = 0;
+        if (b < in_batch && i < in_rows && j < in_cols) v = in[((uint64_t)b * in_rows + i) * in_cols + j];
+        t[ty + 8u * k][tx] = v;
+    }
+    __syncthreads();
+#pragma unroll
+    for (uint32_t k = 0; k < 4; ++k) {
+        const uint32_t j = j0 + ty + 8u * k, i = i0 + tx;
+        if (j < out_rows && i < out_cols) out[((uint64_t)b * out_rows + j) * out_cols + i] = t[tx][ty + 8u * k];
+    }
+}
+}  // namespace
+
+int transpose_u16(const uint16_t* in, uint16_t* out, uint32_t in_batch, uint32_t in_rows, uint32_t in_cols,
+                  uint32_t out_batch, uint32_t out_rows, uint32_t out_cols, cudaStream_t stream) {
+    if (out_batch == 0 || out_rows == 0 || out_cols == 0) return FOIL_OK;
+    if (out_batch > 65535u) {
+        foil_set_error(FOIL_ERR_INVALID, "transpose: batch too large");
+        return FOIL_ERR_INVALID;
+    }
+    const dim3 grid((out_cols + 31u) / 32u, (out_rows + 31u) / 32u, out_batch);
+    transpose_u16_kernel<<<grid, dim3(32, 8), 0, stream>>>(in, out, in_batch, in_rows, in_cols, out_rows, out_cols);
+    return check_launch("transpose");
+}
+
+}  // namespace foil

@@ -114,6 +114,8 @@ SIGNATURES = {
     "foil_peer_close": (ctypes.c_int, [ctypes.c_int32, _P]),
     "foil_peer_free": (ctypes.c_int, [ctypes.c_int32, _P]),
     "foil_set_wait_limit_ns": (ctypes.c_uint64, [ctypes.c_uint64]),
+    "foil_conv2d_chw_dev": (ctypes.c_int, [_U16P, _U16P, _U16P, _U16P] + [ctypes.c_uint32] * 9 +
+                            [ctypes.c_int32, _P]),
 }
 
 # Bits of the device error word (include/foil_c.h FOIL_DEVERR_*).
@@ -247,6 +249,13 @@ def conv2d_nhwc(x, w, bias, y, N, H, W, Cin, Cout, KH, KW, stride, pad, relu=Fal
     """y (N,Ho,Wo,Cout) = relu?(conv(x (N,H,W,Cin), w (Cout,KH,KW,Cin)) + bias)."""
     check(lib().foil_conv2d_nhwc_dev(_ptr(x), _ptr(w), _ptr(bias), _ptr(y), N, H, W, Cin, Cout, KH,
                                      KW, stride, pad, 1 if relu else 0, _stream(stream)))
+
+
+def conv2d_chw(x, w, bias, y, N, Cin, H, W, Cout, KH, KW, stride, pad, relu=False, stream=None):
+    """The reference's convention: y (N,Cout,Ho,Wo) = relu?(conv(x (N,Cin,H,W),
+    w (Cout, Cin*KH*KW)) + bias), operands re-laid on the device."""
+    check(lib().foil_conv2d_chw_dev(_ptr(x), _ptr(w), _ptr(bias), _ptr(y), N, Cin, H, W, Cout, KH, KW, stride,
+                                    pad, 1 if relu else 0, _stream(stream)))
 
 
 def matmul_tiles_host(device, a, b, c, Mt, Kt, Nt, bias=None, relu=False, chunk_rows=0):
