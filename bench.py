@@ -12,6 +12,10 @@ itself, followed by a one-element all-reduce.
 
 value      TFLOP/s over all ranks, operands resident in HBM, CUDA events on the
            launching stream, max over ranks.
+value_with_gather  (N > 1) the same step with the global C reassembled on every
+           rank: the better of GEMM + ncclAllGather and the fused GEMM that
+           stores each tile to every rank's copy over NVLink, with the achieved
+           NVLink GB/s against the link floor.
 e2e        TFLOP/s of the same GEMM on host buffers through the public entry
            point foil_matmul_tiles_host (pinned A, B in; C out; copies of
            chunk i+1 and read-back of chunk i-1 overlap the GEMM of chunk i)
@@ -72,6 +76,7 @@ def parse():
     ap.add_argument("--cpu-seconds", type=float, default=12.0)
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--no-secondary", action="store_true")
+    ap.add_argument("--no-e2e", action="store_true")
     return ap.parse_args()
 
 
@@ -377,16 +382,37 @@ def run_ours(args, dist):
                 "traffic": traffic,
                 "algorithmic_bytes": 2.0 * (M_PER_GPU * K_DIM + K_DIM * N_DIM + M_PER_GPU * N_DIM)}
 
-    # All-gather of the C shards (reassembly of the global tile-layout C).
+    # All-gather of the C shards (reassembly of the global tile-layout C), and
+    # the headline with it: the better of GEMM + ncclAllGather and the fused
+    # GEMM that stores every tile to all ranks' copies itself.
     allgather = None
+    with_gather = None
     if dist.world > 1:
         allgather = time_allgather(dist, c, ms / args.steps, flops)
         try:
             allgather["fused"] = time_fused_gather(dist, a, b, Mt, Kt, Nt, flops)
         except RuntimeError as e:  # raised on every rank alike (see GatheredTiles)
             allgather["fused"] = {"unavailable": str(e)[:300]}
+        shard_bytes = M_PER_GPU * N_DIM * 2
+        recv = (dist.world - 1) * shard_bytes  # C bytes every GPU must receive per step
+        link_gbs = 770.0  # measured peer copy per direction per GPU on this pool
+        nccl_ms = ms / args.steps + allgather["ms"]
+        fused = allgather["fused"]
+        fused_ms = fused.get("ms_per_step") if "ms_per_step" in fused else None
+        best = "fused" if fused_ms is not None and fused_ms < nccl_ms else "ncclAllGather"
+        step_ms = fused_ms if best == "fused" else nccl_ms
+        with_gather = {
+            "value": dist.world * flops / (step_ms / 1e3) / 1e12, "unit": "TFLOP/s", "ms_per_step": step_ms,
+            "path": best, "nccl_ms_per_step": nccl_ms, "fused_ms_per_step": fused_ms,
+            "received_bytes_per_gpu": recv,
+            "nvlink_GBps_fused": recv / (fused_ms / 1e3) / 1e9 if fused_ms else None,
+            "allgather_busbw_GBps": allgather["busbw_GBps"],
+            "link_floor_ms": recv / (link_gbs * 1e9) * 1e3,
+            "compute_floor_ms": ms / args.steps,
+            "note": "per step: the GEMM of every rank's 8192-row shard plus reassembly of the whole C on "
+                    "every rank; floor = max(compute, received bytes at 770 GB/s per direction)"}
 
-    e2e = run_e2e(args, dist, flops)
+    e2e = None if args.no_e2e else run_e2e(args, dist, flops)
 
     secondary = None if args.no_secondary else run_secondary(dist, pk)
 
@@ -406,6 +432,7 @@ def run_ours(args, dist):
                 "gpu_launches": launches, "parity_spot_check": check, "secondary": secondary}
         if allgather:
             line["allgather"] = allgather
+            line["value_with_gather"] = with_gather
         print(json.dumps(line), flush=True)
 
 
