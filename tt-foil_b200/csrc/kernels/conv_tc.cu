@@ -602,25 +602,10 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
             tma_prefetch_map(&tmap_x);
             tma_prefetch_map(&tmap_w);
             const uint32_t lead_full0 = map_to_rank(&full[0], 0);
-            // Resident weights: rows [rank * BN/2, (rank + 1) * BN/2) of the
-            // K x Cout weight matrix, one box per k-block.
+            // Resident weights, once, in one copy: output channels [rank BN/2,
+            // (rank + 1) BN/2) of all k-blocks (see encode_weight_map3).
             if (leader) mbar_expect_tx(bfull, 2u * p.num_kb * PC::kHalfB);
-            {
-                const uint32_t lead_bfull = map_to_rank(bfull, 0);
-                uint32_t kh = 0, kw = 0, cb = 0;
-                for (uint32_t kb = 0; kb < p.num_kb; ++kb) {
-                    tma_load_2d_pair(smem_u32(b_res) + kb * PC::kHalfB, &tmap_w,
-                                     (int32_t)((kh * p.KW + kw) * p.Cin + cb * 64u), (int32_t)(rank * (BN / 2)),
-                                     lead_bfull);
-                    if (++cb == p.cblocks) {
-                        cb = 0;
-                        if (++kw == p.KW) {
-                            kw = 0;
-                            ++kh;
-                        }
-                    }
-                }
-            }
+            tma_load_3d_pair(smem_u32(b_res), &tmap_w, 0, (int32_t)(rank * (BN / 2)), 0, map_to_rank(bfull, 0));
             const uint32_t hw = p.Ho * p.Wo;
             uint32_t stage = 0, phase = 0, issued = 0;
             bool ok = true;
@@ -890,13 +875,12 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
             tma_prefetch_map(&tmap_x0);
             tma_prefetch_map(&tmap_x1);
             tma_prefetch_map(&tmap_w);
-            // Resident weights, once: rows [rank BN/2, (rank + 1) BN/2) of the
-            // K x Cout weight matrix, one box per k-block.
+            // Resident weights, once, in ONE copy: output channels [rank BN/2,
+            // (rank + 1) BN/2) of all num_kb k-blocks (a 3-D box over (64
+            // channels, Cout, k-block) lands k-block-major, each k-block a
+            // K-major SWIZZLE_128B block of BN/2 rows).
             if (leader) mbar_expect_tx(bfull, 2u * p.num_kb * PC::kHalfB);
-            const uint32_t lead_bfull = map_to_rank(bfull, 0);
-            for (uint32_t kb = 0; kb < p.num_kb; ++kb)
-                tma_load_2d_pair(smem_u32(b_res) + kb * PC::kHalfB, &tmap_w, (int32_t)(kb * 64u),
-                                 (int32_t)(rank * (BN / 2)), lead_bfull);
+            tma_load_3d_pair(smem_u32(b_res), &tmap_w, 0, (int32_t)(rank * (BN / 2)), 0, map_to_rank(bfull, 0));
             const uint32_t lead_full0 = map_to_rank(&full[0], 0), slot0 = smem_u32(slots);
             uint32_t slot = 0, phase = 0, issued = 0;
             bool ok = true;
@@ -1273,6 +1257,21 @@ static bool encode_output_map(const Params& p, CUtensorMap* my) {
 
 static bool encode_weight_map(const Params& p, uint32_t w_rows, CUtensorMap* mw);
 
+// All weights of one CTA in one box: the K x Cout weight matrix viewed as
+// (64 channels, Cout, num_kb k-blocks) with byte strides (K * 2, 128), box
+// (64, w_rows, num_kb), SWIZZLE_128B: the box lands k-block-major.
+static bool encode_weight_map3(const Params& p, uint32_t w_rows, CUtensorMap* mw) {
+    const Encoders& e = encoders();
+    if (!e.tiled || p.num_kb > 256) return false;
+    const cuuint64_t dim[3] = {64, p.Cout, p.num_kb};
+    const cuuint64_t str[2] = {(cuuint64_t)p.KH * p.KW * p.Cin * 2, 128};
+    const cuuint32_t box[3] = {64, w_rows, p.num_kb};
+    const cuuint32_t one[3] = {1, 1, 1};
+    return e.tiled(mw, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 3, const_cast<uint16_t*>(p.w), dim, str, box, one,
+                   CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+                   CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
+}
+
 // im2col map of the plane kernel's copies: `pixels` output positions per
 // copy, 64 channels, traversal stride = the conv stride, and the bounding
 // box of base pixels [-pad, dim - 1 + pad - (k - 1)] extended below the last
@@ -1386,7 +1385,7 @@ int launch(const uint16_t* x, const uint16_t* w, const uint16_t* bias, uint16_t*
         uint32_t smem = 0;
         if (plane_geometry(p, bn, (uint32_t)optin, g, smem)) {
             alignas(64) CUtensorMap mx1;
-            if (!encode_weight_map(p, (uint32_t)bn / 2, &mw) || !encode_plane_map(p, g, g.e_map[0], &mx) ||
+            if (!encode_weight_map3(p, (uint32_t)bn / 2, &mw) || !encode_plane_map(p, g, g.e_map[0], &mx) ||
                 !encode_plane_map(p, g, g.e_map[1], &mx1)) {
                 foil_set_error(FOIL_ERR_CUDA, "foil_conv2d_nhwc: tensor-map encoding failed");
                 return FOIL_ERR_CUDA;
@@ -1420,7 +1419,8 @@ int launch(const uint16_t* x, const uint16_t* w, const uint16_t* bias, uint16_t*
                       (strcmp(producer_override(), "pair") == 0 ||
                        (p.num_kb >= 4 && p.m_blocks >= (uint32_t)max_ctas));
     const uint32_t sub = bn <= 128 ? 2u : 1u;
-    if (!encode_maps(p, pair ? (uint32_t)bn / 2 : (uint32_t)bn, pair ? 128u * sub : 128u, &mx, &mw)) {
+    if (!encode_maps(p, pair ? (uint32_t)bn / 2 : (uint32_t)bn, pair ? 128u * sub : 128u, &mx, &mw) ||
+        (pair && !encode_weight_map3(p, (uint32_t)bn / 2, &mw))) {
         foil_set_error(FOIL_ERR_CUDA, "foil_conv2d_nhwc: tensor-map encoding failed");
         return FOIL_ERR_CUDA;
     }

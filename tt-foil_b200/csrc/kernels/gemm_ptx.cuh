@@ -204,6 +204,16 @@ __device__ __forceinline__ void tma_load_2d_pair(uint32_t dst, const void* map, 
         : "memory");
 }
 
+// 3-D tiled load, pair form (see tma_load_2d_pair).
+__device__ __forceinline__ void tma_load_3d_pair(uint32_t dst, const void* map, int32_t x, int32_t y, int32_t z,
+                                                 uint32_t bar_cluster) {
+    asm volatile(
+        "cp.async.bulk.tensor.3d.cta_group::2.shared::cluster.global.mbarrier::complete_tx::bytes"
+        " [%0], [%1, {%2, %3, %4}], [%5];" ::"r"(dst),
+        "l"(reinterpret_cast<uint64_t>(map)), "r"(x), "r"(y), "r"(z), "r"(bar_cluster)
+        : "memory");
+}
+
 __device__ __forceinline__ void tma_load_im2col_4d_pair(uint32_t dst, const void* map, int32_t c,
                                                         int32_t w, int32_t h, int32_t n, uint16_t off_w,
                                                         uint16_t off_h, uint32_t bar_cluster) {
