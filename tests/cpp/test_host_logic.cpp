@@ -2,7 +2,8 @@
 // allocators (reference src/device.cpp:38-58, src/buffer.cpp:11-35), the
 // 64-bit address packing (src/noc_addr.cpp:10-22), program descriptors,
 // CB validation (src/cb_config.cpp:46-64) and runtime-argument planning for
-// every program of the accelerated path.  Prints PASS and returns 0.
+// every program of the accelerated path and of the scalar dispatch examples.
+// Prints PASS and returns 0.
 #include <cstdio>
 #include <cstdlib>
 #include <string>
@@ -82,8 +83,15 @@ static void test_descriptors() {
               resolve_program({parse_descriptor(desc("relu", "reader"), "x"),
                                parse_descriptor(desc("add_tiles", "writer"), "x")});
           }) == FOIL_ERR_INVALID);
-    CHECK(status_of([] { resolve_program({parse_descriptor(desc("add_two_numbers", "reader"), "x")}); }) ==
+    CHECK(status_of([] { resolve_program({parse_descriptor(desc("erisc_ping", "reader"), "x")}); }) ==
           FOIL_ERR_UNSUPPORTED);
+    CHECK(resolve_program({parse_descriptor(desc("add_two_numbers", "reader"), "x"),
+                           parse_descriptor(desc("add_two_numbers", "writer"), "x")}) ==
+          Program::AddTwoNumbers);
+    CHECK(resolve_program({parse_descriptor(desc("noc_passthrough", "reader", "consumer"), "x")}) ==
+          Program::NocConsumer);
+    CHECK(status_of([] { resolve_program({parse_descriptor(desc("noc_passthrough", "reader"), "x")}); }) ==
+          FOIL_ERR_INVALID);
     CHECK(status_of([] { resolve_program({}); }) == FOIL_ERR_INVALID);
     CHECK(role_of_risc(0) == Role::Reader && role_of_risc(1) == Role::Writer &&
           role_of_risc(4) == Role::Compute);
@@ -149,12 +157,53 @@ static void test_plans() {
           ops[0].out.bytes == 2048);
 }
 
+static void test_scalar_plans() {
+    std::array<std::vector<uint32_t>, 5> rta;
+    std::array<bool, 5> has{};
+    // add_two_numbers: BRISC [a, b, sum] -> Add; NCRISC [a, b, prod] -> Mul
+    CHECK(status_of([&] { plan_program(Program::AddTwoNumbers, 0, 0, rta, has); }) == FOIL_ERR_INVALID);
+    rta[0] = {0x20000, 0x20010, 0x20020};
+    has[0] = true;
+    auto ops = plan_program(Program::AddTwoNumbers, 0, 1, rta, has);
+    CHECK(ops.size() == 1 && ops[0].kind == OpKind::Word && ops[0].word == WordOp::Add &&
+          ops[0].in1.offset == 0x20010 && ops[0].out.offset == 0x20020 && ops[0].out.core_y == 1 &&
+          ops[0].out.bytes == 4);
+    rta[1] = {0x20000, 0x20010, 0x20030};
+    has[1] = true;
+    ops = plan_program(Program::AddTwoNumbers, 0, 0, rta, has);
+    CHECK(ops.size() == 2 && ops[1].word == WordOp::Mul && ops[1].out.offset == 0x20030);
+    rta[1] = {0x20000};
+    CHECK(status_of([&] { plan_program(Program::AddTwoNumbers, 0, 0, rta, has); }) == FOIL_ERR_INVALID);
+    has[1] = false;
+    // noc_passthrough producer: sum, sentinel, then send + flag
+    uint64_t sd = pack_addr(0, 1, 0x20040), fd = pack_addr(0, 1, 0x20050);
+    rta[0] = {0x20000, 0x20010, 0x20020, uint32_t(sd), uint32_t(sd >> 32), 0x20030, uint32_t(fd),
+              uint32_t(fd >> 32)};
+    ops = plan_program(Program::NocProducer, 0, 0, rta, has);
+    CHECK(ops.size() == 3 && ops[0].kind == OpKind::Word && ops[0].word == WordOp::Add &&
+          ops[0].out.offset == 0x20020);
+    CHECK(ops[1].kind == OpKind::Word && ops[1].word == WordOp::Set && ops[1].imm == kNocFlagValue &&
+          ops[1].out.offset == 0x20030);
+    CHECK(ops[2].kind == OpKind::Send && ops[2].in0.offset == 0x20020 && ops[2].out.core_y == 1 &&
+          ops[2].out.offset == 0x20040 && ops[2].flag_src.offset == 0x20030 &&
+          ops[2].flag_dst.offset == 0x20050 && ops[2].flag_dst.core_y == 1);
+    rta[0].pop_back();
+    CHECK(status_of([&] { plan_program(Program::NocProducer, 0, 0, rta, has); }) == FOIL_ERR_INVALID);
+    // noc_passthrough consumer: gated on the sentinel, result = sum * 2
+    rta[0] = {0x20050, 0x20040, 0x20060};
+    ops = plan_program(Program::NocConsumer, 0, 1, rta, has);
+    CHECK(ops.size() == 1 && ops[0].gated && ops[0].gate_value == kNocFlagValue &&
+          ops[0].gate_flag.offset == 0x20050 && ops[0].word == WordOp::Scale && ops[0].imm == 2 &&
+          ops[0].in0.offset == 0x20040 && ops[0].out.offset == 0x20060);
+}
+
 int main() {
     test_allocators();
     test_addresses();
     test_descriptors();
     test_cbs();
     test_plans();
+    test_scalar_plans();
     if (failures) {
         std::printf("test_host_logic: FAIL (%d)\n", failures);
         return 1;

@@ -262,9 +262,96 @@ def test_error_behaviour(tf):
             d.execute([])
 
 
+def scalar_bins(tf, program, *names):
+    d = os.path.join(tf.PROGRAMS_DIR, program)
+    risc = {"add_brisc.elf": tf.BRISC, "add_ncrisc.elf": tf.NCRISC, "producer.elf": tf.BRISC,
+            "consumer.elf": tf.BRISC}
+    return [(risc[n], os.path.join(d, n)) for n in names]
+
+
+def test_add_two_numbers_on_eight_cores(tf):
+    """examples/add_two_numbers on 8 cores in one execute: BRISC writes
+    a + b, NCRISC a * b (wrapping u32, like the RISC-V cores), each core
+    with its own operands; all cores are one launch."""
+    cores = [(x, y) for x in range(2) for y in range(4)]
+    rng = np.random.default_rng(21)
+    vals = rng.integers(0, 2**32, size=(len(cores), 2), dtype=np.uint64).astype(np.uint32)
+    vals[0] = [0xFFFFFFFF, 2]  # both results wrap
+    with tf.Device(0, cores=cores) as d:
+        ks, outs = [], []
+        for (x, y), (a, b) in zip(cores, vals):
+            ba, bb, bs, bp = (d.allocate(tf.LOC_L1, 4, (x, y)) for _ in range(4))
+            d.write_array(ba, np.array([a], np.uint32))
+            d.write_array(bb, np.array([b], np.uint32))
+            d.write_array(bs, np.zeros(1, np.uint32))
+            d.write_array(bp, np.zeros(1, np.uint32))
+            k = d.load_kernel(scalar_bins(tf, "add_two_numbers", "add_brisc.elf", "add_ncrisc.elf"), (x, y))
+            d.set_runtime_args(k, tf.BRISC, [ba.device_addr, bb.device_addr, bs.device_addr])
+            d.set_runtime_args(k, tf.NCRISC, [ba.device_addr, bb.device_addr, bp.device_addr])
+            ks.append(k)
+            outs.append((bs, bp))
+        launches = tf.launch_count()
+        d.execute(ks)
+        assert tf.launch_count() == launches + 1
+        for (bs, bp), (a, b) in zip(outs, vals):
+            assert d.read_array(bs, np.uint32, 1)[0] == np.uint32((int(a) + int(b)) & 0xFFFFFFFF)
+            assert d.read_array(bp, np.uint32, 1)[0] == np.uint32((int(a) * int(b)) & 0xFFFFFFFF)
+
+
+def noc_setup(tf, d, a, b):
+    cp, cc = (0, 0), (0, 1)
+    ba, bb, sum_s, flag_s = (d.allocate(tf.LOC_L1, 4, cp) for _ in range(4))
+    sum_d, flag_d, res = (d.allocate(tf.LOC_L1, 4, cc) for _ in range(3))
+    d.write_array(ba, np.array([a], np.uint32))
+    d.write_array(bb, np.array([b], np.uint32))
+    for buf in (sum_s, flag_s, sum_d, flag_d, res):
+        d.write_array(buf, np.zeros(1, np.uint32))
+    kp = d.load_kernel(scalar_bins(tf, "noc_passthrough", "producer.elf"), cp)
+    kc = d.load_kernel(scalar_bins(tf, "noc_passthrough", "consumer.elf"), cc)
+    sn = d.noc_unicast_addr(cc, sum_d.device_addr)
+    fn = d.noc_unicast_addr(cc, flag_d.device_addr)
+    d.set_runtime_args(kp, tf.BRISC, [ba.device_addr, bb.device_addr, sum_s.device_addr, tf.lo(sn), tf.hi(sn),
+                                      flag_s.device_addr, tf.lo(fn), tf.hi(fn)])
+    d.set_runtime_args(kc, tf.BRISC, [flag_d.device_addr, sum_d.device_addr, res.device_addr])
+    return kp, kc, dict(sum_s=sum_s, flag_s=flag_s, sum_d=sum_d, flag_d=flag_d, res=res)
+
+
+@pytest.mark.parametrize("consumer_first", [False, True])
+def test_noc_passthrough_program(tf, consumer_first):
+    """examples/noc_passthrough: the producer sends a + b to the consumer's
+    L1 and then the 0xCAFEBABE sentinel; the consumer waits (bounded, on the
+    device) for the sentinel and writes 2 (a + b).  One launch, either order."""
+    a, b = 0x9E3779B9, 0x7F4A7C15  # the sum wraps
+    with tf.Device(0, cores=[(0, 0), (0, 1)]) as d:
+        kp, kc, buf = noc_setup(tf, d, a, b)
+        launches = tf.launch_count()
+        d.execute([kc, kp] if consumer_first else [kp, kc])
+        assert tf.launch_count() == launches + 1
+        s = (a + b) & 0xFFFFFFFF
+        rd = lambda n: int(d.read_array(buf[n], np.uint32, 1)[0])
+        assert rd("res") == (2 * s) & 0xFFFFFFFF
+        assert rd("sum_s") == s and rd("sum_d") == s
+        assert rd("flag_s") == 0xCAFEBABE and rd("flag_d") == 0xCAFEBABE
+
+
+def test_noc_consumer_alone_times_out(tf):
+    """The consumer without its producer: the device-side wait for the
+    sentinel runs out at the execute's deadline, the execute fails with the
+    timeout status naming the core, the result stays unwritten, and the pair
+    then runs normally."""
+    with tf.Device(0, cores=[(0, 0), (0, 1)]) as d:
+        kp, kc, buf = noc_setup(tf, d, 5, 6)
+        with pytest.raises(tf.FoilError) as e:
+            d.execute([kc], timeout_ms=300)
+        assert e.value.status == 5 and "(0,1)" in str(e.value)
+        assert d.read_array(buf["res"], np.uint32, 1)[0] == 0
+        d.execute([kp, kc])
+        assert d.read_array(buf["res"], np.uint32, 1)[0] == 22
+
+
 def test_unsupported_program_rejected(tf, tmp_path):
     p = tmp_path / "reader.brisc.elf"
-    p.write_text("TTFOIL-B200-PROGRAM 1\nprogram=add_two_numbers\nrole=reader\n")
+    p.write_text("TTFOIL-B200-PROGRAM 1\nprogram=erisc_ping\nrole=reader\n")
     with tf.Device(0) as d:
         with pytest.raises(tf.FoilError) as e:
             d.load_kernel([(tf.BRISC, str(p))])

@@ -660,7 +660,9 @@ void run_op(foil_device* d, ResolvedOp& r) {
                                             sm_count_current()));
             break;
         case foil::OpKind::McastForward:
-            break;  // handled in the forward phase
+        case foil::OpKind::Word:
+        case foil::OpKind::Send:
+            break;  // run by the multi-core launch
     }
 }
 
@@ -704,23 +706,44 @@ extern "C" int foil_execute(foil_device* d, foil_kernel* const* kernels, size_t 
                         r.flag_src = loc_ptr(d, op.flag_src, what);
                         r.flag_dst = loc_ptr(d, op.flag_dst, what);
                         break;
+                    case foil::OpKind::Word:
+                        if (op.word != foil::WordOp::Set) r.p0 = loc_ptr(d, op.in0, what);
+                        if (op.word == foil::WordOp::Add || op.word == foil::WordOp::Mul)
+                            r.p1 = loc_ptr(d, op.in1, what);
+                        r.po = loc_ptr(d, op.out, what);
+                        break;
+                    case foil::OpKind::Send:
+                        r.p0 = loc_ptr(d, op.in0, what);
+                        r.po = loc_ptr(d, op.out, what);
+                        r.flag_src = loc_ptr(d, op.flag_src, what);
+                        r.flag_dst = loc_ptr(d, op.flag_dst, what);
+                        break;
                 }
                 if (op.gated) r.gate = loc_ptr(d, op.gate_flag, what);
+                const bool scalar = op.kind == foil::OpKind::Word || op.kind == foil::OpKind::Send;
                 for (char* p : {r.p0, r.p1, r.po})
-                    if (p && !aligned16(p))
+                    if (p && (scalar ? (reinterpret_cast<uintptr_t>(p) & 3u) != 0 : !aligned16(p)))
                         throw FoilError(FOIL_ERR_INVALID, std::string("tt-foil: ") + what +
-                                                              ": tile operands must be 16-byte aligned");
+                                                              (scalar ? ": word operands must be 4-byte aligned"
+                                                                      : ": tile operands must be 16-byte aligned"));
+                for (char* p : {r.flag_src, r.flag_dst, r.gate})
+                    if (p && (reinterpret_cast<uintptr_t>(p) & 3u) != 0)
+                        throw FoilError(FOIL_ERR_INVALID, std::string("tt-foil: ") + what +
+                                                              ": flag words must be 4-byte aligned");
                 ops.push_back(r);
             }
         }
         // 2. Programs that talk to each other (the mcast producer forwards B
         //    and sets the consumer's ready flag; the consumer waits for it,
-        //    reader_consumer.cpp:40-44) run as ONE cluster launch, one CTA
-        //    per core, so they are resident together and the consumer's
-        //    bounded device-side wait sees the producer's flag.  The other
+        //    reader_consumer.cpp:40-44; likewise noc_passthrough) and the
+        //    scalar add_two_numbers kernels run as ONE cluster launch, one
+        //    CTA per core, so they are resident together and a consumer's
+        //    bounded device-side wait sees its producer's flag.  The other
         //    programs of the execute follow in stream order.
         bool interacting = false;
-        for (auto& r : ops) interacting |= r.gate != nullptr || r.op.kind == foil::OpKind::McastForward;
+        for (auto& r : ops)
+            interacting |= r.gate != nullptr || r.op.kind == foil::OpKind::McastForward ||
+                           r.op.kind == foil::OpKind::Word || r.op.kind == foil::OpKind::Send;
         if (interacting) {
             std::vector<foil::gemm::CoreProgram> cores;
             std::vector<const foil_kernel*> core_kernel;
@@ -731,9 +754,10 @@ extern "C" int foil_execute(foil_device* d, foil_kernel* const* kernels, size_t 
                 for (size_t j = 0; j < ops.size(); ++j) {
                     if (ops[j].k != kernels[i]) continue;
                     const auto& r = ops[j];
-                    if (r.op.kind == foil::OpKind::McastForward) {
+                    if ((r.op.kind == foil::OpKind::McastForward || r.op.kind == foil::OpKind::Send) &&
+                        !c.fwd_bytes) {
                         c.fwd_src = r.p0;
-                        c.fwd_stage = r.p1;
+                        c.fwd_stage = r.op.kind == foil::OpKind::McastForward ? r.p1 : nullptr;
                         c.fwd_peer = r.po;
                         c.fwd_bytes = r.op.in0.bytes;
                         c.flag_src = reinterpret_cast<const uint32_t*>(r.flag_src);
@@ -746,14 +770,32 @@ extern "C" int foil_execute(foil_device* d, foil_kernel* const* kernels, size_t 
                         c.Mt = r.op.Mt;
                         c.Kt = r.op.Kt;
                         c.Nt = r.op.Nt;
-                        if (r.gate) c.gate = reinterpret_cast<const uint32_t*>(r.gate);
+                    } else if (r.op.kind == foil::OpKind::Word && c.nwords < foil::gemm::kMaxWordSteps) {
+                        foil::gemm::WordStep& w = c.words[c.nwords++];
+                        w.a = reinterpret_cast<const uint32_t*>(r.p0);
+                        w.b = reinterpret_cast<const uint32_t*>(r.p1);
+                        w.out = reinterpret_cast<uint32_t*>(r.po);
+                        w.imm = r.op.imm;
+                        switch (r.op.word) {
+                            case foil::WordOp::Add: w.code = foil::gemm::kWordAdd; break;
+                            case foil::WordOp::Mul: w.code = foil::gemm::kWordMul; break;
+                            case foil::WordOp::Set: w.code = foil::gemm::kWordSet; break;
+                            case foil::WordOp::Scale: w.code = foil::gemm::kWordScale; break;
+                        }
+                        any = true;
                     } else {
                         plain = false;
+                    }
+                    if (r.gate) {
+                        c.gate = reinterpret_cast<const uint32_t*>(r.gate);
+                        c.gate_value = r.op.gate_value;
                     }
                 }
                 if (c.gate || any || (plain && c.Mt)) {
                     if (!plain)
-                        throw FoilError(FOIL_ERR_UNSUPPORTED, "tt-foil: a core that waits or forwards runs one matmul");
+                        throw FoilError(FOIL_ERR_UNSUPPORTED,
+                                        "tt-foil: a core that waits, forwards or runs scalar steps runs at most "
+                                        "one matmul and no tile programs");
                     for (size_t j = 0; j < ops.size(); ++j)
                         if (ops[j].k == kernels[i]) in_cluster[j] = true;
                     cores.push_back(c);

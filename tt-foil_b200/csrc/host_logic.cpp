@@ -105,6 +105,12 @@ Program resolve_program(const std::vector<Descriptor>& ds) {
     if (name == "relu") return Program::Relu;
     if (name == "add_tiles") return Program::AddTiles;
     if (name == "bias_add") return Program::BiasAdd;
+    if (name == "add_two_numbers") return Program::AddTwoNumbers;
+    if (name == "noc_passthrough") {
+        if (variant == "producer") return Program::NocProducer;
+        if (variant == "consumer") return Program::NocConsumer;
+        throw FoilError(FOIL_ERR_INVALID, "tt-foil: noc_passthrough kernel needs a producer or consumer binary");
+    }
     throw FoilError(FOIL_ERR_UNSUPPORTED, "tt-foil: program '" + name +
                                               "' is not part of the B200 accelerated path");
 }
@@ -121,6 +127,9 @@ const char* program_name(Program p) {
         case Program::Relu: return "relu";
         case Program::AddTiles: return "add_tiles";
         case Program::BiasAdd: return "bias_add";
+        case Program::AddTwoNumbers: return "add_two_numbers";
+        case Program::NocProducer: return "noc_passthrough/producer";
+        case Program::NocConsumer: return "noc_passthrough/consumer";
     }
     return "?";
 }
@@ -186,6 +195,17 @@ void check_count(Program prog, uint64_t got, uint64_t want) {
         throw FoilError(FOIL_ERR_INVALID, std::string("tt-foil: ") + program_name(prog) +
                                               ": writer tile count " + std::to_string(got) +
                                               " != Mt*Nt " + std::to_string(want));
+}
+
+PlanOp word(WordOp w, Loc in0, Loc in1, Loc out, uint32_t imm = 0) {
+    PlanOp op;
+    op.kind = OpKind::Word;
+    op.word = w;
+    op.in0 = in0;
+    op.in1 = in1;
+    op.out = out;
+    op.imm = imm;
+    return op;
 }
 
 PlanOp matmul(Loc a, Loc b, Loc c, uint32_t Mt, uint32_t Kt, uint32_t Nt) {
@@ -306,6 +326,47 @@ std::vector<PlanOp> plan_program(Program prog, uint32_t cx, uint32_t cy,
                                noc(w[0], w[1], T * Mt * Nt), Mt, Kt, Nt);
             op.gated = true;
             op.gate_flag = l1(cx, cy, r[3], 4);
+            ops.push_back(op);
+            break;
+        }
+        case Program::AddTwoNumbers: {
+            // examples/add_two_numbers/kernels/add_brisc.cpp:25-37 (BRISC,
+            // [a, b, result]: result = a + b) and add_ncrisc.cpp:19-29
+            // (NCRISC, same arguments: result = a * b); either or both.
+            if (!has[0] && !has[1]) need(rta, has, 0, 3, prog);
+            for (int risc : {0, 1}) {
+                if (!has[risc]) continue;
+                auto& r = need(rta, has, risc, 3, prog);
+                ops.push_back(word(risc == 0 ? WordOp::Add : WordOp::Mul, l1(cx, cy, r[0], 4),
+                                   l1(cx, cy, r[1], 4), l1(cx, cy, r[2], 4)));
+            }
+            break;
+        }
+        case Program::NocProducer: {
+            // examples/noc_passthrough/kernels/producer.cpp:29-58: [a, b,
+            // sum_scratch, dst_sum lo/hi, flag_scratch, dst_flag lo/hi].  The
+            // sum and the sentinel are assembled locally, then the sum is
+            // sent and the flag published after it.
+            auto& r = need(rta, has, 0, 8, prog);
+            ops.push_back(word(WordOp::Add, l1(cx, cy, r[0], 4), l1(cx, cy, r[1], 4), l1(cx, cy, r[2], 4)));
+            ops.push_back(word(WordOp::Set, Loc{}, Loc{}, l1(cx, cy, r[5], 4), kNocFlagValue));
+            PlanOp send;
+            send.kind = OpKind::Send;
+            send.in0 = l1(cx, cy, r[2], 4);
+            send.out = noc(r[3], r[4], 4);
+            send.flag_src = l1(cx, cy, r[5], 4);
+            send.flag_dst = noc(r[6], r[7], 4);
+            ops.push_back(send);
+            break;
+        }
+        case Program::NocConsumer: {
+            // examples/noc_passthrough/kernels/consumer.cpp:22-38: [flag, sum,
+            // result]; wait for the sentinel, then result = sum * 2.
+            auto& r = need(rta, has, 0, 3, prog);
+            PlanOp op = word(WordOp::Scale, l1(cx, cy, r[1], 4), Loc{}, l1(cx, cy, r[2], 4), 2u);
+            op.gated = true;
+            op.gate_flag = l1(cx, cy, r[0], 4);
+            op.gate_value = kNocFlagValue;
             ops.push_back(op);
             break;
         }

@@ -68,6 +68,9 @@ enum class Program {
     Relu,
     AddTiles,
     BiasAdd,
+    AddTwoNumbers,   // add_brisc (BRISC: sum) / add_ncrisc (NCRISC: product)
+    NocProducer,     // noc_passthrough producer core
+    NocConsumer,     // noc_passthrough consumer core
 };
 
 enum class Role { Reader, Writer, Compute };
@@ -82,8 +85,8 @@ struct Descriptor {
 Descriptor parse_descriptor(const std::string& text, const std::string& path);
 
 // Program for a set of descriptors (all must name the same program; the
-// reader's variant selects mcast producer / consumer).  Throws FoilError for
-// programs outside the accelerated path (add_two_numbers, noc_passthrough).
+// reader's variant selects the producer / consumer of matmul_2core_mcast and
+// noc_passthrough).  Throws FoilError for programs it does not know.
 Program resolve_program(const std::vector<Descriptor>& ds);
 
 const char* program_name(Program p);
@@ -111,18 +114,32 @@ struct Loc {
     uint64_t bytes{0};
 };
 
-enum class OpKind { Copy, Relu, Add, BiasAdd, Matmul, McastForward };
+enum class OpKind { Copy, Relu, Add, BiasAdd, Matmul, McastForward, Word, Send };
+
+// Scalar u32 step of a Word op (wrapping arithmetic, like the RISC-V cores):
+// Add out = in0 + in1, Mul out = in0 * in1, Set out = imm, Scale out = in0 * imm.
+enum class WordOp : uint8_t { Add, Mul, Set, Scale };
+
+// Sentinel the noc_passthrough producer publishes and its consumer waits for
+// (examples/noc_passthrough/kernels/producer.cpp:27, consumer.cpp:20).
+constexpr uint32_t kNocFlagValue = 0xCAFEBABEu;
 
 struct PlanOp {
     OpKind kind;
     Loc in0, in1, out;  // operands used by the op kind
     uint32_t Mt{0}, Kt{0}, Nt{0};
     // McastForward: in0 = B in DRAM, in1 = local staging, out = peer staging,
-    // flag_src -> flag_dst (4 bytes).
+    // flag_src -> flag_dst (4 bytes).  Send: in0 -> out (no staging), then
+    // flag_src -> flag_dst.
     Loc flag_src, flag_dst;
-    // McastConsumer GEMM: the consumer's local flag must read non-zero.
+    // Word: the step and its immediate.
+    WordOp word{WordOp::Add};
+    uint32_t imm{0};
+    // Gated ops wait until the core's local flag reads gate_value (0: any
+    // non-zero value).
     bool gated{false};
     Loc gate_flag;
+    uint32_t gate_value{0};
 };
 
 constexpr size_t kMaxRtaWords = 64;  // src/kernel.hpp:29

@@ -405,9 +405,11 @@ gemm_tiles_kernel(const Params p) {
 // cluster, hence resident together: a consumer core may wait for a flag that
 // a producer core of the same launch sets.  Replaces the reference's
 // fire-all-then-poll dispatch of several core kernels (src/dispatch.cpp:
-// 223-274) for programs that talk to each other, here the matmul_2core_mcast
-// producer / consumer pair (examples/matmul_2core_mcast/kernels/
-// reader_producer.cpp:60-82, reader_consumer.cpp:38-44).
+// 223-274) for programs that talk to each other (the matmul_2core_mcast
+// producer / consumer pair, examples/matmul_2core_mcast/kernels/
+// reader_producer.cpp:60-82, reader_consumer.cpp:38-44; the noc_passthrough
+// producer / consumer, examples/noc_passthrough/kernels/producer.cpp:29-58,
+// consumer.cpp:22-38) and for the scalar add_two_numbers kernels.
 struct CoreLaunch {
     CoreProgram core[kMaxCores];
     Params gemm[kMaxCores];  // the GEMM of core i (Mt = 0: none)
@@ -415,25 +417,34 @@ struct CoreLaunch {
     uint32_t* status;
     uint64_t gate_wait_ns;
 };
+static_assert(sizeof(CoreLaunch) <= 4096, "multi-core launch parameters must fit the classic 4 KiB limit");
 
-// Bounded acquire poll of a flag in global memory: true once it is nonzero,
-// false after limit_ns.
-__device__ __forceinline__ bool wait_flag_acquire(const uint32_t* flag, uint64_t limit_ns) {
+// Bounded acquire poll of a flag in global memory: true once it reads
+// `want` (want 0: any non-zero value), false after limit_ns.
+__device__ __forceinline__ bool wait_flag_acquire(const uint32_t* flag, uint32_t want, uint64_t limit_ns) {
     const uint64_t t0 = global_ns();
 #pragma unroll 1
     while (true) {
         uint32_t v;
         asm volatile("ld.acquire.gpu.global.u32 %0, [%1];" : "=r"(v) : "l"(flag) : "memory");
-        if (v != 0u) return true;
+        if (want == 0u ? v != 0u : v == want) return true;
         if (global_ns() - t0 > limit_ns) return false;
         __nanosleep(256);
     }
 }
 
-__device__ __forceinline__ void copy_block16(const void* src, void* dst, uint64_t bytes) {
-    const uint4* s = static_cast<const uint4*>(src);
-    uint4* d = static_cast<uint4*>(dst);
-    for (uint64_t i = threadIdx.x; i < bytes / 16u; i += blockDim.x) d[i] = s[i];
+// Block-wide copy: 16-byte units when both ends and the size allow, else
+// 4-byte words (the host checks 4-byte alignment and size).
+__device__ __forceinline__ void copy_block(const void* src, void* dst, uint64_t bytes) {
+    if (((reinterpret_cast<uintptr_t>(src) | reinterpret_cast<uintptr_t>(dst) | bytes) & 15u) == 0) {
+        const uint4* s = static_cast<const uint4*>(src);
+        uint4* d = static_cast<uint4*>(dst);
+        for (uint64_t i = threadIdx.x; i < bytes / 16u; i += blockDim.x) d[i] = s[i];
+    } else {
+        const uint32_t* s = static_cast<const uint32_t*>(src);
+        uint32_t* d = static_cast<uint32_t*>(dst);
+        for (uint64_t i = threadIdx.x; i < bytes / 4u; i += blockDim.x) d[i] = s[i];
+    }
 }
 
 __global__ void __launch_bounds__(kThreads, 1) cores_kernel(const __grid_constant__ CoreLaunch L) {
@@ -441,22 +452,41 @@ __global__ void __launch_bounds__(kThreads, 1) cores_kernel(const __grid_constan
     __shared__ uint32_t go;
     const CoreProgram& c = L.core[blockIdx.x];
     if (threadIdx.x == 0) {
-        const bool ok = c.gate == nullptr || wait_flag_acquire(c.gate, L.gate_wait_ns);
+        const bool ok = c.gate == nullptr || wait_flag_acquire(c.gate, c.gate_value, L.gate_wait_ns);
         if (!ok) {
             atomicOr(L.err, kErrWaitTimeout);
             L.status[blockIdx.x] = 1u;
         }
         go = ok ? 1u : 0u;
+        // Scalar steps, in program order on one thread, after the gate's
+        // acquire (a consumer reads what the producer sent before its flag).
+        if (ok) {
+            for (uint32_t i = 0; i < c.nwords && i < kMaxWordSteps; ++i) {
+                const WordStep& w = c.words[i];
+                uint32_t v;
+                switch (w.code) {
+                    case kWordAdd: v = *w.a + *w.b; break;
+                    case kWordMul: v = *w.a * *w.b; break;
+                    case kWordSet: v = w.imm; break;
+                    default: v = *w.a * w.imm; break;
+                }
+                *w.out = v;
+            }
+        }
     }
     __syncthreads();
     if (!go) return;
     if (c.fwd_bytes) {
-        // Stage, forward to the peer core, then publish its flag: the flag's
-        // release store orders every thread's copies (joined by the CTA
-        // barrier and made GPU-visible by the fence) before it.
-        copy_block16(c.fwd_src, c.fwd_stage, c.fwd_bytes);
-        __syncthreads();
-        copy_block16(c.fwd_stage, c.fwd_peer, c.fwd_bytes);
+        // (Stage and) forward to the peer core, then publish its flag: the
+        // flag's release store orders every thread's copies (joined by the
+        // CTA barrier and made GPU-visible by the fence) before it.
+        if (c.fwd_stage) {
+            copy_block(c.fwd_src, c.fwd_stage, c.fwd_bytes);
+            __syncthreads();
+            copy_block(c.fwd_stage, c.fwd_peer, c.fwd_bytes);
+        } else {
+            copy_block(c.fwd_src, c.fwd_peer, c.fwd_bytes);
+        }
         __syncthreads();
         if (threadIdx.x == 0) {
             __threadfence();
@@ -480,7 +510,13 @@ int launch_cores(const CoreProgram* cores, uint32_t ncores, uint32_t* err, uint3
     }
     CoreLaunch L;
     memset(&L, 0, sizeof L);
+    bool any_gemm = false;
     for (uint32_t i = 0; i < ncores; ++i) {
+        if (cores[i].nwords > kMaxWordSteps) {
+            foil_set_error(FOIL_ERR_INVALID, "tt-foil: too many scalar steps on one core");
+            return FOIL_ERR_INVALID;
+        }
+        any_gemm |= cores[i].Mt != 0;
         L.core[i] = cores[i];
         Params& p = L.gemm[i];
         p.a = cores[i].a;
@@ -505,7 +541,8 @@ int launch_cores(const CoreProgram* cores, uint32_t ncores, uint32_t* err, uint3
     memset(&cfg, 0, sizeof cfg);
     cfg.gridDim = dim3(ncores, 1, 1);
     cfg.blockDim = dim3(kThreads, 1, 1);
-    cfg.dynamicSmemBytes = kSmemBytes;
+    // Shared memory only serves the GEMM stages.
+    cfg.dynamicSmemBytes = any_gemm ? kSmemBytes : 0;
     cfg.stream = stream;
     cudaLaunchAttribute attr[1];
     attr[0].id = cudaLaunchAttributeClusterDimension;

@@ -22,12 +22,28 @@ int launch(const uint16_t* a, const uint16_t* b, uint16_t* c, uint32_t Mt, uint3
 // One "core" of a multi-core execute: the work one logical core's program
 // does, run by one CTA of a single cluster launch in which every core's CTA
 // is resident at the same time, so cores may wait on each other's flags.
-// In order: (1) if `gate` is set, wait (bounded) until *gate != 0;
-// (2) if fwd_bytes, copy fwd_src -> fwd_stage -> fwd_peer and then publish
-// *flag_dst = *flag_src with release semantics (after the copies); (3) if
-// Mt, the tiled GEMM c = a . b (Mt x Kt x Nt tiles).
+// In order: (1) if `gate` is set, wait (bounded) until *gate == gate_value
+// (gate_value 0: until *gate != 0); (2) the scalar u32 steps words[0..nwords)
+// in order; (3) if fwd_bytes, copy fwd_src -> fwd_stage -> fwd_peer (or
+// fwd_src -> fwd_peer when fwd_stage is null) and then publish *flag_dst =
+// *flag_src with release semantics (after the copies); (4) if Mt, the tiled
+// GEMM c = a . b (Mt x Kt x Nt tiles).
+enum WordCode : uint32_t { kWordAdd = 0, kWordMul = 1, kWordSet = 2, kWordScale = 3 };
+// out = a + b | a * b | imm | a * imm (wrapping u32).
+struct WordStep {
+    const uint32_t* a;
+    const uint32_t* b;
+    uint32_t* out;
+    uint32_t imm;
+    uint32_t code;
+};
+constexpr uint32_t kMaxWordSteps = 4;
+
 struct CoreProgram {
     const uint32_t* gate;
+    uint32_t gate_value;
+    uint32_t nwords;
+    WordStep words[kMaxWordSteps];
     const void* fwd_src;
     void* fwd_stage;
     void* fwd_peer;

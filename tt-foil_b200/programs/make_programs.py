@@ -3,7 +3,9 @@
 tt-foil tests name their device binaries by convention
 (``<kernel_dir>/reader.brisc.elf``, ``writer.ncrisc.elf``,
 ``compute.trisc{0,1,2}.elf``; the mcast example uses
-``reader_producer.brisc.elf`` / ``reader_consumer.brisc.elf``) and
+``reader_producer.brisc.elf`` / ``reader_consumer.brisc.elf``; the scalar
+examples use ``add_brisc.elf`` / ``add_ncrisc.elf`` and ``producer.elf`` /
+``consumer.elf``) and
 ``load_kernel`` fails when a file is missing (reference src/kernel.cpp:42-45).
 On the B200 there is no per-RISC ELF: each file is a small text descriptor
 naming the program and the role, and ``load_kernel`` maps the bundle to the
@@ -26,6 +28,19 @@ PROGRAMS = [
     "relu", "add_tiles", "bias_add",
 ]
 
+# The scalar dispatch examples (examples/add_two_numbers, examples/
+# noc_passthrough): one BRISC (or NCRISC) binary each, named as there.
+SCALAR_PROGRAMS = {
+    "add_two_numbers": {
+        "add_brisc.elf": ("reader", ""),
+        "add_ncrisc.elf": ("writer", ""),
+    },
+    "noc_passthrough": {
+        "producer.elf": ("reader", "producer"),
+        "consumer.elf": ("reader", "consumer"),
+    },
+}
+
 
 def descriptor(program, role, variant=""):
     lines = [MAGIC, f"program={program}", f"role={role}"]
@@ -34,7 +49,18 @@ def descriptor(program, role, variant=""):
     return "\n".join(lines) + "\n"
 
 
+def write_file(path, text):
+    if not os.path.exists(path) or open(path).read() != text:
+        with open(path, "w") as f:
+            f.write(text)
+
+
 def write_all(out_dir):
+    for prog, files in SCALAR_PROGRAMS.items():
+        d = os.path.join(out_dir, prog)
+        os.makedirs(d, exist_ok=True)
+        for name, (role, variant) in files.items():
+            write_file(os.path.join(d, name), descriptor(prog, role, variant))
     for prog in PROGRAMS:
         d = os.path.join(out_dir, prog)
         os.makedirs(d, exist_ok=True)
@@ -50,10 +76,7 @@ def write_all(out_dir):
         else:
             files["reader.brisc.elf"] = descriptor(prog, "reader")
         for name, text in files.items():
-            path = os.path.join(d, name)
-            if not os.path.exists(path) or open(path).read() != text:
-                with open(path, "w") as f:
-                    f.write(text)
+            write_file(os.path.join(d, name), text)
 
 
 if __name__ == "__main__":
