@@ -6,16 +6,20 @@ matmul_dram program at Mt = Kt = Nt = 256), run by the sm_100a tcgen05 kernel
 of libfoil.  With N GPUs (torchrun, one process per GPU) every rank computes
 its own 8192-row shard of an (8192 N) x 8192 x 8192 product (weak scaling, no
 collective inside the step).  Reassembling the global tile-layout C is timed
-separately under "allgather": ncclAllGather after the GEMM, and ("fused") the
+separately under "allgather": ncclAllGather after the GEMM; ("fused") the
 GEMM kernel that stores every C tile into all ranks' copies over NVLink
-itself, followed by a one-element all-reduce.
+itself; and ("copy_engines") the GEMM in row chunks whose finished chunks the
+copy engines send to the peers while the next chunk computes; the last two
+followed by a one-element all-reduce.
 
 value      TFLOP/s over all ranks, operands resident in HBM, CUDA events on the
            launching stream, max over ranks.
 value_with_gather  (N > 1) the same step with the global C reassembled on every
-           rank: the better of GEMM + ncclAllGather and the fused GEMM that
-           stores each tile to every rank's copy over NVLink, with the achieved
-           NVLink GB/s against the link floor.
+           rank: the best of GEMM + ncclAllGather, the fused GEMM that stores
+           each tile to every rank's copy over NVLink, and the GEMM in row
+           chunks whose finished chunks the copy engines send to the peers
+           while the next chunk computes, with the achieved NVLink GB/s
+           against the link floor.
 e2e        TFLOP/s of the same GEMM on host buffers through the public entry
            point foil_matmul_tiles_host (pinned A, B in; C out; copies of
            chunk i+1 and read-back of chunk i-1 overlap the GEMM of chunk i)
@@ -77,6 +81,8 @@ def parse():
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--no-secondary", action="store_true")
     ap.add_argument("--no-e2e", action="store_true")
+    ap.add_argument("--gather-chunks", type=int, default=8,
+                    help="row chunks of the copy-engine reassembly path (N > 1)")
     return ap.parse_args()
 
 
@@ -389,23 +395,28 @@ def run_ours(args, dist):
     with_gather = None
     if dist.world > 1:
         allgather = time_allgather(dist, c, ms / args.steps, flops)
-        try:
-            allgather["fused"] = time_fused_gather(dist, a, b, Mt, Kt, Nt, flops)
-        except RuntimeError as e:  # raised on every rank alike (see GatheredTiles)
-            allgather["fused"] = {"unavailable": str(e)[:300]}
+        for key, method in (("fused", "fused"), ("copy_engines", "ce")):
+            try:
+                allgather[key] = time_fused_gather(dist, a, b, Mt, Kt, Nt, flops, method=method,
+                                                   chunks=args.gather_chunks)
+            except RuntimeError as e:  # raised on every rank alike (see GatheredTiles)
+                allgather[key] = {"unavailable": str(e)[:300]}
         shard_bytes = M_PER_GPU * N_DIM * 2
         recv = (dist.world - 1) * shard_bytes  # C bytes every GPU must receive per step
         link_gbs = 770.0  # measured peer copy per direction per GPU on this pool
         nccl_ms = ms / args.steps + allgather["ms"]
-        fused = allgather["fused"]
-        fused_ms = fused.get("ms_per_step") if "ms_per_step" in fused else None
-        best = "fused" if fused_ms is not None and fused_ms < nccl_ms else "ncclAllGather"
-        step_ms = fused_ms if best == "fused" else nccl_ms
+        step_of = lambda k: allgather[k].get("ms_per_step")
+        fused_ms, ce_ms = step_of("fused"), step_of("copy_engines")
+        paths = {"ncclAllGather": nccl_ms, "fused": fused_ms, "copy_engines": ce_ms}
+        best = min((v, k) for k, v in paths.items() if v is not None)[1]
+        step_ms = paths[best]
         with_gather = {
             "value": dist.world * flops / (step_ms / 1e3) / 1e12, "unit": "TFLOP/s", "ms_per_step": step_ms,
             "path": best, "nccl_ms_per_step": nccl_ms, "fused_ms_per_step": fused_ms,
+            "copy_engines_ms_per_step": ce_ms,
             "received_bytes_per_gpu": recv,
             "nvlink_GBps_fused": recv / (fused_ms / 1e3) / 1e9 if fused_ms else None,
+            "nvlink_GBps_copy_engines": recv / (ce_ms / 1e3) / 1e9 if ce_ms else None,
             "allgather_busbw_GBps": allgather["busbw_GBps"],
             "link_floor_ms": recv / (link_gbs * 1e9) * 1e3,
             "compute_floor_ms": ms / args.steps,
@@ -649,11 +660,14 @@ def time_allgather(dist, c, compute_ms, flops):
             "note": "ncclAllGather of the C shards after the step, timed separately"}
 
 
-def time_fused_gather(dist, a, b, Mt, Kt, Nt, flops):
-    """The same per-rank GEMM with its own all-gather: one kernel per rank
-    stores every output tile into all ranks' copies of the global C over
-    NVLink (ttfoil.shard.GatheredTiles), then a one-element all-reduce orders
-    the ranks' launches.  Time per step = kernel + fence, max over ranks."""
+def time_fused_gather(dist, a, b, Mt, Kt, Nt, flops, method="fused", chunks=8):
+    """The same per-rank GEMM with its own all-gather into all ranks' copies
+    of the global C over NVLink (ttfoil.shard.GatheredTiles), then a
+    one-element all-reduce orders the ranks' launches.  method "fused": one
+    kernel per rank whose pusher warps store every tile to the peers; "ce":
+    the GEMM in `chunks` row chunks, each finished chunk copied to the peers
+    by the copy engines while the next computes.  Time per step = GEMM +
+    transfer + fence, max over ranks."""
     import torch
     import ttfoil
     from ttfoil import shard
@@ -662,7 +676,7 @@ def time_fused_gather(dist, a, b, Mt, Kt, Nt, flops):
         assert g.rows == (dist.rank * Mt, (dist.rank + 1) * Mt)
 
         def step():
-            g.matmul(a, b, Kt)
+            g.matmul(a, b, Kt, method=method, chunks=chunks)
             g.fence()
 
         for _ in range(3):
@@ -689,11 +703,17 @@ def time_fused_gather(dist, a, b, Mt, Kt, Nt, flops):
         consistent = bool(torch.equal(sums, ref))
     finally:
         g.close()
-    return {"ms_per_step": ms, "value_TFLOPs": dist.world * flops / (ms / 1e3) / 1e12,
-            "copies_consistent": consistent,
-            "note": "one GEMM kernel per rank that also stores each C tile to every peer GPU's copy "
-                    "over NVLink (256x512 pair tiles; four pusher warps copy finished tiles to the peers "
-                    "while later tiles compute), plus a one-element all-reduce"}
+    note = ("one GEMM kernel per rank that also stores each C tile to every peer GPU's copy "
+            "over NVLink (256x512 pair tiles; four pusher warps copy finished tiles to the peers "
+            "while later tiles compute), plus a one-element all-reduce") if method == "fused" else (
+        f"the GEMM as {chunks} row-chunk launches per rank; one copy stream per peer copies each "
+        "finished chunk over NVLink (copy engines) while the next chunk computes, plus a one-element "
+        "all-reduce")
+    out = {"ms_per_step": ms, "value_TFLOPs": dist.world * flops / (ms / 1e3) / 1e12,
+           "copies_consistent": consistent, "note": note}
+    if method == "ce":
+        out["chunks"] = chunks
+    return out
 
 
 def run_e2e(args, dist, flops):

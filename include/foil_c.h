@@ -281,6 +281,18 @@ FOIL_API int foil_matmul_tiles_gather_dev(const uint16_t* a, const uint16_t* b, 
                           uint32_t Mt, uint32_t Kt, uint32_t Nt,
                           const uint16_t* bias, int32_t relu, void* stream);
 
+/* The same result as foil_matmul_tiles_gather_dev, with the transfer on the
+ * copy engines instead of the SMs: the GEMM runs as `chunks` launches over
+ * row chunks of C (whole 256-row blocks, 1..64 chunks) on `stream`, and as
+ * soon as a chunk's launch completes one copy stream per peer copies that
+ * chunk into peer_c[d] (cudaMemcpyAsync over NVLink) while the next chunk
+ * computes.  `stream` waits for every copy before its later work, so the
+ * same fence as for foil_matmul_tiles_gather_dev orders the ranks. */
+FOIL_API int foil_matmul_tiles_gather_ce_dev(const uint16_t* a, const uint16_t* b, uint16_t* c,
+                          uint16_t* const* peer_c, uint32_t npeers,
+                          uint32_t Mt, uint32_t Kt, uint32_t Nt,
+                          const uint16_t* bias, int32_t relu, uint32_t chunks, void* stream);
+
 /* Device buffers shared between the processes of a node (CUDA IPC).
  * foil_peer_alloc allocates `bytes` on CUDA device `device` and writes its
  * 64-byte export handle; another process passes the handle to

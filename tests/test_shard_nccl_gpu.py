@@ -7,7 +7,8 @@
   stored to both GPUs' copies of C over NVLink, by the epilogue or by pusher
   warps): after the fence, both copies equal the per-rank results of the
   plain GEMM concatenated (bit for bit, same kernels), and the oracle on
-  sampled rows.
+  sampled rows; likewise with the GEMM in row chunks whose finished chunks
+  the copy engines push to the peer ("ce").
 """
 import datetime
 import os
@@ -76,7 +77,10 @@ def gather_worker(rank, world, port, q):
         # Mt odd -> uneven row split; Nt 8 (256-column kernel, the epilogue
         # stores to the peer) and 24 (512-column kernel, pusher warps copy
         # finished tiles to the peer).  Both are the plain GEMM's kernels.
-        for (Mt, Kt, Nt) in ((25, 16, 8), (19, 12, 24)):
+        # "ce": the same GEMM in row chunks, copy engines push each chunk.
+        cases = [(Mt, Kt, Nt, m, ch) for (Mt, Kt, Nt) in ((25, 16, 8), (19, 12, 24))
+                 for (m, ch) in (("fused", 0), ("ce", 1), ("ce", 3))] + [(40, 4, 24, "ce", 64)]
+        for (Mt, Kt, Nt, method, chunks) in cases:
             a_all = oracle.rand_bf16(Mt * Kt * 1024, 40 + Nt)
             b = oracle.rand_bf16(Kt * Nt * 1024, 41 + Nt)
             dev = lambda arr: torch.from_numpy(np.ascontiguousarray(arr).view(np.int16)).cuda()
@@ -87,7 +91,7 @@ def gather_worker(rank, world, port, q):
             g.tensor().fill_(0x7fff)
             torch.cuda.synchronize()
             dist.barrier()          # no rank's GEMM may land before every fill
-            g.matmul(a_r, b_d, Kt)
+            g.matmul(a_r, b_d, Kt, method=method, chunks=max(1, chunks))
             g.fence()
             torch.cuda.synchronize()
             full = g.tensor().cpu().numpy().view(np.uint16).copy()

@@ -879,6 +879,100 @@ extern "C" int foil_matmul_tiles_gather_dev(const uint16_t* a, const uint16_t* b
     });
 }
 
+// ------------------------ GEMM in row chunks, copy engines push to the peers ---
+// Per device: one copy stream per peer and the events that order each copy
+// after the GEMM launch of its chunk (reused under the device's lock).
+namespace {
+
+struct CopyPipe {
+    std::mutex mu;
+    int device = -1;
+    cudaStream_t copy[foil::gemm::kMaxPeers] = {};
+    cudaEvent_t done[foil::gemm::kMaxPeers] = {};
+    std::vector<cudaEvent_t> chunk_ev;
+};
+
+CopyPipe& copy_pipe(int device) {
+    static std::mutex mu;
+    static std::vector<std::unique_ptr<CopyPipe>> pipes;
+    std::lock_guard<std::mutex> lk(mu);
+    for (auto& p : pipes)
+        if (p->device == device) return *p;
+    auto p = std::make_unique<CopyPipe>();
+    p->device = device;
+    for (uint32_t i = 0; i < foil::gemm::kMaxPeers; ++i) {
+        cuda_check(cudaStreamCreateWithFlags(&p->copy[i], cudaStreamNonBlocking), "cudaStreamCreate(copy)");
+        cuda_check(cudaEventCreateWithFlags(&p->done[i], cudaEventDisableTiming), "cudaEventCreate");
+    }
+    pipes.push_back(std::move(p));
+    return *pipes.back();
+}
+
+}  // namespace
+
+extern "C" int foil_matmul_tiles_gather_ce_dev(const uint16_t* a, const uint16_t* b, uint16_t* c,
+                                               uint16_t* const* peer_c, uint32_t npeers, uint32_t Mt,
+                                               uint32_t Kt, uint32_t Nt, const uint16_t* bias, int32_t relu,
+                                               uint32_t chunks, void* stream) {
+    return guarded([&] {
+        if (npeers > foil::gemm::kMaxPeers)
+            throw FoilError(FOIL_ERR_INVALID, "foil_matmul_tiles_gather_ce_dev: at most 7 peer copies");
+        if (npeers && !peer_c)
+            throw FoilError(FOIL_ERR_INVALID, "foil_matmul_tiles_gather_ce_dev: null peer list");
+        for (uint32_t i = 0; i < npeers; ++i)
+            if (!peer_c[i] || !aligned16(peer_c[i]))
+                throw FoilError(FOIL_ERR_INVALID, "foil_matmul_tiles_gather_ce_dev: null or misaligned peer buffer");
+        if (chunks == 0 || chunks > 64)
+            throw FoilError(FOIL_ERR_INVALID, "foil_matmul_tiles_gather_ce_dev: chunks must be in 1..64");
+        if (Mt == 0 || Kt == 0 || Nt == 0) return;
+        if (Mt > 65535 || Kt > 65535 || Nt > 65535)
+            throw FoilError(FOIL_ERR_INVALID, "foil_matmul_tiles_gather_ce_dev: tile counts must be <= 65535");
+        if (!a || !b || !c || !aligned16(a) || !aligned16(b) || !aligned16(c) || (bias && !aligned16(bias)))
+            throw FoilError(FOIL_ERR_INVALID, "foil_matmul_tiles_gather_ce_dev: null or misaligned pointer");
+        int dev = 0;
+        cuda_check(cudaGetDevice(&dev), "cudaGetDevice");
+        uint32_t* err = error_word_for_current_device();
+        cudaStream_t s = (cudaStream_t)stream;
+        // Chunks of whole 256-row pair tiles (8 tile rows), the last one shorter.
+        uint32_t per = (Mt + chunks - 1) / chunks;
+        per = (per + 7u) / 8u * 8u;
+        CopyPipe& cp = copy_pipe(dev);
+        std::lock_guard<std::mutex> lk(cp.mu);
+        const uint32_t nchunks = (Mt + per - 1) / per;
+        while (cp.chunk_ev.size() < nchunks) {
+            cudaEvent_t e;
+            cuda_check(cudaEventCreateWithFlags(&e, cudaEventDisableTiming), "cudaEventCreate");
+            cp.chunk_ev.push_back(e);
+        }
+        // The copy streams start after everything already queued on `s`
+        // (earlier readers of the peers' buffers are ordered by the caller's
+        // collective on `s`).
+        for (uint32_t d = 0; d < npeers; ++d) {
+            cuda_check(cudaEventRecord(cp.done[d], s), "cudaEventRecord");
+            cuda_check(cudaStreamWaitEvent(cp.copy[d], cp.done[d], 0), "cudaStreamWaitEvent");
+        }
+        const int sms = sm_count_current();
+        for (uint32_t k = 0; k < nchunks; ++k) {
+            const uint32_t m0 = k * per, mt = std::min(per, Mt - m0);
+            const uint64_t c_off = (uint64_t)m0 * Nt * 1024u, a_off = (uint64_t)m0 * Kt * 1024u;
+            throw_status(foil::gemm::launch(a + a_off, b, c + c_off, mt, Kt, Nt, bias, relu, err, s, sms));
+            if (npeers == 0) continue;
+            cuda_check(cudaEventRecord(cp.chunk_ev[k], s), "cudaEventRecord");
+            for (uint32_t d = 0; d < npeers; ++d) {
+                cuda_check(cudaStreamWaitEvent(cp.copy[d], cp.chunk_ev[k], 0), "cudaStreamWaitEvent");
+                cuda_check(cudaMemcpyAsync(peer_c[d] + c_off, c + c_off, (uint64_t)mt * Nt * 2048u,
+                                           cudaMemcpyDeviceToDevice, cp.copy[d]),
+                           "cudaMemcpyAsync(peer chunk)");
+            }
+        }
+        // `s` continues after every chunk has reached every peer.
+        for (uint32_t d = 0; d < npeers; ++d) {
+            cuda_check(cudaEventRecord(cp.done[d], cp.copy[d]), "cudaEventRecord");
+            cuda_check(cudaStreamWaitEvent(s, cp.done[d], 0), "cudaStreamWaitEvent");
+        }
+    });
+}
+
 // Inter-process device buffers: allocated here, exported as a 64-byte handle,
 // opened by the other processes of the node as peer-mapped pointers.
 static_assert(sizeof(cudaIpcMemHandle_t) == FOIL_PEER_HANDLE_BYTES, "IPC handle size");

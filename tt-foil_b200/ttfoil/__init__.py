@@ -108,6 +108,9 @@ SIGNATURES = {
     "foil_matmul_tiles_gather_dev": (ctypes.c_int, [_U16P, _U16P, _U16P, ctypes.POINTER(_P), ctypes.c_uint32,
                                                     ctypes.c_uint32, ctypes.c_uint32, ctypes.c_uint32, _U16P,
                                                     ctypes.c_int32, _P]),
+    "foil_matmul_tiles_gather_ce_dev": (ctypes.c_int, [_U16P, _U16P, _U16P, ctypes.POINTER(_P), ctypes.c_uint32,
+                                                       ctypes.c_uint32, ctypes.c_uint32, ctypes.c_uint32, _U16P,
+                                                       ctypes.c_int32, ctypes.c_uint32, _P]),
     "foil_peer_alloc": (ctypes.c_int, [ctypes.c_int32, ctypes.c_uint64, ctypes.POINTER(_P),
                                        ctypes.POINTER(ctypes.c_uint8)]),
     "foil_peer_open": (ctypes.c_int, [ctypes.c_int32, ctypes.POINTER(ctypes.c_uint8), ctypes.POINTER(_P)]),
@@ -212,6 +215,16 @@ def matmul_tiles_gather(a, b, c, peer_c, Mt, Kt, Nt, bias=None, relu=False, stre
     arr = (_P * max(1, len(peer_c)))(*[int(x) for x in peer_c])
     check(lib().foil_matmul_tiles_gather_dev(_ptr(a), _ptr(b), _ptr(c), arr, len(peer_c), Mt, Kt, Nt,
                                              _ptr(bias), 1 if relu else 0, _stream(stream)))
+
+
+def matmul_tiles_gather_ce(a, b, c, peer_c, Mt, Kt, Nt, bias=None, relu=False, chunks=8, stream=None):
+    """matmul_tiles_gather with the transfer on the copy engines: the GEMM
+    runs in `chunks` row chunks and each finished chunk is copied to every
+    peer buffer while the next one computes; `stream` continues after the
+    last copy."""
+    arr = (_P * max(1, len(peer_c)))(*[int(x) for x in peer_c])
+    check(lib().foil_matmul_tiles_gather_ce_dev(_ptr(a), _ptr(b), _ptr(c), arr, len(peer_c), Mt, Kt, Nt,
+                                                _ptr(bias), 1 if relu else 0, int(chunks), _stream(stream)))
 
 
 PEER_HANDLE_BYTES = 64

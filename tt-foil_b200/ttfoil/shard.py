@@ -176,15 +176,24 @@ class GatheredTiles:
         import torch
         return torch.as_tensor(_DeviceArray(self.ptr, self.nbytes // 2), device=torch.device("cuda", self.device))
 
-    def matmul(self, a, b, Kt, bias=None, relu=False, stream=None):
+    def matmul(self, a, b, Kt, bias=None, relu=False, stream=None, method="fused", chunks=8):
         """C[rows of this rank] = A_r . B: `a` holds this rank's tile rows of A
-        (tile layout, rows[1] - rows[0] tile rows x Kt), `b` all of B."""
-        from . import matmul_tiles_gather
+        (tile layout, rows[1] - rows[0] tile rows x Kt), `b` all of B.
+        method "fused": one kernel whose pusher warps store every tile to the
+        peers; "ce": the GEMM in `chunks` row chunks, each chunk copied to
+        the peers by the copy engines while the next one computes."""
+        from . import matmul_tiles_gather, matmul_tiles_gather_ce
         m0, m1 = self.rows
         off = m0 * self.Nt * 2048
         peers = [self.bases[r] + off for r in range(self.world) if r != self.rank]
-        matmul_tiles_gather(a, b, self.ptr + off, peers, m1 - m0, Kt, self.Nt, bias=bias, relu=relu,
-                            stream=stream)
+        if method == "ce":
+            matmul_tiles_gather_ce(a, b, self.ptr + off, peers, m1 - m0, Kt, self.Nt, bias=bias, relu=relu,
+                                   chunks=chunks, stream=stream)
+        elif method == "fused":
+            matmul_tiles_gather(a, b, self.ptr + off, peers, m1 - m0, Kt, self.Nt, bias=bias, relu=relu,
+                                stream=stream)
+        else:
+            raise ValueError(f"GatheredTiles.matmul: unknown method {method!r}")
 
     def fence(self, stream=None):
         """Stream-ordered completion of every rank's work issued so far on
