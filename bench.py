@@ -527,7 +527,17 @@ def run_secondary(dist, pk):
     out["eltwise_frac_of_hbm"] = {k: v / hbm for k, v in elt.items()}
 
     # ---- conv (configs: 3x3 s1 N=1, and the batch-32 pair sharded by batch)
-    def conv_case(N, H, Cin, Cout, k, stride, pad, x=None):
+    # The per-launch figure brackets one launch with events after an L2
+    # flush; that method reads ~6 us even for an empty kernel (launch_floor).
+    # "stream" also times back-to-back launches that cycle through `sets`
+    # copies of the operands, together more than twice L2, so every launch
+    # reads inputs that other launches have evicted and the outputs' write-
+    # backs land inside the timed interval.
+    tiny = torch.zeros(1, dtype=torch.int32, device=dev)
+    floor_ms = dist.max(_timed(torch, lambda: tiny.add_(1), 20, flush))
+    l2_bytes = 126 * 2 ** 20
+
+    def conv_case(N, H, Cin, Cout, k, stride, pad, x=None, stream=False):
         Ho = (H + 2 * pad - k) // stride + 1
         x = rnd(N * H * H * Cin) if x is None else x
         w = rnd(Cout * k * k * Cin, (2.0 / (k * k * Cin)) ** 0.5)
@@ -538,14 +548,28 @@ def run_secondary(dist, pk):
         flops = 2.0 * N * Ho * Ho * Cout * k * k * Cin
         nbytes = 2.0 * (N * H * H * Cin + Cout * k * k * Cin + Cout + N * Ho * Ho * Cout)
         gbs = dist.world * nbytes / (ms / 1e3) / 1e9
-        return y, {"us": ms * 1e3, "TFLOPs": dist.world * flops / (ms / 1e3) / 1e12,
-                   "hbm_GBps": gbs, "hbm_frac": gbs / (dist.world * hbm), "bound": "hbm",
-                   "algorithmic_bytes_per_rank": nbytes, "flops_per_rank": flops}
+        res = {"us": ms * 1e3, "TFLOPs": dist.world * flops / (ms / 1e3) / 1e12,
+               "hbm_GBps": gbs, "hbm_frac": gbs / (dist.world * hbm), "bound": "hbm",
+               "algorithmic_bytes_per_rank": nbytes, "flops_per_rank": flops}
+        if stream:
+            sets = max(2, int(-(-2 * l2_bytes // nbytes)))
+            ops = [(x, y)] + [(rnd(N * H * H * Cin), torch.empty_like(y)) for _ in range(sets - 1)]
+            it = iter(range(1 << 30))
+
+            def nxt():
+                xi, yi = ops[next(it) % sets]
+                ttfoil.conv2d_nhwc(xi, w, b, yi, N, H, H, Cin, Cout, k, k, stride, pad, relu=True)
+            sms = dist.max(_timed(torch, nxt, 10 * sets, warmup=sets))
+            sg = dist.world * nbytes / (sms / 1e3) / 1e9
+            res["stream"] = {"us": sms * 1e3, "hbm_GBps": sg, "hbm_frac": sg / (dist.world * hbm),
+                             "operand_sets": sets, "footprint_bytes": sets * nbytes}
+            del ops
+        return y, res
 
     _, c2 = conv_case(1, 56, 64, 64, 3, 1, 1)
     nb = max(1, 32 // dist.world)
-    y1, c3a = conv_case(nb, 112, 64, 128, 3, 2, 1)
-    _, c3b = conv_case(nb, 56, 128, 256, 1, 1, 0, x=y1)
+    y1, c3a = conv_case(nb, 112, 64, 128, 3, 2, 1, stream=True)
+    _, c3b = conv_case(nb, 56, 128, 256, 1, 1, 0, x=y1, stream=True)
     pair_us = c3a["us"] + c3b["us"]
     pair_flops = dist.world * (c3a["flops_per_rank"] + c3b["flops_per_rank"])
     out["conv"] = {"conv3x3_s1_56x56x64_n1": c2,
@@ -553,7 +577,10 @@ def run_secondary(dist, pk):
                    "conv1x1_56x56x128to256": dict(c3b, batch_per_rank=nb),
                    "pair_TFLOPs": pair_flops / (pair_us / 1e6) / 1e12,
                    "pair_us": pair_us, "global_batch": nb * dist.world,
-                   "l2": "flushed before each timed launch (256 MiB written, another 256 MiB read)"}
+                   "launch_floor_us": floor_ms * 1e3,
+                   "l2": "flushed before each timed launch (256 MiB written, another 256 MiB read); "
+                         "launch_floor_us: a one-element torch kernel timed the same way; 'stream': "
+                         "back-to-back launches over operand copies totalling more than twice L2"}
 
     # ---- GEMM sweep (config 4): square per rank, tall M-sharded
     sweep = {}

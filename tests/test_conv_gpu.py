@@ -179,6 +179,11 @@ VARIANTS = {
     "single": {"FOIL_CONV_PRODUCER": "single"},
     "pair": {"FOIL_CONV_PRODUCER": "pair"},
     "plane": {"FOIL_CONV_PRODUCER": "plane"},
+    # epilogue store paths: rows straight from registers, or staged for
+    # tensor stores (each kernel's default is the other one for some shapes)
+    "single_direct": {"FOIL_CONV_PRODUCER": "single", "FOIL_CONV_EPILOGUE": "direct"},
+    "pair_staged": {"FOIL_CONV_PRODUCER": "pair", "FOIL_CONV_EPILOGUE": "staged"},
+    "gather_direct": {"FOIL_CONV_PRODUCER": "gather", "FOIL_CONV_EPILOGUE": "direct"},
 }
 
 VARIANT_CASES = [  # x shape, w shape, stride, pad
@@ -263,11 +268,13 @@ def variant_inputs(env, tmp_path_factory):
     return script, cases
 
 
-@pytest.mark.parametrize("variant", ["gather", "single", "pair", "plane"])
+@pytest.mark.parametrize("variant", ["gather", "single", "pair", "plane", "single_direct", "pair_staged",
+                                     "gather_direct"])
 def test_kernel_variants(variant_inputs, tmp_path, variant):
     """The im2col kernels (gather producer, single-CTA tensor copies, 2-SM
     weight-stationary pair) feed identical operand tiles in the same K order,
-    so each reproduces the default path's output bit for bit on every case.
+    and both epilogue store paths write the same values, so each reproduces
+    the default path's output bit for bit on every case.
     The plane kernel sums the same products in plane order: where it serves
     a case, its output is checked against the oracle."""
     script, cases = variant_inputs

@@ -42,9 +42,13 @@
 // copy per ~295 ns, nearly independent of the box size up to 128-256 rows
 // and of how many copies are in flight or how many SMs issue them.  So copy
 // INSTRUCTIONS are the budget: a 128-row im2col of 16 KiB moves ~56 GB/s per
-// SM, a 256-row one twice that.  Hence the weight-stationary pair kernel
-// (no weight copies per k-block, 256-row im2col copies) and epilogue stores
-// of whole 128-row boxes.  Every wait is bounded (see gemm_ptx.cuh).
+// SM, a 256-row one twice that.  Hence the weight-stationary pair kernel (no
+// weight copies per k-block, 256-row im2col copies).  A per-role trace of
+// that kernel (3x3 stride 2, batch 32) showed each 32 KiB stride-2 im2col
+// copy taking ~0.9 us from issue to completion, one completing every
+// ~0.5 us, so the number of stages in flight sets its pace; its epilogue
+// therefore stores from registers and gives the staging buffer to a fourth
+// stage.  Every wait is bounded (see gemm_ptx.cuh).
 #include <cuda.h>
 #include <cudaTypedefs.h>
 
@@ -84,17 +88,20 @@ struct Params {
     uint32_t m_blocks, n_blocks;
     int relu;
     uint32_t box_cols;     // columns of the output tensor map's box (must equal Epi<BN>::kCols)
+    uint32_t direct;       // pair kernel: epilogue stores rows from registers (no staging)
+    uint32_t wide_y;       // y 32-byte aligned: 256-bit stores in the direct epilogue
     uint32_t* err;
     uint64_t wait_ns;      // wall-time limit of each bounded wait
 };
 
-template <int BN>
+template <int BN, bool kDirect = false>
 struct Cfg {
     static constexpr int kABytes = 128 * 128;               // 128 rows x 64 ch x 2 B (max kc)
     static constexpr int kBBytes = BN * 128;                // BN rows x 64 ch x 2 B
     static constexpr int kStageBytes = kABytes + kBBytes;
-    // Epilogue staging: 8 warps x 32 rows x BN/2 columns (see Epi).
-    static constexpr int kStagingBytes = 256 * BN;
+    // Epilogue staging: 8 warps x 32 rows x BN/2 columns (see Epi); none when
+    // the epilogue stores from registers.
+    static constexpr int kStagingBytes = kDirect ? 0 : 256 * BN;
     static constexpr int kLimit = 220 * 1024;
     static constexpr int kFit = (kLimit - kStagingBytes - 1024 - kBarrierBytes) / kStageBytes;
     static constexpr int kStages = kFit > 8 ? 8 : kFit;
@@ -231,6 +238,62 @@ __device__ __forceinline__ void epilogue_rows(const Params& p, const CUtensorMap
     }
 }
 
+// The same share of an accumulator tile stored straight from registers: lane
+// = output row, each 32-column chunk is 64 contiguous bytes of that row,
+// written as two 32-byte stores (whole L2 sectors) or, for a y that is only
+// 16-byte aligned, four 16-byte stores.  Needs no staging buffer, so the
+// pair kernel can keep one more operand stage in flight.
+template <int BN, class Release>
+__device__ __forceinline__ void epilogue_rows_direct(const Params& p, uint32_t t_row, uint32_t m0, uint32_t co0,
+                                                     int mode, uint32_t lane, uint32_t m_end, Release release) {
+    constexpr int kChunks = BN / 64;
+    const uint32_t m = m0 + lane;
+    const bool row_ok = m < m_end;
+    uint16_t* yrow = p.y + (uint64_t)(row_ok ? m : 0u) * p.Cout;
+    const bool want_bias = mode != 0 && p.bias != nullptr;
+    uint32_t v[2][32], bw[2][16];
+    load_bias32(p, co0, want_bias, bw[0]);
+    tmem_ld32(t_row, v[0]);
+#pragma unroll
+    for (int ci = 0; ci < kChunks; ++ci) {
+        tmem_ld_wait();
+        if (ci + 1 < kChunks) {
+            tmem_ld32(t_row + 32u * (ci + 1), v[(ci + 1) & 1]);
+            load_bias32(p, co0 + 32u * (ci + 1), want_bias, bw[(ci + 1) & 1]);
+        }
+        if (ci + 1 == kChunks) release();
+        const uint32_t* c = v[ci & 1];
+        const uint32_t* b = bw[ci & 1];
+        uint32_t o[16];
+        if (mode == 0) {
+#pragma unroll
+            for (int i = 0; i < 16; ++i) o[i] = epi_pair(c[2 * i], c[2 * i + 1], 0u, 0);
+        } else if (mode == 1) {
+#pragma unroll
+            for (int i = 0; i < 16; ++i) o[i] = epi_pair(c[2 * i], c[2 * i + 1], b[i], 1);
+        } else {
+#pragma unroll
+            for (int i = 0; i < 16; ++i) o[i] = epi_pair(c[2 * i], c[2 * i + 1], b[i], 2);
+        }
+        const uint32_t co = co0 + 32u * (uint32_t)ci;
+        if (row_ok) {
+#pragma unroll
+            for (int h = 0; h < 2; ++h) {
+                if (co + 16u * h < p.Cout) {
+                    uint16_t* dst = yrow + co + 16u * h;
+                    if (p.wide_y) {
+                        st_global_v8(dst, o + 8 * h);
+                    } else {
+                        uint4* d4 = reinterpret_cast<uint4*>(dst);
+                        d4[0] = make_uint4(o[8 * h], o[8 * h + 1], o[8 * h + 2], o[8 * h + 3]);
+                        d4[1] = make_uint4(o[8 * h + 4], o[8 * h + 5], o[8 * h + 6], o[8 * h + 7]);
+                    }
+                }
+            }
+        }
+    }
+}
+
 // Bounded wait for the copies of the last `stages` of `issued` loads (load
 // j completes phase (j / stages) & 1 of full[j % stages]); phases that have
 // completed return at once.
@@ -240,11 +303,11 @@ __device__ __forceinline__ void drain_loads(uint64_t* full, uint32_t issued, uin
     for (uint32_t j = j0; j < issued; ++j) mbar_drain(&full[j % stages], (j / stages) & 1u, 100000000ull);
 }
 
-template <int BN, bool kTma>
+template <int BN, bool kTma, bool kDirect>
 __global__ void __launch_bounds__(kThreads, 1)
     conv_kernel(const Params p, const __grid_constant__ CUtensorMap tmap_x,
                 const __grid_constant__ CUtensorMap tmap_w, const __grid_constant__ CUtensorMap tmap_y) {
-    using C = Cfg<BN>;
+    using C = Cfg<BN, kDirect>;
     extern __shared__ uint8_t smem_raw[];
     uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) &
                                                ~uintptr_t(1023));
@@ -488,12 +551,17 @@ __global__ void __launch_bounds__(kThreads, 1)
             if (!ok) break;
             tc_fence_after();
             uint64_t* te = &tempty[acc];
-            epilogue_rows<BN>(p, &tmap_y, tmem_base + ((qd * 32u) << 16) + acc * BN + col0, mb * 128u + qd * 32u,
-                              nb * BN + col0, stg, mode, lane, p.M, [&] {
-                                  tc_fence_before();
-                                  __syncwarp();
-                                  if (lane == 0) mbar_arrive(te);
-                              });
+            auto release = [&] {
+                tc_fence_before();
+                __syncwarp();
+                if (lane == 0) mbar_arrive(te);
+            };
+            const uint32_t t_row = tmem_base + ((qd * 32u) << 16) + acc * BN + col0;
+            if constexpr (kDirect)
+                epilogue_rows_direct<BN>(p, t_row, mb * 128u + qd * 32u, nb * BN + col0, mode, lane, p.M, release);
+            else
+                epilogue_rows<BN>(p, &tmap_y, t_row, mb * 128u + qd * 32u, nb * BN + col0, stg, mode, lane, p.M,
+                                  release);
             if (++acc == 2) {
                 acc = 0;
                 acc_phase ^= 1u;
@@ -550,7 +618,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
     uint8_t* b_res = smem;
     uint8_t* a_st = b_res + p.num_kb * PC::kHalfB;
     uint8_t* staging = a_st + stages * PC::kABytes;
-    uint64_t* full = reinterpret_cast<uint64_t*>(staging + 256u * BN);
+    uint64_t* full = reinterpret_cast<uint64_t*>(staging + (p.direct ? 0u : 256u * BN));
     uint64_t* empty = full + kPairMaxStages;
     uint64_t* tfull = empty + kPairMaxStages;
     uint64_t* tempty = tfull + 2;
@@ -719,13 +787,17 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
 #pragma unroll 1
             for (int sub = 0; sub < kSub; ++sub) {
                 const uint32_t m0 = (tile * 2u + rank) * (128u * kSub) + 128u * sub + qd * 32u;
-                epilogue_rows<BN>(p, &tmap_y,
-                                  tmem_base + ((qd * 32u) << 16) + acc * (uint32_t)(kSub * BN) + sub * BN + col0, m0,
-                                  col0, stg, mode, lane, p.M, [&] {
-                                      tc_fence_before();
-                                      __syncwarp();
-                                      if (lane == 0) mbar_arrive_remote_relaxed(te);
-                                  });
+                const uint32_t t_row =
+                    tmem_base + ((qd * 32u) << 16) + acc * (uint32_t)(kSub * BN) + sub * BN + col0;
+                auto release = [&] {
+                    tc_fence_before();
+                    __syncwarp();
+                    if (lane == 0) mbar_arrive_remote_relaxed(te);
+                };
+                if (p.direct)
+                    epilogue_rows_direct<BN>(p, t_row, m0, col0, mode, lane, p.M, release);
+                else
+                    epilogue_rows<BN>(p, &tmap_y, t_row, m0, col0, stg, mode, lane, p.M, release);
             }
             if (++acc == 2) {
                 acc = 0;
@@ -1025,17 +1097,17 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
     }
 }
 
-template <int BN, bool kTma>
+template <int BN, bool kTma, bool kDirect>
 static int launch_bn(const Params& p, const CUtensorMap& mx, const CUtensorMap& mw,
                      const CUtensorMap& my, cudaStream_t stream, int max_ctas) {
-    using C = Cfg<BN>;
-    if (foil_smem_optin((const void*)conv_kernel<BN, kTma>, C::kSmemBytes) != cudaSuccess) {
+    using C = Cfg<BN, kDirect>;
+    if (foil_smem_optin((const void*)conv_kernel<BN, kTma, kDirect>, C::kSmemBytes) != cudaSuccess) {
         foil_set_error(FOIL_ERR_CUDA, "foil_conv2d_nhwc: cudaFuncSetAttribute failed");
         return FOIL_ERR_CUDA;
     }
     const uint32_t tiles = p.m_blocks * p.n_blocks;
     const uint32_t grid = tiles < (uint32_t)max_ctas ? tiles : (uint32_t)max_ctas;
-    conv_kernel<BN, kTma><<<grid, kThreads, C::kSmemBytes, stream>>>(p, mx, mw, my);
+    conv_kernel<BN, kTma, kDirect><<<grid, kThreads, C::kSmemBytes, stream>>>(p, mx, mw, my);
     cudaError_t e = cudaGetLastError();
     if (e != cudaSuccess) {
         char buf[200];
@@ -1051,8 +1123,8 @@ static int launch_bn(const Params& p, const CUtensorMap& mx, const CUtensorMap& 
 // epilogue staging, barriers (+ 1 KiB alignment slack).
 static uint32_t pair_smem_bytes(const Params& p, int bn, uint32_t stages) {
     const uint32_t sub = bn <= 128 ? 2u : 1u;
-    return p.num_kb * (uint32_t)(bn / 2) * 128u + stages * sub * 16384u + 256u * (uint32_t)bn + 1024u +
-           (uint32_t)kBarrierBytes;
+    return p.num_kb * (uint32_t)(bn / 2) * 128u + stages * sub * 16384u + (p.direct ? 0u : 256u * (uint32_t)bn) +
+           1024u + (uint32_t)kBarrierBytes;
 }
 
 template <int BN>
@@ -1188,10 +1260,17 @@ static int launch_plane(const Params& p, const PlaneGeo& g, uint32_t smem, const
 template <bool kTma>
 static int launch_tiles(const Params& p, int bn, const CUtensorMap& mx, const CUtensorMap& mw,
                         const CUtensorMap& my, cudaStream_t stream, int max_ctas) {
+    if (p.direct) {
+        switch (bn) {
+            case 64: return launch_bn<64, kTma, true>(p, mx, mw, my, stream, max_ctas);
+            case 128: return launch_bn<128, kTma, true>(p, mx, mw, my, stream, max_ctas);
+            default: return launch_bn<256, kTma, true>(p, mx, mw, my, stream, max_ctas);
+        }
+    }
     switch (bn) {
-        case 64: return launch_bn<64, kTma>(p, mx, mw, my, stream, max_ctas);
-        case 128: return launch_bn<128, kTma>(p, mx, mw, my, stream, max_ctas);
-        default: return launch_bn<256, kTma>(p, mx, mw, my, stream, max_ctas);
+        case 64: return launch_bn<64, kTma, false>(p, mx, mw, my, stream, max_ctas);
+        case 128: return launch_bn<128, kTma, false>(p, mx, mw, my, stream, max_ctas);
+        default: return launch_bn<256, kTma, false>(p, mx, mw, my, stream, max_ctas);
     }
 }
 
@@ -1356,6 +1435,17 @@ int launch(const uint16_t* x, const uint16_t* w, const uint16_t* bias, uint16_t*
     p.err = err;
     p.wait_ns = foil_wait_limit_ns();
     p.m_blocks = (p.M + 127) / 128;
+    // Epilogue store path: the pair kernel stores rows from registers by
+    // default (its staging buffer then holds a fourth operand stage: 3x3
+    // stride-2 batch 32, L2 flushed, 27.7-27.9 against 28.9-29.3 us), the
+    // single-CTA kernel stages for tensor stores (1x1 batch 32: 20.5-20.7
+    // against 27.2-27.5 us from registers).  FOIL_CONV_EPILOGUE=direct or
+    // staged forces one path (tests compare both).
+    const char* ep = getenv("FOIL_CONV_EPILOGUE");
+    const bool force_direct = ep != nullptr && strcmp(ep, "direct") == 0;
+    const bool force_staged = ep != nullptr && strcmp(ep, "staged") == 0;
+    p.wide_y = ((uintptr_t)y & 31u) == 0 ? 1u : 0u;
+    p.direct = force_staged ? 0u : 1u;  // the pair kernel's default
     // Column tile: the smallest of 64 / 128 / 256 covering Cout, else 256.
     const int bn = Cout <= 64 ? 64 : (Cout <= 128 ? 128 : 256);
     p.n_blocks = (Cout + bn - 1) / bn;
@@ -1402,9 +1492,12 @@ int launch(const uint16_t* x, const uint16_t* w, const uint16_t* bias, uint16_t*
                                              "does not serve this shape");
         return FOIL_ERR_UNSUPPORTED;
     }
-    if (!tc) return launch_tiles<false>(p, bn, mx, mw, my, stream, max_ctas);
+    if (!tc) {
+        p.direct = force_direct ? 1u : 0u;
+        return launch_tiles<false>(p, bn, mx, mw, my, stream, max_ctas);
+    }
     // Weight-stationary pair kernel: one column block, more than one 128-row
-    // block, and at least 4 A stages beside the resident weights.
+    // block, and at least 3 A stages beside the resident weights.
     uint32_t stages = 0;
     while (stages < (uint32_t)kPairMaxStages && pair_smem_bytes(p, bn, stages + 1) <= (uint32_t)optin) ++stages;
     // The pair kernel pays ~1 us more start-up (cluster launch, resident
@@ -1433,6 +1526,7 @@ int launch(const uint16_t* x, const uint16_t* w, const uint16_t* bias, uint16_t*
             default: return launch_pair<256>(q, stages, mx, mw, my, stream, max_ctas, optin);
         }
     }
+    p.direct = force_direct ? 1u : 0u;
     return launch_tiles<true>(p, bn, mx, mw, my, stream, max_ctas);
 }
 
