@@ -16,7 +16,9 @@ value      TFLOP/s over all ranks, operands resident in HBM, CUDA events on the
            launching stream, max over ranks.
 value_with_gather  (N > 1) the same step with the global C reassembled on every
            rank: the best of GEMM + ncclAllGather, the fused GEMM that stores
-           each tile to every rank's copy over NVLink, and the GEMM in row
+           each tile to every rank's copy over NVLink (per peer; with
+           --gather-multicast also once through an NVLink multicast
+           address), and the GEMM in row
            chunks whose finished chunks the copy engines send to the peers
            while the next chunk computes, with the achieved NVLink GB/s
            against the link floor.
@@ -83,6 +85,9 @@ def parse():
     ap.add_argument("--no-e2e", action="store_true")
     ap.add_argument("--gather-chunks", type=int, default=8,
                     help="row chunks of the copy-engine reassembly path (N > 1)")
+    ap.add_argument("--gather-multicast", action="store_true",
+                    help="also time the NVLink-multicast reassembly path (N > 1; measured slower: "
+                         "2.77 against 1.68 ms per step at 8 GPUs)")
     return ap.parse_args()
 
 
@@ -395,7 +400,10 @@ def run_ours(args, dist):
     with_gather = None
     if dist.world > 1:
         allgather = time_allgather(dist, c, ms / args.steps, flops)
-        for key, method in (("fused", "fused"), ("copy_engines", "ce")):
+        methods = [("fused", "fused"), ("copy_engines", "ce")]
+        if args.gather_multicast:
+            methods.append(("multicast", "multicast"))
+        for key, method in methods:
             try:
                 allgather[key] = time_fused_gather(dist, a, b, Mt, Kt, Nt, flops, method=method,
                                                    chunks=args.gather_chunks)
@@ -405,15 +413,16 @@ def run_ours(args, dist):
         recv = (dist.world - 1) * shard_bytes  # C bytes every GPU must receive per step
         link_gbs = 770.0  # measured peer copy per direction per GPU on this pool
         nccl_ms = ms / args.steps + allgather["ms"]
-        step_of = lambda k: allgather[k].get("ms_per_step")
-        fused_ms, ce_ms = step_of("fused"), step_of("copy_engines")
-        paths = {"ncclAllGather": nccl_ms, "fused": fused_ms, "copy_engines": ce_ms}
+        step_of = lambda k: allgather.get(k, {}).get("ms_per_step")
+        fused_ms, ce_ms, mc_ms = step_of("fused"), step_of("copy_engines"), step_of("multicast")
+        paths = {"ncclAllGather": nccl_ms, "fused": fused_ms, "multicast": mc_ms, "copy_engines": ce_ms}
         best = min((v, k) for k, v in paths.items() if v is not None)[1]
         step_ms = paths[best]
         with_gather = {
             "value": dist.world * flops / (step_ms / 1e3) / 1e12, "unit": "TFLOP/s", "ms_per_step": step_ms,
             "path": best, "nccl_ms_per_step": nccl_ms, "fused_ms_per_step": fused_ms,
-            "copy_engines_ms_per_step": ce_ms,
+            "copy_engines_ms_per_step": ce_ms, "multicast_ms_per_step": mc_ms,
+            "nvlink_GBps_multicast": recv / (mc_ms / 1e3) / 1e9 if mc_ms else None,
             "received_bytes_per_gpu": recv,
             "nvlink_GBps_fused": recv / (fused_ms / 1e3) / 1e9 if fused_ms else None,
             "nvlink_GBps_copy_engines": recv / (ce_ms / 1e3) / 1e9 if ce_ms else None,
@@ -698,12 +707,17 @@ def time_fused_gather(dist, a, b, Mt, Kt, Nt, flops, method="fused", chunks=8):
     import torch
     import ttfoil
     from ttfoil import shard
-    g = shard.GatheredTiles(Mt * dist.world, Nt)
+    if method == "multicast":
+        g = shard.MulticastTiles(Mt * dist.world, Nt)
+        mm = lambda: g.matmul(a, b, Kt)
+    else:
+        g = shard.GatheredTiles(Mt * dist.world, Nt)
+        mm = lambda: g.matmul(a, b, Kt, method=method, chunks=chunks)
     try:
         assert g.rows == (dist.rank * Mt, (dist.rank + 1) * Mt)
 
         def step():
-            g.matmul(a, b, Kt, method=method, chunks=chunks)
+            mm()
             g.fence()
 
         for _ in range(3):
@@ -730,12 +744,15 @@ def time_fused_gather(dist, a, b, Mt, Kt, Nt, flops, method="fused", chunks=8):
         consistent = bool(torch.equal(sums, ref))
     finally:
         g.close()
-    note = ("one GEMM kernel per rank that also stores each C tile to every peer GPU's copy "
-            "over NVLink (256x512 pair tiles; four pusher warps copy finished tiles to the peers "
-            "while later tiles compute), plus a one-element all-reduce") if method == "fused" else (
-        f"the GEMM as {chunks} row-chunk launches per rank; one copy stream per peer copies each "
-        "finished chunk over NVLink (copy engines) while the next chunk computes, plus a one-element "
-        "all-reduce")
+    note = {"fused": "one GEMM kernel per rank that also stores each C tile to every peer GPU's copy "
+                     "over NVLink (256x512 pair tiles; four pusher warps copy finished tiles to the peers "
+                     "while later tiles compute), plus a one-element all-reduce",
+            "multicast": "the same kernel whose pusher warps store each C tile once through an NVLink "
+                         "multicast address (PyTorch symmetric memory); the NVSwitch writes it into every "
+                         "GPU's copy; plus a one-element all-reduce",
+            "ce": f"the GEMM as {chunks} row-chunk launches per rank; one copy stream per peer copies each "
+                  "finished chunk over NVLink (copy engines) while the next chunk computes, plus a "
+                  "one-element all-reduce"}[method]
     out = {"ms_per_step": ms, "value_TFLOPs": dist.world * flops / (ms / 1e3) / 1e12,
            "copies_consistent": consistent, "note": note}
     if method == "ce":

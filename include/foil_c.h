@@ -281,6 +281,16 @@ FOIL_API int foil_matmul_tiles_gather_dev(const uint16_t* a, const uint16_t* b, 
                           uint32_t Mt, uint32_t Kt, uint32_t Nt,
                           const uint16_t* bias, int32_t relu, void* stream);
 
+/* foil_matmul_tiles_gather_dev through an NVLink multicast object: `mc_c`
+ * is the multicast address, at c's offset, of a buffer bound on every GPU of
+ * the node (this one included; e.g. PyTorch symmetric memory's
+ * multicast_ptr).  Each output tile is stored once through it and the
+ * NVSwitch writes it into every GPU's copy.  The same fence as for
+ * foil_matmul_tiles_gather_dev orders the ranks. */
+FOIL_API int foil_matmul_tiles_gather_mc_dev(const uint16_t* a, const uint16_t* b, uint16_t* c,
+                          uint16_t* mc_c, uint32_t Mt, uint32_t Kt, uint32_t Nt,
+                          const uint16_t* bias, int32_t relu, void* stream);
+
 /* The same result as foil_matmul_tiles_gather_dev, with the transfer on the
  * copy engines instead of the SMs: the GEMM runs as `chunks` launches over
  * row chunks of C (whole 256-row blocks, 1..64 chunks) on `stream`, and as

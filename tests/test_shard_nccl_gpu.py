@@ -8,7 +8,8 @@
   warps): after the fence, both copies equal the per-rank results of the
   plain GEMM concatenated (bit for bit, same kernels), and the oracle on
   sampled rows; likewise with the GEMM in row chunks whose finished chunks
-  the copy engines push to the peer ("ce").
+  the copy engines push to the peer ("ce"), and with every tile stored once
+  through an NVLink multicast address (skipped without multicast support).
 """
 import datetime
 import os
@@ -139,6 +140,55 @@ def gather_worker(rank, world, port, q):
         dist.destroy_process_group()
 
 
+def mc_worker(rank, world, port, q):
+    """MulticastTiles: the tiles stored once through the NVLink multicast
+    address equal the plain GEMM's shards on both GPUs, bit for bit."""
+    import sys
+    repo = os.path.dirname(os.path.dirname(os.path.abspath(__file__)))
+    sys.path[:0] = [repo, os.path.join(repo, "tt-foil_b200")]
+    os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port))
+    import torch
+    import torch.distributed as dist
+    from oracle import oracle
+    import ttfoil
+    from ttfoil import shard
+    torch.cuda.set_device(rank)
+    dist.init_process_group("nccl", rank=rank, world_size=world, timeout=datetime.timedelta(seconds=60),
+                            device_id=torch.device("cuda", rank))
+    ok = []
+    try:
+        for (Mt, Kt, Nt) in ((25, 16, 8), (19, 12, 24), (3, 4, 24)):
+            a_all = oracle.rand_bf16(Mt * Kt * 1024, 80 + Nt + Mt)
+            b = oracle.rand_bf16(Kt * Nt * 1024, 81 + Nt + Mt)
+            dev = lambda arr: torch.from_numpy(np.ascontiguousarray(arr).view(np.int16)).cuda()
+            try:
+                g = shard.MulticastTiles(Mt, Nt)
+            except RuntimeError as e:
+                q.put((rank, True, ["skip: " + str(e)[:200]]))
+                return
+            m0, m1 = g.rows
+            a_r = dev(a_all[m0 * Kt * 1024:m1 * Kt * 1024])
+            b_d = dev(b)
+            g.tensor().fill_(0x7fff)
+            torch.cuda.synchronize()
+            dist.barrier()
+            g.matmul(a_r, b_d, Kt)
+            g.fence()
+            torch.cuda.synchronize()
+            full = g.tensor().cpu().numpy().view(np.uint16).copy()
+            c_r = torch.empty((m1 - m0) * Nt * 1024, dtype=torch.int16, device="cuda")
+            ttfoil.matmul_tiles(a_r, b_d, c_r, m1 - m0, Kt, Nt)
+            torch.cuda.synchronize()
+            parts = [None] * world
+            dist.all_gather_object(parts, c_r.cpu().numpy().view(np.uint16))
+            ok.append(bool(np.array_equal(full, np.concatenate(parts))))
+            ok.append(ttfoil.device_error() == 0)
+            g.close()
+        q.put((rank, all(ok), ok))
+    finally:
+        dist.destroy_process_group()
+
+
 def run_two(target):
     import torch
     if torch.cuda.device_count() < 2:
@@ -160,6 +210,14 @@ def run_two(target):
 def test_gemm_is_its_own_allgather_two_gpus():
     res = run_two(gather_worker)
     assert all(r[1] for r in res), res
+
+
+def test_gemm_allgather_through_multicast_two_gpus():
+    res = run_two(mc_worker)
+    assert all(r[1] for r in res), res
+    skipped = [r for r in res if r[2] and str(r[2][0]).startswith("skip")]
+    if skipped:
+        pytest.skip(skipped[0][2][0])
 
 
 def test_row_sharded_conv_two_gpus():

@@ -879,6 +879,24 @@ extern "C" int foil_matmul_tiles_gather_dev(const uint16_t* a, const uint16_t* b
     });
 }
 
+// ------------------------------- GEMM whose tiles go out through multicast ---
+extern "C" int foil_matmul_tiles_gather_mc_dev(const uint16_t* a, const uint16_t* b, uint16_t* c, uint16_t* mc_c,
+                                               uint32_t Mt, uint32_t Kt, uint32_t Nt, const uint16_t* bias,
+                                               int32_t relu, void* stream) {
+    return guarded([&] {
+        if (!mc_c || !aligned16(mc_c))
+            throw FoilError(FOIL_ERR_INVALID, "foil_matmul_tiles_gather_mc_dev: null or misaligned multicast address");
+        if (Mt == 0 || Kt == 0 || Nt == 0) return;
+        if (Mt > 65535 || Kt > 65535 || Nt > 65535)
+            throw FoilError(FOIL_ERR_INVALID, "foil_matmul_tiles_gather_mc_dev: tile counts must be <= 65535");
+        if (!a || !b || !c || !aligned16(a) || !aligned16(b) || !aligned16(c) || (bias && !aligned16(bias)))
+            throw FoilError(FOIL_ERR_INVALID, "foil_matmul_tiles_gather_mc_dev: null or misaligned pointer");
+        uint32_t* err = error_word_for_current_device();
+        throw_status(foil::gemm::launch(a, b, c, Mt, Kt, Nt, bias, relu, err, (cudaStream_t)stream,
+                                        sm_count_current(), nullptr, 0, mc_c));
+    });
+}
+
 // ------------------------ GEMM in row chunks, copy engines push to the peers ---
 // Per device: one copy stream per peer and the events that order each copy
 // after the GEMM launch of its chunk (reused under the device's lock).

@@ -264,6 +264,16 @@ __device__ __forceinline__ void st_global_v8(void* p, const uint32_t* w) {
                  : "memory");
 }
 
+// 16-byte store through an NVLink multicast address (multimem): the one
+// store reaches the same offset of every GPU's buffer bound to the multicast
+// object, replicated by the NVSwitch.  16-byte aligned; the words are bf16
+// pairs, stored unchanged.
+__device__ __forceinline__ void st_multimem_v4(void* p, uint32_t a, uint32_t b, uint32_t c, uint32_t d) {
+    asm volatile("multimem.st.relaxed.sys.global.v4.bf16x2 [%0], {%1, %2, %3, %4};" ::"l"(p), "r"(a), "r"(b),
+                 "r"(c), "r"(d)
+                 : "memory");
+}
+
 // 256-bit global load through L2 only (no L1 allocation), 32-byte aligned.
 __device__ __forceinline__ void ld_global_cg_v8(const void* p, uint32_t* w) {
     asm volatile("ld.global.cg.v8.b32 {%0, %1, %2, %3, %4, %5, %6, %7}, [%8];"

@@ -101,6 +101,9 @@ struct Params {
     // tile is also stored there, so the kernel is its own all-gather.
     uint16_t* peer_c[kMaxPeers];
     uint32_t npeers;
+    // Or: an NVLink multicast address of C (same layout as c), bound to every
+    // GPU's copy; one multimem store per 16 bytes reaches all of them.
+    uint16_t* mc_c;
     uint32_t wide_stores;  // c and every peer_c 32-byte aligned: 256-bit stores
     uint64_t wait_ns;      // wall-time limit of each bounded wait
 };
@@ -172,7 +175,12 @@ __device__ __forceinline__ void store_tile_row(const Params& p, uint32_t t_row, 
             // lines, also over NVLink for the peer copies).
             // (Buffers only 16-byte aligned take two 128-bit stores per row.)
             const uint64_t t0 = ((uint64_t)mt * p.Nt + nt) * 1024u + fr * 512u + r0 * 16u;
-            if (p.wide_stores) {
+            if (kPeers && p.mc_c) {
+                st_multimem_v4(p.mc_c + t0, o[0], o[1], o[2], o[3]);
+                st_multimem_v4(p.mc_c + t0 + 8u, o[4], o[5], o[6], o[7]);
+                st_multimem_v4(p.mc_c + t0 + 256u, o[8], o[9], o[10], o[11]);
+                st_multimem_v4(p.mc_c + t0 + 264u, o[12], o[13], o[14], o[15]);
+            } else if (p.wide_stores) {
                 st_global_v8(p.c + t0, o);
                 st_global_v8(p.c + t0 + 256u, o + 8);
 #pragma unroll
@@ -380,7 +388,7 @@ __device__ __forceinline__ void gemm_tiles_body(const Params& p, uint32_t cta, u
         }
         // Peer copies of C: make this thread's remote stores visible
         // system-wide before the kernel's completion is observed.
-        if (p.npeers) __threadfence_system();
+        if (p.npeers || p.mc_c) __threadfence_system();
     }
 
     tc_fence_before();
@@ -532,6 +540,7 @@ int launch_cores(const CoreProgram* cores, uint32_t ncores, uint32_t* err, uint3
         p.err = err;
         p.wait_ns = foil_wait_limit_ns();
         p.npeers = 0;
+        p.mc_c = nullptr;
         p.wide_stores = ((uintptr_t)p.c & 31u) == 0 ? 1u : 0u;
     }
     L.err = err;
@@ -780,7 +789,7 @@ gemm_pair_kernel(const Params p) {
         }
         // Peer copies of C: make this thread's remote stores visible
         // system-wide before the kernel's completion is observed.
-        if (p.npeers) __threadfence_system();
+        if (p.npeers || p.mc_c) __threadfence_system();
     }
 
     tc_fence_before();
@@ -850,7 +859,7 @@ gemm_pair_wide_kernel(const Params p) {
     const uint32_t rank = cluster_ctarank();
     const bool leader = rank == 0;
     const uint32_t pair_id = blockIdx.x >> 1, num_pairs = gridDim.x >> 1;
-    const bool pushers = blockDim.x == (uint32_t)kWThreadsPush && p.npeers > 0;
+    const bool pushers = blockDim.x == (uint32_t)kWThreadsPush && (p.npeers > 0 || p.mc_c != nullptr);
 
     if (threadIdx.x == 0) {
         *epi_done = 0u;
@@ -1058,13 +1067,23 @@ gemm_pair_wide_kernel(const Params p) {
 #pragma unroll
                 for (int u = 0; u < 4; ++u)
                     if (i + 32u * u < n32) ld_global_cg_v8(p.c + e0 + (uint64_t)(i + 32u * u) * 16u, w[u]);
+                if (p.mc_c) {
 #pragma unroll
-                for (uint32_t d = 0; d < kMaxPeers; ++d) {
-                    if (d < p.npeers) {
+                    for (int u = 0; u < 4; ++u)
+                        if (i + 32u * u < n32) {
+                            uint16_t* dst = p.mc_c + e0 + (uint64_t)(i + 32u * u) * 16u;
+                            st_multimem_v4(dst, w[u][0], w[u][1], w[u][2], w[u][3]);
+                            st_multimem_v4(dst + 8, w[u][4], w[u][5], w[u][6], w[u][7]);
+                        }
+                } else {
 #pragma unroll
-                        for (int u = 0; u < 4; ++u)
-                            if (i + 32u * u < n32)
-                                st_global_v8(p.peer_c[d] + e0 + (uint64_t)(i + 32u * u) * 16u, w[u]);
+                    for (uint32_t d = 0; d < kMaxPeers; ++d) {
+                        if (d < p.npeers) {
+#pragma unroll
+                            for (int u = 0; u < 4; ++u)
+                                if (i + 32u * u < n32)
+                                    st_global_v8(p.peer_c[d] + e0 + (uint64_t)(i + 32u * u) * 16u, w[u]);
+                        }
                     }
                 }
             }
@@ -1085,7 +1104,7 @@ gemm_pair_wide_kernel(const Params p) {
 
 int launch(const uint16_t* a, const uint16_t* b, uint16_t* c, uint32_t Mt, uint32_t Kt,
            uint32_t Nt, const uint16_t* bias, int relu, uint32_t* err, cudaStream_t stream,
-           int max_ctas, uint16_t* const* peer_c, uint32_t npeers) {
+           int max_ctas, uint16_t* const* peer_c, uint32_t npeers, uint16_t* mc_c) {
     cudaError_t attr_err = foil_smem_optin((const void*)gemm_tiles_kernel, kSmemBytes);
     if (attr_err == cudaSuccess) attr_err = foil_smem_optin((const void*)gemm_pair_kernel, kPSmemBytes);
     if (attr_err != cudaSuccess) {
@@ -1106,7 +1125,9 @@ int launch(const uint16_t* a, const uint16_t* b, uint16_t* c, uint32_t Mt, uint3
     p.wait_ns = foil_wait_limit_ns();
     p.npeers = peer_c ? npeers : 0u;
     for (uint32_t d = 0; d < kMaxPeers; ++d) p.peer_c[d] = d < p.npeers ? peer_c[d] : nullptr;
-    bool al32 = ((uintptr_t)c & 31u) == 0;
+    p.mc_c = mc_c;
+    if (mc_c) p.npeers = 0;  // the multicast address reaches every copy
+    bool al32 = ((uintptr_t)c & 31u) == 0 && ((uintptr_t)mc_c & 31u) == 0;
     for (uint32_t d = 0; d < p.npeers; ++d) al32 = al32 && ((uintptr_t)p.peer_c[d] & 31u) == 0;
     p.wide_stores = al32 ? 1u : 0u;
     if (Mt <= 4 || max_ctas < 2) {
@@ -1125,7 +1146,7 @@ int launch(const uint16_t* a, const uint16_t* b, uint16_t* c, uint32_t Mt, uint3
     // tiles to the peers while later tiles compute (their 256-bit copies need
     // 32-byte aligned buffers; otherwise the 256-column kernel's epilogue
     // stores to the peers itself).
-    if (Nt > 8 && (p.npeers == 0 || p.wide_stores)) {
+    if (Nt > 8 && ((p.npeers == 0 && p.mc_c == nullptr) || p.wide_stores)) {
         if (foil_smem_optin((const void*)gemm_pair_wide_kernel, kWSmemBytes) != cudaSuccess) {
             foil_set_error(FOIL_ERR_CUDA, "foil_matmul_tiles: cudaFuncSetAttribute failed");
             return FOIL_ERR_CUDA;
@@ -1134,7 +1155,7 @@ int launch(const uint16_t* a, const uint16_t* b, uint16_t* c, uint32_t Mt, uint3
         const uint32_t wtiles = p.m_blocks * p.n_blocks;
         const uint32_t wmax = (uint32_t)max_ctas / 2;
         const uint32_t wpairs = wtiles < wmax ? wtiles : wmax;
-        const int threads = p.npeers ? kWThreadsPush : kWThreads;
+        const int threads = (p.npeers || p.mc_c) ? kWThreadsPush : kWThreads;
         gemm_pair_wide_kernel<<<wpairs * 2, threads, kWSmemBytes, stream>>>(p);
         return check_launch("foil_matmul_tiles (2-SM, 512 columns)");
     }

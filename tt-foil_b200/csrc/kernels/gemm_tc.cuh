@@ -14,10 +14,12 @@ constexpr uint32_t kMaxPeers = 7;
 // that receives device-side error codes (may be null).  `max_ctas` caps the
 // persistent grid (normally the SM count).  `peer_c[0..npeers)`: other GPUs'
 // buffers (peer-mapped device pointers, same layout as c) that receive every
-// output tile as well.  Returns a foil_status.
+// output tile as well.  `mc_c` (instead of peer_c): an NVLink multicast
+// address bound to every GPU's copy of C, this one included, at c's offset;
+// each output tile is stored once through it.  Returns a foil_status.
 int launch(const uint16_t* a, const uint16_t* b, uint16_t* c, uint32_t Mt, uint32_t Kt,
            uint32_t Nt, const uint16_t* bias, int relu, uint32_t* err, cudaStream_t stream,
-           int max_ctas, uint16_t* const* peer_c = nullptr, uint32_t npeers = 0);
+           int max_ctas, uint16_t* const* peer_c = nullptr, uint32_t npeers = 0, uint16_t* mc_c = nullptr);
 
 // One "core" of a multi-core execute: the work one logical core's program
 // does, run by one CTA of a single cluster launch in which every core's CTA

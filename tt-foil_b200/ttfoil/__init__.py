@@ -108,6 +108,8 @@ SIGNATURES = {
     "foil_matmul_tiles_gather_dev": (ctypes.c_int, [_U16P, _U16P, _U16P, ctypes.POINTER(_P), ctypes.c_uint32,
                                                     ctypes.c_uint32, ctypes.c_uint32, ctypes.c_uint32, _U16P,
                                                     ctypes.c_int32, _P]),
+    "foil_matmul_tiles_gather_mc_dev": (ctypes.c_int, [_U16P, _U16P, _U16P, _U16P, ctypes.c_uint32, ctypes.c_uint32,
+                                                       ctypes.c_uint32, _U16P, ctypes.c_int32, _P]),
     "foil_matmul_tiles_gather_ce_dev": (ctypes.c_int, [_U16P, _U16P, _U16P, ctypes.POINTER(_P), ctypes.c_uint32,
                                                        ctypes.c_uint32, ctypes.c_uint32, ctypes.c_uint32, _U16P,
                                                        ctypes.c_int32, ctypes.c_uint32, _P]),
@@ -215,6 +217,14 @@ def matmul_tiles_gather(a, b, c, peer_c, Mt, Kt, Nt, bias=None, relu=False, stre
     arr = (_P * max(1, len(peer_c)))(*[int(x) for x in peer_c])
     check(lib().foil_matmul_tiles_gather_dev(_ptr(a), _ptr(b), _ptr(c), arr, len(peer_c), Mt, Kt, Nt,
                                              _ptr(bias), 1 if relu else 0, _stream(stream)))
+
+
+def matmul_tiles_gather_mc(a, b, c, mc_c, Mt, Kt, Nt, bias=None, relu=False, stream=None):
+    """matmul_tiles whose output tiles are stored through the NVLink
+    multicast address `mc_c` (an int: c's offset in a multicast object bound
+    on every GPU), so C lands in every GPU's copy."""
+    check(lib().foil_matmul_tiles_gather_mc_dev(_ptr(a), _ptr(b), _ptr(c), _P(int(mc_c)), Mt, Kt, Nt, _ptr(bias),
+                                                1 if relu else 0, _stream(stream)))
 
 
 def matmul_tiles_gather_ce(a, b, c, peer_c, Mt, Kt, Nt, bias=None, relu=False, chunks=8, stream=None):

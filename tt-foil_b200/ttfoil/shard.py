@@ -225,3 +225,82 @@ class GatheredTiles:
         dist.barrier()
         peer_free(self.device, self.ptr)
         self._closed = True
+
+
+class MulticastTiles:
+    """GatheredTiles over an NVLink multicast object: every rank's copy of
+    the Mt x Nt tile-layout C lives in PyTorch symmetric memory, bound to one
+    multicast object (NVSwitch), and `matmul` stores each output tile once
+    through the multicast address; the switch writes it into every GPU's
+    copy (foil_matmul_tiles_gather_mc_dev).  Same row split, same ordering
+    rules and the same `fence` as GatheredTiles.  Raises RuntimeError on
+    every rank alike when a rank has no multicast support."""
+
+    def __init__(self, Mt, Nt, device=None):
+        import torch
+        import torch.distributed as dist
+        import torch.distributed._symmetric_memory as symm
+        self.rank, self.world = dist.get_rank(), dist.get_world_size()
+        self.device = torch.cuda.current_device() if device is None else int(device)
+        self.Mt, self.Nt = Mt, Nt
+        self.nbytes = Mt * Nt * 2048
+        self.rows = split_rows(Mt, self.world, self.rank)
+        why = ""
+        self.buf, self.handle = None, None
+        try:
+            if not symm._SymmetricMemory.has_multicast_support(symm.DeviceType.CUDA, self.device):
+                why = f"rank {self.rank}: no NVLink multicast support on device {self.device}"
+        except Exception as e:  # noqa: BLE001 - reported on every rank below
+            why = f"rank {self.rank}: {e}"
+        states = [None] * self.world
+        dist.all_gather_object(states, why)
+        errors = [w for w in states if w]
+        if not errors:
+            try:
+                self.buf = symm.empty(Mt * Nt * 1024, dtype=torch.int16,
+                                      device=torch.device("cuda", self.device))
+                self.handle = symm.rendezvous(self.buf, dist.group.WORLD)
+                mc = int(self.handle.multicast_ptr)
+                if mc == 0:
+                    why = f"rank {self.rank}: the symmetric buffer has no multicast address"
+                else:
+                    # the multicast mapping mirrors this rank's buffer base
+                    base = int(self.handle.buffer_ptrs[self.rank])
+                    self.mc = mc + (self.buf.data_ptr() - base)
+            except Exception as e:  # noqa: BLE001
+                why = f"rank {self.rank}: {e}"
+            states = [None] * self.world
+            dist.all_gather_object(states, why)
+            errors = [w for w in states if w]
+        if errors:
+            self.handle, self.buf = None, None
+            raise RuntimeError("MulticastTiles: " + "; ".join(errors))
+        self.ptr = self.buf.data_ptr()
+        self._one = None
+        self._closed = False
+
+    def tensor(self):
+        """This rank's copy of C as an int16 CUDA tensor (bf16 bits, tile layout)."""
+        return self.buf
+
+    def matmul(self, a, b, Kt, bias=None, relu=False, stream=None):
+        """C[rows of this rank] = A_r . B, stored through the multicast
+        address into every rank's copy (see GatheredTiles.matmul)."""
+        from . import matmul_tiles_gather_mc
+        m0, m1 = self.rows
+        off = m0 * self.Nt * 2048
+        matmul_tiles_gather_mc(a, b, self.ptr + off, self.mc + off, m1 - m0, Kt, self.Nt, bias=bias, relu=relu,
+                               stream=stream)
+
+    fence = GatheredTiles.fence
+
+    def close(self):
+        """Release the symmetric buffer (collective)."""
+        if self._closed:
+            return
+        import torch
+        import torch.distributed as dist
+        torch.cuda.synchronize(self.device)
+        dist.barrier()
+        self.handle, self.buf = None, None
+        self._closed = True
