@@ -179,6 +179,7 @@ VARIANTS = {
     "single": {"FOIL_CONV_PRODUCER": "single"},
     "pair": {"FOIL_CONV_PRODUCER": "pair"},
     "plane": {"FOIL_CONV_PRODUCER": "plane"},
+    "resident": {"FOIL_CONV_PRODUCER": "resident"},
     # epilogue store paths: rows straight from registers, or staged for
     # tensor stores (each kernel's default is the other one for some shapes)
     "single_direct": {"FOIL_CONV_PRODUCER": "single", "FOIL_CONV_EPILOGUE": "direct"},
@@ -193,6 +194,8 @@ VARIANT_CASES = [  # x shape, w shape, stride, pad
     ((2, 14, 14, 256), (64, 3, 3, 256), 1, 1),     # K = 2304: 144 KiB of resident weights
     ((1, 23, 29, 128), (128, 3, 3, 128), 2, 1),    # M = 180, odd sizes
     ((4, 16, 16, 64), (64, 5, 5, 64), 1, 2),       # 5x5
+    ((2, 28, 28, 128), (256, 1, 1, 128), 1, 0),    # 1x1, BN 256 (resident weights: 64 KiB)
+    ((1, 20, 20, 64), (96, 1, 1, 64), 1, 0),       # 1x1, Cout tail in BN 128
 ]
 
 # Shapes the plane kernel serves (Cin a multiple of 64, Ho Wo a multiple of
@@ -268,13 +271,14 @@ def variant_inputs(env, tmp_path_factory):
     return script, cases
 
 
-@pytest.mark.parametrize("variant", ["gather", "single", "pair", "plane", "single_direct", "pair_staged",
-                                     "gather_direct"])
+@pytest.mark.parametrize("variant", ["gather", "single", "pair", "plane", "resident", "single_direct",
+                                     "pair_staged", "gather_direct"])
 def test_kernel_variants(variant_inputs, tmp_path, variant):
     """The im2col kernels (gather producer, single-CTA tensor copies, 2-SM
-    weight-stationary pair) feed identical operand tiles in the same K order,
-    and both epilogue store paths write the same values, so each reproduces
-    the default path's output bit for bit on every case.
+    weight-stationary pair, single-CTA with resident weights, where it fits)
+    feed identical operand tiles in the same K order, and both epilogue
+    store paths write the same values, so each reproduces the default path's
+    output bit for bit on every case.
     The plane kernel sums the same products in plane order: where it serves
     a case, its output is checked against the oracle."""
     script, cases = variant_inputs
@@ -282,7 +286,7 @@ def test_kernel_variants(variant_inputs, tmp_path, variant):
     served = 0
     for i, ((inp, got, x, w, b, stride, pad), out) in enumerate(zip(cases, outs)):
         if not out.exists():
-            assert variant == "plane", f"{variant} must serve case {i}"
+            assert variant in ("plane", "resident"), f"{variant} must serve case {i}"
             continue
         served += 1
         y = np.load(out).view(np.uint16).reshape(got.shape)

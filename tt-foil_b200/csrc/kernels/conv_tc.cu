@@ -582,6 +582,197 @@ __global__ void __launch_bounds__(kThreads, 1)
 }
 
 // ------------------------------------------------------------------------
+// Weight-stationary single-CTA variant (tensor copies, one column block):
+// the CTA loads all of its BN output channels' weights (every k-block) once,
+// with one 3-D tensor copy, and per k-block only the 128-row im2col copy of
+// A (16 KiB) into a ring of `stages` A buffers.  For convolutions with few
+// k-blocks (the 1x1: 2), where the pair kernel's start-up is not amortised,
+// this removes the weight copies of the streaming kernel (2/3 of its copy
+// bytes for 128 -> 256 channels) and the freed shared memory holds twice
+// the A stages.  Epilogue as in the streaming kernel (staged tensor stores).
+constexpr int kResMaxStages = 12;
+
+template <int BN>
+__global__ void __launch_bounds__(kThreads, 1)
+    conv_res_kernel(const Params p, const __grid_constant__ CUtensorMap tmap_x,
+                    const __grid_constant__ CUtensorMap tmap_w, const __grid_constant__ CUtensorMap tmap_y,
+                    uint32_t stages) {
+    constexpr uint32_t kA = 128u * 128u;             // A bytes per k-block
+    constexpr uint32_t kB = (uint32_t)BN * 128u;     // weight bytes per k-block
+    extern __shared__ uint8_t smem_raw[];
+    uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) &
+                                               ~uintptr_t(1023));
+    uint8_t* b_res = smem;
+    uint8_t* a_st = b_res + p.num_kb * kB;
+    uint8_t* staging = a_st + stages * kA;
+    uint64_t* full = reinterpret_cast<uint64_t*>(staging + 256u * BN);
+    uint64_t* empty = full + kResMaxStages;
+    uint64_t* tfull = empty + kResMaxStages;
+    uint64_t* tempty = tfull + 2;
+    uint64_t* bfull = tempty + 2;
+    uint64_t* drain = bfull + 1;
+    uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(drain + 1);
+    volatile uint32_t* abort_flag = tmem_slot + 1;
+
+    if (p.box_cols != (uint32_t)Epi<BN>::kCols || stages == 0 || stages > (uint32_t)kResMaxStages) {
+        if (threadIdx.x == 0 && blockIdx.x == 0) atomicOr(p.err, kErrConfig);
+        return;
+    }
+    const uint32_t warp = threadIdx.x >> 5, lane = threadIdx.x & 31u;
+    if (threadIdx.x == 0) {
+        for (uint32_t s = 0; s < stages; ++s) {
+            mbar_init(&full[s], 1);
+            mbar_init(&empty[s], 1);
+        }
+        for (int b = 0; b < 2; ++b) {
+            mbar_init(&tfull[b], 1);
+            mbar_init(&tempty[b], kEpiWarps);
+        }
+        mbar_init(bfull, 1);
+        mbar_init(drain, 1);
+        *abort_flag = 0u;
+        asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+        asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+    }
+    if (warp == kMmaWarp) {
+        asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(
+                         smem_u32(tmem_slot)),
+                     "r"(2u * BN)
+                     : "memory");
+        asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;" ::: "memory");
+    }
+    tc_fence_before();
+    __syncthreads();
+    tc_fence_after();
+    const uint32_t tmem_base = *tmem_slot;
+    const uint32_t num_tiles = p.m_blocks;  // one column block
+
+    if (warp == 0) {
+        if (lane == 0) {
+            // ----------------------------------------- tensor-copy producer
+            tma_prefetch_map(&tmap_x);
+            tma_prefetch_map(&tmap_w);
+            // All weights, once: [k-block][BN rows][64 ch] (encode_weight_map3).
+            mbar_expect_tx(bfull, p.num_kb * kB);
+            tma_load_3d(smem_u32(b_res), &tmap_w, 0, 0, 0, bfull);
+            const uint32_t hw = p.Ho * p.Wo;
+            uint32_t stage = 0, phase = 0, issued = 0;
+            bool ok = true;
+            for (uint32_t tile = blockIdx.x; ok && tile < num_tiles; tile += gridDim.x) {
+                const uint32_t m0 = tile * 128u, n = m0 / hw, rem = m0 - n * hw;
+                const uint32_t ho = rem / p.Wo, wo = rem - ho * p.Wo;
+                const int32_t w0 = (int32_t)(wo * p.stride) - (int32_t)p.pad;
+                const int32_t h0 = (int32_t)(ho * p.stride) - (int32_t)p.pad;
+                uint32_t kh = 0, kw = 0, cb = 0;
+                for (uint32_t kb = 0; kb < p.num_kb; ++kb) {
+                    if (!mbar_wait(&empty[stage], phase ^ 1u, abort_flag, p.err, p.wait_ns)) {
+                        ok = false;
+                        break;
+                    }
+                    mbar_expect_tx(&full[stage], kA);
+                    tma_load_im2col_4d(smem_u32(a_st + stage * kA), &tmap_x, (int32_t)(cb * 64u), w0, h0,
+                                       (int32_t)n, (uint16_t)kw, (uint16_t)kh, &full[stage]);
+                    ++issued;
+                    if (++stage == stages) {
+                        stage = 0;
+                        phase ^= 1u;
+                    }
+                    if (++cb == p.cblocks) {
+                        cb = 0;
+                        if (++kw == p.KW) {
+                            kw = 0;
+                            ++kh;
+                        }
+                    }
+                }
+            }
+            // Copies of the weights and of the last stages may still be in
+            // flight after an abort: wait (bounded) for each before the CTA ends.
+            mbar_drain(bfull, 0, 100000000ull);
+            drain_loads(full, issued, stages);
+        }
+    } else if (warp == kMmaWarp) {
+        if (lane == 0) {
+            // ------------------------------------------------ MMA issuer
+            const uint32_t idesc = (1u << 4) | (1u << 7) | (1u << 10) | ((uint32_t)(BN >> 3) << 17) |
+                                   ((128u >> 4) << 24);
+            constexpr uint64_t kmaj = smem_desc_sw128_kmajor();
+            const uint32_t a0 = smem_u32(a_st), b0 = smem_u32(b_res);
+            uint32_t stage = 0, phase = 0, acc = 0, acc_phase = 0;
+            bool ok = mbar_wait(bfull, 0, abort_flag, p.err, p.wait_ns);
+            for (uint32_t tile = blockIdx.x; ok && tile < num_tiles; tile += gridDim.x) {
+                if (!mbar_wait(&tempty[acc], acc_phase ^ 1u, abort_flag, p.err, p.wait_ns)) break;
+                tc_fence_after();
+                const uint32_t d_tmem = tmem_base + acc * BN;
+                for (uint32_t kb = 0; kb < p.num_kb; ++kb) {
+                    if (!mbar_wait(&full[stage], phase, abort_flag, p.err, p.wait_ns)) {
+                        ok = false;
+                        break;
+                    }
+                    tc_fence_after();
+                    const uint32_t a_addr = a0 + stage * kA, b_addr = b0 + kb * kB;
+#pragma unroll
+                    for (uint32_t s = 0; s < 4; ++s) {
+                        const uint64_t ad = kmaj | (uint64_t)(((a_addr + s * 32u) >> 4) & 0x3fffu);
+                        const uint64_t bd = kmaj | (uint64_t)(((b_addr + s * 32u) >> 4) & 0x3fffu);
+                        tc_mma(d_tmem, ad, bd, idesc, (kb | s) != 0u);
+                    }
+                    tc_commit(&empty[stage]);
+                    if (++stage == stages) {
+                        stage = 0;
+                        phase ^= 1u;
+                    }
+                }
+                if (!ok) break;
+                tc_commit(&tfull[acc]);
+                if (++acc == 2) {
+                    acc = 0;
+                    acc_phase ^= 1u;
+                }
+            }
+            tc_commit(drain);
+            mbar_drain(drain, 0, 100000000ull);
+        }
+    } else if (warp > kMmaWarp) {
+        // ---------------------------------------------------- epilogue
+        const uint32_t e = warp - 5u, qd = warp & 3u, half = e >> 2;
+        const uint32_t col0 = half * (uint32_t)(BN / 2);
+        const uint32_t stg = smem_u32(staging) + e * Epi<BN>::kWarpBytes;
+        const int mode = epi_mode(p);
+        if (lane == 0) tma_prefetch_map(&tmap_y);
+        uint32_t acc = 0, acc_phase = 0;
+        for (uint32_t tile = blockIdx.x; tile < num_tiles; tile += gridDim.x) {
+            bool ok = true;
+            if (lane == 0) ok = mbar_wait(&tfull[acc], acc_phase, abort_flag, p.err, p.wait_ns);
+            ok = __shfl_sync(0xffffffffu, ok ? 1 : 0, 0) != 0;
+            if (!ok) break;
+            tc_fence_after();
+            uint64_t* te = &tempty[acc];
+            epilogue_rows<BN>(p, &tmap_y, tmem_base + ((qd * 32u) << 16) + acc * BN + col0,
+                              tile * 128u + qd * 32u, col0, stg, mode, lane, p.M, [&] {
+                                  tc_fence_before();
+                                  __syncwarp();
+                                  if (lane == 0) mbar_arrive(te);
+                              });
+            if (++acc == 2) {
+                acc = 0;
+                acc_phase ^= 1u;
+            }
+        }
+        if (lane == 0) bulk_wait_all();
+    }
+
+    tc_fence_before();
+    __syncthreads();
+    if (warp == kMmaWarp) {
+        __syncwarp();
+        tc_fence_after();
+        asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem_base), "r"(2u * BN)
+                     : "memory");
+    }
+}
+
+// ------------------------------------------------------------------------
 // Weight-stationary 2-SM variant (tensor copies, Cout <= 256).  A CTA pair
 // (cluster of 2) computes tiles of 256 kSub rows with tcgen05.mma.cta_group::2
 // (M = 256, N = BN): each CTA loads 128 kSub consecutive output pixels of A
@@ -1148,6 +1339,32 @@ static int launch_pair(const Params& p, uint32_t stages, const CUtensorMap& mx, 
     return FOIL_OK;
 }
 
+// Shared memory of the resident-weight single-CTA kernel.
+static uint32_t res_smem_bytes(const Params& p, int bn, uint32_t stages) {
+    return p.num_kb * (uint32_t)bn * 128u + stages * 16384u + 256u * (uint32_t)bn + 1024u +
+           (uint32_t)kBarrierBytes;
+}
+
+template <int BN>
+static int launch_res(const Params& p, uint32_t stages, const CUtensorMap& mx, const CUtensorMap& mw,
+                      const CUtensorMap& my, cudaStream_t stream, int max_ctas, int smem_optin) {
+    if (foil_smem_optin((const void*)conv_res_kernel<BN>, smem_optin) != cudaSuccess) {
+        foil_set_error(FOIL_ERR_CUDA, "foil_conv2d_nhwc: cudaFuncSetAttribute failed");
+        return FOIL_ERR_CUDA;
+    }
+    const uint32_t grid = p.m_blocks < (uint32_t)max_ctas ? p.m_blocks : (uint32_t)max_ctas;
+    conv_res_kernel<BN><<<grid, kThreads, res_smem_bytes(p, BN, stages), stream>>>(p, mx, mw, my, stages);
+    cudaError_t e = cudaGetLastError();
+    if (e != cudaSuccess) {
+        char buf[200];
+        snprintf(buf, sizeof buf, "foil_conv2d_nhwc: launch failed: %s", cudaGetErrorString(e));
+        foil_set_error(FOIL_ERR_CUDA, buf);
+        return FOIL_ERR_CUDA;
+    }
+    foil_count_launch();
+    return FOIL_OK;
+}
+
 // Plane-kernel geometry (see conv_plane_kernel).  False when the shape is
 // not served: Cin not a multiple of 64, more than 25 taps or 16 planes, Ho Wo
 // not a multiple of 32, Wo not a multiple of 8, a plane span above 256
@@ -1509,6 +1726,7 @@ int launch(const uint16_t* x, const uint16_t* w, const uint16_t* bias, uint16_t*
     // k-blocks; 18.8 against 16.8 us), where weights are a small share of the
     // operand copies and the start-up is not amortised.
     const bool pair = pair_ok && strcmp(producer_override(), "single") != 0 &&
+                      strcmp(producer_override(), "resident") != 0 &&
                       (strcmp(producer_override(), "pair") == 0 ||
                        (p.num_kb >= 4 && p.m_blocks >= (uint32_t)max_ctas));
     const uint32_t sub = bn <= 128 ? 2u : 1u;
@@ -1525,6 +1743,30 @@ int launch(const uint16_t* x, const uint16_t* w, const uint16_t* bias, uint16_t*
             case 128: return launch_pair<128>(q, stages, mx, mw, my, stream, max_ctas, optin);
             default: return launch_pair<256>(q, stages, mx, mw, my, stream, max_ctas, optin);
         }
+    }
+    // Resident-weight single-CTA kernel: one column block, at least 4 A
+    // stages beside the weights.  Measured (L2 flushed, three alternating
+    // rounds): 1x1 batch 32 128 -> 256 18.9-19.0 against 20.1-20.4 us for the
+    // streaming kernel, 3x3 N = 1 64 -> 64 11.4-11.9 against 12.9-13.2 us.
+    uint32_t rstages = 0;
+    while (rstages < (uint32_t)kResMaxStages && res_smem_bytes(p, bn, rstages + 1) <= (uint32_t)optin) ++rstages;
+    const bool res = p.n_blocks == 1 && rstages >= 4 && strcmp(producer_override(), "single") != 0;
+    if (res) {
+        if (!encode_weight_map3(p, (uint32_t)bn, &mw)) {
+            foil_set_error(FOIL_ERR_CUDA, "foil_conv2d_nhwc: tensor-map encoding failed");
+            return FOIL_ERR_CUDA;
+        }
+        p.direct = 0u;
+        switch (bn) {
+            case 64: return launch_res<64>(p, rstages, mx, mw, my, stream, max_ctas, optin);
+            case 128: return launch_res<128>(p, rstages, mx, mw, my, stream, max_ctas, optin);
+            default: return launch_res<256>(p, rstages, mx, mw, my, stream, max_ctas, optin);
+        }
+    }
+    if (strcmp(producer_override(), "resident") == 0) {
+        foil_set_error(FOIL_ERR_UNSUPPORTED, "foil_conv2d_nhwc: FOIL_CONV_PRODUCER=resident but the resident-weight "
+                                             "kernel does not serve this shape");
+        return FOIL_ERR_UNSUPPORTED;
     }
     p.direct = force_direct ? 1u : 0u;
     return launch_tiles<true>(p, bn, mx, mw, my, stream, max_ctas);

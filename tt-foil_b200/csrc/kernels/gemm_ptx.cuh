@@ -192,6 +192,16 @@ __device__ __forceinline__ void tma_load_im2col_4d(uint32_t dst, const void* map
         : "memory");
 }
 
+// 3-D tiled load: box origin (x, y, z).
+__device__ __forceinline__ void tma_load_3d(uint32_t dst, const void* map, int32_t x, int32_t y, int32_t z,
+                                            uint64_t* bar) {
+    asm volatile(
+        "cp.async.bulk.tensor.3d.shared::cluster.global.tile.mbarrier::complete_tx::bytes"
+        " [%0], [%1, {%2, %3, %4}], [%5];" ::"r"(dst),
+        "l"(reinterpret_cast<uint64_t>(map)), "r"(x), "r"(y), "r"(z), "r"(smem_u32(bar))
+        : "memory");
+}
+
 // Pair (cta_group::2) forms, no multicast: the destination is this CTA's
 // shared memory and completion is signalled on the mbarrier at shared::cluster
 // address `bar_cluster`, which may be the pair leader's.
