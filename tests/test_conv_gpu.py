@@ -323,3 +323,33 @@ def test_conv_rejects_bad_shapes(env):
         tf.conv2d_nhwc(z, z, None, z, 1, 4, 4, 8, 16, 3, 3, 1, 1)
     with pytest.raises(tf.FoilError, match="unsupported"):
         tf.conv2d_nhwc(z, z, None, z, 1, 4, 4, 16, 16, 3, 3, 0, 1)
+
+
+@pytest.mark.parametrize("shape", [
+    ((8, 56, 56, 64), (64, 3, 3, 64), 1, 1),      # pair kernel (rows from registers)
+    ((2, 28, 28, 128), (256, 1, 1, 128), 1, 0),   # resident-weight kernel (tensor stores)
+])
+def test_output_only_16_byte_aligned(env, shape):
+    """An output buffer that is 16- but not 32-byte aligned: the pair
+    kernel's register epilogue takes its 128-bit store path, the tensor-store
+    epilogues start their boxes there; both bit-equal to an aligned run."""
+    torch, tf = env
+    xs, ws, stride, pad = shape
+    x = oracle.rand_bf16(xs, 911)
+    w = oracle.randn_bf16(ws, 912, np.sqrt(2.0 / (ws[1] * ws[2] * ws[3])))
+    b = oracle.rand_bf16((ws[0],), 913, -0.1, 0.1)
+    N, H, W, Cin = xs
+    Cout, KH, KW, _ = ws
+    Ho, Wo = (H + 2 * pad - KH) // stride + 1, (W + 2 * pad - KW) // stride + 1
+    n = N * Ho * Wo * Cout
+    ref = run_conv(env, x, w, b, stride, pad, relu=True)
+    big = torch.full((n + 16,), 0x7fc0, dtype=torch.int16, device="cuda")
+    y = big[8:8 + n]                                   # base + 16 bytes
+    assert y.data_ptr() % 32 == 16
+    tf.conv2d_nhwc(dev(torch, x), dev(torch, w), dev(torch, b), y, N, H, W, Cin, Cout, KH, KW, stride, pad,
+                   relu=True)
+    torch.cuda.synchronize()
+    assert tf.device_error() == 0
+    got = big.cpu().numpy().view(np.uint16)
+    assert np.array_equal(got[8:8 + n].reshape(ref.shape), ref)
+    assert np.all(got[:8] == 0x7fc0) and np.all(got[8 + n:] == 0x7fc0), "bytes outside y written"
