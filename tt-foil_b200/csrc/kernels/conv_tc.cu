@@ -56,6 +56,7 @@
 #include <cstdlib>
 #include <cstring>
 #include <mutex>
+#include <utility>
 
 #include "common.cuh"
 #include "gemm_ptx.cuh"
@@ -351,6 +352,11 @@ __global__ void __launch_bounds__(kThreads, 1)
     tc_fence_before();
     __syncthreads();
     tc_fence_after();
+    // Launched with programmatic stream serialization, the set-up above may
+    // overlap the previous kernel's tail; global memory is touched only after
+    // that kernel has completed.
+    griddep_wait();
+    griddep_launch_dependents();
     const uint32_t tmem_base = *tmem_slot;
     const uint32_t num_tiles = p.m_blocks * p.n_blocks;
     const uint32_t ksteps = p.kc / 16;  // K-steps (16 channels) per k-block
@@ -644,6 +650,11 @@ __global__ void __launch_bounds__(kThreads, 1)
     tc_fence_before();
     __syncthreads();
     tc_fence_after();
+    // Launched with programmatic stream serialization, the set-up above may
+    // overlap the previous kernel's tail; global memory is touched only after
+    // that kernel has completed.
+    griddep_wait();
+    griddep_launch_dependents();
     const uint32_t tmem_base = *tmem_slot;
     const uint32_t num_tiles = p.m_blocks;  // one column block
 
@@ -852,6 +863,11 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
     __syncthreads();
     cluster_sync();
     tc_fence_after();
+    // Launched with programmatic stream serialization, the set-up above may
+    // overlap the previous kernel's tail; global memory is touched only after
+    // that kernel has completed.
+    griddep_wait();
+    griddep_launch_dependents();
     const uint32_t tmem_base = *tmem_slot;
     const uint32_t num_tiles = p.m_blocks;  // tiles of 256 kSub rows
 
@@ -1288,6 +1304,34 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
     }
 }
 
+// Launch with programmatic stream serialization (the kernels' set-up may
+// overlap the previous kernel's tail; they wait for it before touching
+// global memory).  FOIL_CONV_PDL=0 launches plainly (for comparisons).
+static bool use_pdl() {
+    static const bool on = [] {
+        const char* v = getenv("FOIL_CONV_PDL");
+        return v == nullptr || strcmp(v, "0") != 0;
+    }();
+    return on;
+}
+
+template <typename... KArgs, typename... Args>
+static cudaError_t launch_conv(void (*kernel)(KArgs...), uint32_t grid, size_t smem, cudaStream_t stream,
+                               Args&&... args) {
+    cudaLaunchConfig_t cfg;
+    memset(&cfg, 0, sizeof cfg);
+    cfg.gridDim = dim3(grid, 1, 1);
+    cfg.blockDim = dim3(kThreads, 1, 1);
+    cfg.dynamicSmemBytes = smem;
+    cfg.stream = stream;
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attr[0].val.programmaticStreamSerializationAllowed = 1;
+    cfg.attrs = attr;
+    cfg.numAttrs = use_pdl() ? 1 : 0;
+    return cudaLaunchKernelEx(&cfg, kernel, std::forward<Args>(args)...);
+}
+
 template <int BN, bool kTma, bool kDirect>
 static int launch_bn(const Params& p, const CUtensorMap& mx, const CUtensorMap& mw,
                      const CUtensorMap& my, cudaStream_t stream, int max_ctas) {
@@ -1298,8 +1342,7 @@ static int launch_bn(const Params& p, const CUtensorMap& mx, const CUtensorMap& 
     }
     const uint32_t tiles = p.m_blocks * p.n_blocks;
     const uint32_t grid = tiles < (uint32_t)max_ctas ? tiles : (uint32_t)max_ctas;
-    conv_kernel<BN, kTma, kDirect><<<grid, kThreads, C::kSmemBytes, stream>>>(p, mx, mw, my);
-    cudaError_t e = cudaGetLastError();
+    cudaError_t e = launch_conv(conv_kernel<BN, kTma, kDirect>, grid, C::kSmemBytes, stream, p, mx, mw, my);
     if (e != cudaSuccess) {
         char buf[200];
         snprintf(buf, sizeof buf, "foil_conv2d_nhwc: launch failed: %s", cudaGetErrorString(e));
@@ -1327,8 +1370,8 @@ static int launch_pair(const Params& p, uint32_t stages, const CUtensorMap& mx, 
     }
     const uint32_t max_pairs = (uint32_t)max_ctas / 2;
     const uint32_t pairs = p.m_blocks < max_pairs ? p.m_blocks : max_pairs;
-    conv_pair_kernel<BN><<<2 * pairs, kThreads, pair_smem_bytes(p, BN, stages), stream>>>(p, mx, mw, my, stages);
-    cudaError_t e = cudaGetLastError();
+    cudaError_t e = launch_conv(conv_pair_kernel<BN>, 2 * pairs, pair_smem_bytes(p, BN, stages), stream, p, mx, mw,
+                                my, stages);
     if (e != cudaSuccess) {
         char buf[200];
         snprintf(buf, sizeof buf, "foil_conv2d_nhwc: launch failed: %s", cudaGetErrorString(e));
@@ -1353,8 +1396,8 @@ static int launch_res(const Params& p, uint32_t stages, const CUtensorMap& mx, c
         return FOIL_ERR_CUDA;
     }
     const uint32_t grid = p.m_blocks < (uint32_t)max_ctas ? p.m_blocks : (uint32_t)max_ctas;
-    conv_res_kernel<BN><<<grid, kThreads, res_smem_bytes(p, BN, stages), stream>>>(p, mx, mw, my, stages);
-    cudaError_t e = cudaGetLastError();
+    cudaError_t e = launch_conv(conv_res_kernel<BN>, grid, res_smem_bytes(p, BN, stages), stream, p, mx, mw, my,
+                                stages);
     if (e != cudaSuccess) {
         char buf[200];
         snprintf(buf, sizeof buf, "foil_conv2d_nhwc: launch failed: %s", cudaGetErrorString(e));
