@@ -255,6 +255,11 @@ __device__ __forceinline__ void gemm_tiles_body(const Params& p, uint32_t cta, u
     __syncthreads();
     tc_fence_after();
     const uint32_t tmem_base = *tmem_slot;
+    // Launched with programmatic stream serialization, the set-up above may
+    // overlap the previous kernel's tail; global memory is touched only after
+    // that kernel has completed.
+    griddep_wait();
+    griddep_launch_dependents();
 
     const uint32_t num_tiles = p.m_blocks * p.n_blocks;
     const uint32_t num_kb = (p.Kt + kBKT - 1) / kBKT;
@@ -638,6 +643,11 @@ gemm_pair_kernel(const Params p) {
     cluster_sync();
     tc_fence_after();
     const uint32_t tmem_base = *tmem_slot;
+    // Launched with programmatic stream serialization, the set-up above may
+    // overlap the previous kernel's tail; global memory is touched only after
+    // that kernel has completed.
+    griddep_wait();
+    griddep_launch_dependents();
 
     const uint32_t num_tiles = p.m_blocks * p.n_blocks;  // m_blocks = 256-row pairs
     const uint32_t num_kb = (p.Kt + kBKT - 1) / kBKT;
@@ -804,8 +814,9 @@ gemm_pair_kernel(const Params p) {
 }
 
 // ------------------------------------------------------------------ host ---
-static int check_launch(const char* what) {
+static int check_launch(const char* what, cudaError_t launch_err = cudaSuccess) {
     cudaError_t e = cudaGetLastError();
+    if (launch_err != cudaSuccess) e = launch_err;
     if (e != cudaSuccess) {
         char buf[256];
         snprintf(buf, sizeof buf, "%s: launch failed: %s", what, cudaGetErrorString(e));
@@ -886,6 +897,11 @@ gemm_pair_wide_kernel(const Params p) {
     cluster_sync();
     tc_fence_after();
     const uint32_t tmem_base = *tmem_slot;
+    // Launched with programmatic stream serialization, the set-up above may
+    // overlap the previous kernel's tail; global memory is touched only after
+    // that kernel has completed.
+    griddep_wait();
+    griddep_launch_dependents();
 
     const uint32_t num_tiles = p.m_blocks * p.n_blocks;  // 256-row x 512-column blocks
     const uint32_t num_kb = (p.Kt + kBKT - 1) / kBKT;
@@ -1102,6 +1118,28 @@ gemm_pair_wide_kernel(const Params p) {
     }
 }
 
+// Launch with programmatic stream serialization (see the kernels' set-up):
+// FOIL_GEMM_PDL=0 launches plainly (for comparisons).
+static cudaError_t launch_gemm(void (*kernel)(const Params), uint32_t grid, int threads, int smem,
+                               cudaStream_t stream, const Params& p) {
+    static const bool pdl = [] {
+        const char* v = getenv("FOIL_GEMM_PDL");
+        return v == nullptr || strcmp(v, "0") != 0;
+    }();
+    cudaLaunchConfig_t cfg;
+    memset(&cfg, 0, sizeof cfg);
+    cfg.gridDim = dim3(grid, 1, 1);
+    cfg.blockDim = dim3((unsigned)threads, 1, 1);
+    cfg.dynamicSmemBytes = (size_t)smem;
+    cfg.stream = stream;
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attr[0].val.programmaticStreamSerializationAllowed = 1;
+    cfg.attrs = attr;
+    cfg.numAttrs = pdl ? 1 : 0;
+    return cudaLaunchKernelEx(&cfg, kernel, p);
+}
+
 int launch(const uint16_t* a, const uint16_t* b, uint16_t* c, uint32_t Mt, uint32_t Kt,
            uint32_t Nt, const uint16_t* bias, int relu, uint32_t* err, cudaStream_t stream,
            int max_ctas, uint16_t* const* peer_c, uint32_t npeers, uint16_t* mc_c) {
@@ -1135,8 +1173,8 @@ int launch(const uint16_t* a, const uint16_t* b, uint16_t* c, uint32_t Mt, uint3
         p.m_blocks = (Mt + 3) / 4;
         const uint32_t tiles = p.m_blocks * p.n_blocks;
         const uint32_t grid = tiles < (uint32_t)max_ctas ? tiles : (uint32_t)max_ctas;
-        gemm_tiles_kernel<<<grid, kThreads, kSmemBytes, stream>>>(p);
-        return check_launch("foil_matmul_tiles");
+        const cudaError_t le = launch_gemm(gemm_tiles_kernel, grid, kThreads, kSmemBytes, stream, p);
+        return check_launch("foil_matmul_tiles", le);
     }
     p.m_blocks = (Mt + 7) / 8;  // 256-row blocks, one per CTA pair
     // More than one 256-column block: the 512-column pair kernel (a quarter
@@ -1156,14 +1194,14 @@ int launch(const uint16_t* a, const uint16_t* b, uint16_t* c, uint32_t Mt, uint3
         const uint32_t wmax = (uint32_t)max_ctas / 2;
         const uint32_t wpairs = wtiles < wmax ? wtiles : wmax;
         const int threads = (p.npeers || p.mc_c) ? kWThreadsPush : kWThreads;
-        gemm_pair_wide_kernel<<<wpairs * 2, threads, kWSmemBytes, stream>>>(p);
-        return check_launch("foil_matmul_tiles (2-SM, 512 columns)");
+        const cudaError_t le = launch_gemm(gemm_pair_wide_kernel, wpairs * 2, threads, kWSmemBytes, stream, p);
+        return check_launch("foil_matmul_tiles (2-SM, 512 columns)", le);
     }
     const uint32_t tiles = p.m_blocks * p.n_blocks;
     const uint32_t max_pairs = (uint32_t)max_ctas / 2;
     const uint32_t pairs = tiles < max_pairs ? tiles : max_pairs;
-    gemm_pair_kernel<<<pairs * 2, kThreads, kPSmemBytes, stream>>>(p);
-    return check_launch("foil_matmul_tiles (2-SM)");
+    const cudaError_t le = launch_gemm(gemm_pair_kernel, pairs * 2, kThreads, kPSmemBytes, stream, p);
+    return check_launch("foil_matmul_tiles (2-SM)", le);
 }
 
 }  // namespace gemm
