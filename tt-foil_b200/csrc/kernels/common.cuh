@@ -4,6 +4,7 @@
 #include <cstdint>
 #include <cuda_runtime.h>
 #include <cstdio>
+#include <cstdlib>
 
 namespace foil {
 
@@ -62,6 +63,24 @@ enum : uint32_t {
 };
 
 // Wall-clock nanoseconds (for bounded waits).
+// Programmatic dependent launch.  griddep_wait: block until the grids this
+// one depends on (the previous kernel in the stream, when launched with
+// programmatic stream serialization) have completed and their memory is
+// visible; a no-op otherwise.  griddep_launch_dependents: allow the next
+// such kernel to start launching (its own griddep_wait still waits for this
+// grid to complete).
+__device__ __forceinline__ void griddep_wait() { asm volatile("griddepcontrol.wait;" ::: "memory"); }
+__device__ __forceinline__ void griddep_launch_dependents() {
+    asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
+}
+
+// Launch attribute for programmatic stream serialization, on unless the
+// environment variable `env` is "0" (read once per variable by the caller).
+inline bool pdl_enabled(const char* env) {
+    const char* v = getenv(env);
+    return v == nullptr || v[0] != '0' || v[1] != '\0';
+}
+
 __device__ __forceinline__ uint64_t global_ns() {
     uint64_t t;
     asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t));

@@ -1308,10 +1308,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
 // overlap the previous kernel's tail; they wait for it before touching
 // global memory).  FOIL_CONV_PDL=0 launches plainly (for comparisons).
 static bool use_pdl() {
-    static const bool on = [] {
-        const char* v = getenv("FOIL_CONV_PDL");
-        return v == nullptr || strcmp(v, "0") != 0;
-    }();
+    static const bool on = pdl_enabled("FOIL_CONV_PDL");
     return on;
 }
 

@@ -18,6 +18,8 @@
 // (tests/tile_utils.hpp:33-47, tests/test_relu.cpp:54-59,
 // tests/test_add_tiles.cpp:60), bit-exact.  Every wait is bounded; a timeout
 // raises the CTA's abort flag and sets kErrWaitTimeout in the error word.
+#include <cstring>
+
 #include "eltwise.cuh"
 
 #include "gemm_ptx.cuh"
@@ -121,6 +123,10 @@ stream_kernel(const uint8_t* a, const uint8_t* b, uint8_t* out, uint64_t bytes,
         asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
     }
     __syncthreads();
+    // Launched with programmatic stream serialization: the set-up above may
+    // overlap the previous kernel's tail; global memory only after it.
+    griddep_wait();
+    griddep_launch_dependents();
 
     const uint64_t nchunks = (bytes + CHUNK - 1) / CHUNK;
     const uint64_t first = blockIdx.x, step = gridDim.x;
@@ -215,11 +221,25 @@ int launch_op(const void* a, const void* b, void* out, uint64_t bytes, const uin
     const uint64_t nchunks = (bytes + CHUNK - 1) / CHUNK;
     const uint64_t cap = (uint64_t)foil_sm_count() * CTAS;
     const unsigned grid = (unsigned)(nchunks < cap ? nchunks : cap);
-    kern<<<grid, C::kThreads, C::kSmem, stream>>>(static_cast<const uint8_t*>(a),
-                                                   static_cast<const uint8_t*>(b),
-                                                   static_cast<uint8_t*>(out), bytes, bias_tiles, Nt, err,
-                                                   foil_wait_limit_ns());
-    return (int)cudaGetLastError();
+    // add_tiles measured 0.7 % slower with it (6110 against 6155 GB/s); the
+    // others 0.7-1.7 % faster.
+    static const bool pdl = OP != kAdd && pdl_enabled("FOIL_STREAM_PDL");
+    cudaLaunchConfig_t cfg;
+    memset(&cfg, 0, sizeof cfg);
+    cfg.gridDim = dim3(grid, 1, 1);
+    cfg.blockDim = dim3(C::kThreads, 1, 1);
+    cfg.dynamicSmemBytes = C::kSmem;
+    cfg.stream = stream;
+    cudaLaunchAttribute la[1];
+    la[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    la[0].val.programmaticStreamSerializationAllowed = 1;
+    cfg.attrs = la;
+    cfg.numAttrs = pdl ? 1 : 0;
+    const cudaError_t e = cudaLaunchKernelEx(&cfg, kern, static_cast<const uint8_t*>(a),
+                                             static_cast<const uint8_t*>(b), static_cast<uint8_t*>(out), bytes,
+                                             bias_tiles, Nt, err, foil_wait_limit_ns());
+    const cudaError_t last = cudaGetLastError();
+    return (int)(e != cudaSuccess ? e : last);
 }
 
 }  // namespace

@@ -160,17 +160,6 @@ __host__ __device__ constexpr uint64_t smem_desc_sw128_kmajor() {
     return (1ull << 16) | ((uint64_t)(1024u >> 4) << 32) | (1ull << 46) | (2ull << 61);
 }
 
-// Programmatic dependent launch.  griddep_wait: block until the grids this
-// one depends on (the previous kernel in the stream, when launched with
-// programmatic stream serialization) have completed and their memory is
-// visible; a no-op otherwise.  griddep_launch_dependents: allow the next
-// such kernel to start launching (its own griddep_wait still waits for this
-// grid to complete).
-__device__ __forceinline__ void griddep_wait() { asm volatile("griddepcontrol.wait;" ::: "memory"); }
-__device__ __forceinline__ void griddep_launch_dependents() {
-    asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
-}
-
 // ------------------------------------------------ tensor copies (no multicast)
 // The tensor map is a __grid_constant__ kernel parameter; its generic address
 // is the operand.  Completion is signalled on `bar` as transaction bytes.

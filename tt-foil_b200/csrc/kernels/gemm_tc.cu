@@ -1122,10 +1122,7 @@ gemm_pair_wide_kernel(const Params p) {
 // FOIL_GEMM_PDL=0 launches plainly (for comparisons).
 static cudaError_t launch_gemm(void (*kernel)(const Params), uint32_t grid, int threads, int smem,
                                cudaStream_t stream, const Params& p) {
-    static const bool pdl = [] {
-        const char* v = getenv("FOIL_GEMM_PDL");
-        return v == nullptr || strcmp(v, "0") != 0;
-    }();
+    static const bool pdl = pdl_enabled("FOIL_GEMM_PDL");
     cudaLaunchConfig_t cfg;
     memset(&cfg, 0, sizeof cfg);
     cfg.gridDim = dim3(grid, 1, 1);

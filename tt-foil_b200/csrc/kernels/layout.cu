@@ -8,6 +8,8 @@
 // accesses, and the permutation happens in shared memory.  The shared-memory
 // index is XOR-swizzled so that every 8-lane phase of a 16-byte access hits 8
 // distinct 4-bank groups (conflict-free on both sides).
+#include <cstring>
+
 #include "common.cuh"
 #include "layout.cuh"
 #include "../../../include/foil_c.h"
@@ -40,6 +42,8 @@ __device__ __forceinline__ uint32_t smem_slot(uint32_t idx) {
 __global__ void __launch_bounds__(kLayoutThreads)
 tilize_kernel(const uint4* __restrict__ in, uint4* __restrict__ out,
               uint32_t rows, uint32_t cols) {
+    griddep_wait();  // see launch_layout
+    griddep_launch_dependents();
     __shared__ uint4 buf[kBandChunks];
     const uint32_t Ct = cols / 32u, Rt = rows / 32u;
     const uint32_t bands_per_row = (Ct + kBandTiles - 1) / kBandTiles;
@@ -70,6 +74,8 @@ tilize_kernel(const uint4* __restrict__ in, uint4* __restrict__ out,
 __global__ void __launch_bounds__(kLayoutThreads)
 untilize_kernel(const uint4* __restrict__ in, uint4* __restrict__ out,
                 uint32_t rows, uint32_t cols) {
+    griddep_wait();  // see launch_layout
+    griddep_launch_dependents();
     __shared__ uint4 buf[kBandChunks];
     const uint32_t Ct = cols / 32u, Rt = rows / 32u;
     const uint32_t bands_per_row = (Ct + kBandTiles - 1) / kBandTiles;
@@ -100,8 +106,28 @@ untilize_kernel(const uint4* __restrict__ in, uint4* __restrict__ out,
 
 extern "C" void foil_set_error(int status, const char* msg);
 
-static int check_launch(const char* what) {
+// Launch with programmatic stream serialization (FOIL_STREAM_PDL=0: plainly):
+// the CTAs may be scheduled during the previous kernel's tail and wait
+// (griddepcontrol.wait) before touching global memory.
+static cudaError_t launch_layout(void (*kernel)(const uint4*, uint4*, uint32_t, uint32_t), unsigned grid,
+                                 cudaStream_t stream, const uint4* in, uint4* out, uint32_t rows, uint32_t cols) {
+    static const bool pdl = foil::pdl_enabled("FOIL_STREAM_PDL");
+    cudaLaunchConfig_t cfg;
+    memset(&cfg, 0, sizeof cfg);
+    cfg.gridDim = dim3(grid, 1, 1);
+    cfg.blockDim = dim3(foil::kLayoutThreads, 1, 1);
+    cfg.stream = stream;
+    cudaLaunchAttribute la[1];
+    la[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    la[0].val.programmaticStreamSerializationAllowed = 1;
+    cfg.attrs = la;
+    cfg.numAttrs = pdl ? 1 : 0;
+    return cudaLaunchKernelEx(&cfg, kernel, in, out, rows, cols);
+}
+
+static int check_launch(const char* what, cudaError_t launch_err = cudaSuccess) {
     cudaError_t e = cudaGetLastError();
+    if (launch_err != cudaSuccess) e = launch_err;
     if (e != cudaSuccess) {
         char buf[256];
         snprintf(buf, sizeof buf, "%s: CUDA launch failed: %s", what, cudaGetErrorString(e));
@@ -127,9 +153,9 @@ extern "C" int foil_tilize_dev(const uint16_t* row_major, uint16_t* tiles,
     }
     uint64_t bands = (uint64_t)(rows / 32) * ((cols / 32 + 7) / 8);
     uint64_t grid = bands < (uint64_t)foil_sm_count() * 8 ? bands : (uint64_t)foil_sm_count() * 8;
-    foil::tilize_kernel<<<(unsigned)grid, foil::kLayoutThreads, 0, (cudaStream_t)stream>>>(
-        (const uint4*)row_major, (uint4*)tiles, rows, cols);
-    return check_launch("foil_tilize_dev");
+    const cudaError_t le = launch_layout(foil::tilize_kernel, (unsigned)grid, (cudaStream_t)stream,
+                                         (const uint4*)row_major, (uint4*)tiles, rows, cols);
+    return check_launch("foil_tilize_dev", le);
 }
 
 extern "C" int foil_untilize_dev(const uint16_t* tiles, uint16_t* row_major,
@@ -145,9 +171,9 @@ extern "C" int foil_untilize_dev(const uint16_t* tiles, uint16_t* row_major,
     }
     uint64_t bands = (uint64_t)(rows / 32) * ((cols / 32 + 7) / 8);
     uint64_t grid = bands < (uint64_t)foil_sm_count() * 8 ? bands : (uint64_t)foil_sm_count() * 8;
-    foil::untilize_kernel<<<(unsigned)grid, foil::kLayoutThreads, 0, (cudaStream_t)stream>>>(
-        (const uint4*)tiles, (uint4*)row_major, rows, cols);
-    return check_launch("foil_untilize_dev");
+    const cudaError_t le = launch_layout(foil::untilize_kernel, (unsigned)grid, (cudaStream_t)stream,
+                                         (const uint4*)tiles, (uint4*)row_major, rows, cols);
+    return check_launch("foil_untilize_dev", le);
 }
 
 // ---------------------------------------------------- batched transpose ---
