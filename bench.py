@@ -389,13 +389,8 @@ def run_ours(args, dist):
     per_launch_ms = ms_local / args.steps
     achieved = flops / (per_launch_ms / 1e3) / 1e12
     traffic = read_traffic()
-    # Denominator: the burst cuBLAS figure while the SM clock held its maximum
-    # in the timed region; the sustained (power-capped) one when the clock
-    # samples show the power cap pulling it down, as in a long run of steps.
+    peak, capped = roofline_peak(pk, clk)
     burst, sustained = pk["bf16_tflops"], pk.get("bf16_tflops_sustained", pk["bf16_tflops"])
-    capped = bool(clk and clk.get("sm_mhz") and clk.get("sm_max_mhz") and
-                  clk["sm_mhz"] < 0.95 * clk["sm_max_mhz"] and "sw_power_cap" in clk.get("reasons", []))
-    peak = sustained if capped else burst
     roofline = {"bound": "tensor", "achieved": achieved, "peak": peak,
                 "unit": "TFLOP/s", "frac": achieved / peak,
                 "frac_of_burst": achieved / burst, "frac_of_sustained": achieved / sustained,
@@ -427,7 +422,7 @@ def run_ours(args, dist):
         step_of = lambda k: allgather.get(k, {}).get("ms_per_step")
         fused_ms, ce_ms, mc_ms = step_of("fused"), step_of("copy_engines"), step_of("multicast")
         paths = {"ncclAllGather": nccl_ms, "fused": fused_ms, "multicast": mc_ms, "copy_engines": ce_ms}
-        best = min((v, k) for k, v in paths.items() if v is not None)[1]
+        best = best_path(paths)
         step_ms = paths[best]
         with_gather = {
             "value": dist.world * flops / (step_ms / 1e3) / 1e12, "unit": "TFLOP/s", "ms_per_step": step_ms,
@@ -465,6 +460,23 @@ def run_ours(args, dist):
             line["allgather"] = allgather
             line["value_with_gather"] = with_gather
         print(json.dumps(line), flush=True)
+
+
+def roofline_peak(pk, clk):
+    """(peak TFLOP/s, capped) for the GEMM roofline: the burst cuBLAS figure
+    while the SM clock held its maximum in the timed region, the sustained
+    (power-capped) one when the clock samples show the power cap holding the
+    median SM clock below 95 % of its maximum, as in a long run of steps."""
+    burst, sustained = pk["bf16_tflops"], pk.get("bf16_tflops_sustained", pk["bf16_tflops"])
+    capped = bool(clk and clk.get("sm_mhz") and clk.get("sm_max_mhz") and
+                  clk["sm_mhz"] < 0.95 * clk["sm_max_mhz"] and "sw_power_cap" in clk.get("reasons", []))
+    return (sustained if capped else burst), capped
+
+
+def best_path(paths):
+    """Name of the fastest reassembly path: `paths` maps names to ms per
+    step, None for a path that did not run."""
+    return min((v, k) for k, v in paths.items() if v is not None)[1]
 
 
 def _timed(torch, fn, iters, flush=None, warmup=3):
