@@ -93,6 +93,32 @@ def test_program_descriptors_present():
     mc = os.path.join(ttfoil.PROGRAMS_DIR, "matmul_2core_mcast")
     assert "variant=producer" in open(os.path.join(mc, "reader_producer.brisc.elf")).read()
     assert "variant=consumer" in open(os.path.join(mc, "reader_consumer.brisc.elf")).read()
+    # the scalar dispatch examples, under the reference's binary names
+    add = os.path.join(ttfoil.PROGRAMS_DIR, "add_two_numbers")
+    assert "role=reader" in open(os.path.join(add, "add_brisc.elf")).read()
+    assert "role=writer" in open(os.path.join(add, "add_ncrisc.elf")).read()
+    noc = os.path.join(ttfoil.PROGRAMS_DIR, "noc_passthrough")
+    assert "variant=producer" in open(os.path.join(noc, "producer.elf")).read()
+    assert "variant=consumer" in open(os.path.join(noc, "consumer.elf")).read()
+
+
+def test_make_programs_reproduces_the_committed_descriptors(tmp_path):
+    """programs/make_programs.py writes exactly the committed descriptor
+    files, and every program directory a drop-in test uses exists."""
+    import filecmp
+    import subprocess
+    import sys
+    import ttfoil
+    subprocess.run([sys.executable, os.path.join(ttfoil.PROGRAMS_DIR, "make_programs.py"), str(tmp_path)],
+                   check=True)
+    made = sorted(os.path.relpath(os.path.join(r, f), tmp_path) for r, _, fs in os.walk(tmp_path) for f in fs)
+    assert made, "no descriptors written"
+    for rel in made:
+        assert filecmp.cmp(os.path.join(tmp_path, rel), os.path.join(ttfoil.PROGRAMS_DIR, rel), shallow=False), rel
+    with open(os.path.join(REPO, "oracle", "ref", "droptests.txt")) as f:
+        progs = {line.split()[2] for line in f if line.strip() and not line.startswith("#")}
+    for prog in progs:
+        assert os.path.isdir(os.path.join(ttfoil.PROGRAMS_DIR, prog)), prog
 
 
 def test_validation_errors_without_gpu():
