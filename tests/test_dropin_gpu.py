@@ -1,9 +1,11 @@
-"""Drop-in runs: the reference's own hot-path tests (tests/test_*.cpp of
-tt-foil), compiled unchanged against libtt_foil by oracle/build.py, executed
-on the GPU.  Each binary builds its inputs, computes its own CPU golden and
-compares with the device output using its own tolerance (bitwise for
-tile_copy / dram_roundtrip, exact for relu, max(0.05, 1%) for matmul / conv,
-0.05 abs for add / bias), printing PASS and returning 0.
+"""Drop-in runs: the reference's own tests (tests/test_*.cpp of tt-foil) for
+the hot path and for the scalar dispatch examples (add_two_numbers on one,
+two and BRISC + NCRISC, noc_passthrough producer / consumer), compiled
+unchanged against libtt_foil by oracle/build.py, executed on the GPU.  Each
+binary builds its inputs, computes its own CPU golden and compares with the
+device output using its own tolerance (bitwise for tile_copy /
+dram_roundtrip, exact for relu and the u32 examples, max(0.05, 1%) for
+matmul / conv, 0.05 abs for add / bias), printing PASS and returning 0.
 """
 import os
 import subprocess
